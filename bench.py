@@ -1,0 +1,336 @@
+"""Benchmark of the BlockFHT hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...           (N > 1)
+
+Workload (headline point): bf16 latent of 32768 values
+~N(0,1), padded block size 32768, layers=3, seed=123, 2^28 generated
+coordinates per GPU (8192 blocks).  One step = forward of all 2^28
+coordinates + backward of an upstream gradient of the same size to the
+latent.  value = generated coordinates (all ranks) / step time, in Gcoords/s.
+
+Multi-GPU: blocks are independent, so rank r owns blocks
+[r*8192, (r+1)*8192) of one generator (weak scaling); the only exchange is
+the NCCL all-reduce of the [32768] latent-gradient partials.
+
+The reference arm (--impl reference) times the reference algorithm's CPU
+restatement (oracle/, OpenMP over all host cores, fp32 math) on a bounded
+sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "latent-weight-lab_b200"))
+sys.path.insert(0, str(REPO))
+
+METRIC = "BlockFHT Gcoords/s (bf16, bs=32768)"
+BLOCK = 32768
+LAYERS = 3
+SEED = 123
+COORDS_PER_GPU = 1 << 28
+
+
+def _peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[4:8]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_sample(threads: int, blocks: int = 24) -> dict:
+    """Reference algorithm on the host (fp32, OpenMP): fwd+bwd of `blocks` blocks of the workload."""
+    import numpy as np
+
+    from oracle import oracle as orc
+
+    rng = np.random.default_rng(0)
+    z = rng.standard_normal(BLOCK).astype(np.float32)
+    size = blocks * BLOCK
+    g = rng.standard_normal(size).astype(np.float32)
+    orc.fht_forward(z, BLOCK * 2, LAYERS, SEED, 0, BLOCK * 2, threads=threads)  # warm the library
+    t0 = time.perf_counter()
+    orc.fht_forward(z, size, LAYERS, SEED, 0, size, threads=threads)
+    orc.fht_backward(g, BLOCK, size, LAYERS, SEED, 0, size, threads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": size / dt / 1e9, "unit": "Gcoords/s", "cores": threads, "kind": "port",
+            "sample": f"{blocks} blocks x {BLOCK} (fwd+bwd, fp32, layers={LAYERS}) of the bench workload, "
+                      f"{dt:.2f}s"}
+
+
+def run_reference(args) -> None:
+    world, rank, _ = _dist_env()
+    if rank != 0:
+        return
+    from oracle import oracle as orc
+
+    threads = orc.max_threads()
+    vals = []
+    for _ in range(max(args.warmup, 0)):
+        cpu_sample(threads, blocks=8)
+    t_all = []
+    for _ in range(args.steps):
+        r = cpu_sample(threads, blocks=16)
+        vals.append(r["value"])
+        t_all.append(16 * BLOCK / (r["value"] * 1e9))
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "Gcoords/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * statistics.median(t_all),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": _config(args.gpus),
+        "cpu_baseline": {"value": value, "unit": "Gcoords/s", "cores": threads, "kind": "port",
+                         "sample": f"16 blocks x {BLOCK} per step, fwd+bwd, fp32 math (oracle/ C port, OpenMP)"},
+        "e2e": {"value": value, "unit": "Gcoords/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _config(n: int) -> dict:
+    return {"workload": "C2 headline: BlockFHT fwd+bwd, bf16, block_size=32768, layers=3, 2^28 coords/GPU",
+            "block_size": BLOCK, "layers": LAYERS, "seed": SEED, "coords_per_gpu": COORDS_PER_GPU,
+            "parallelism": f"block-sharded x{n}", "l2": "inputs and outputs (512 MiB each) exceed L2"}
+
+
+def run_ours(args) -> None:
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from latent_weight_lab import BlockFHT, _native
+
+    world, rank, local = _dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl")
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    lib = _native.load()
+
+    size_total = COORDS_PER_GPU * world
+    start, stop = rank * COORDS_PER_GPU, (rank + 1) * COORDS_PER_GPU
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    z_host = torch.randn(BLOCK, generator=gen).to(torch.bfloat16).pin_memory()
+    z = z_host.to(dev)
+    g = torch.randn(COORDS_PER_GPU, device=dev, dtype=torch.bfloat16)
+    y = torch.empty(COORDS_PER_GPU, device=dev, dtype=torch.bfloat16)
+    code = _native.LWL_BF16
+    ws_f = lib.lwl_fht_forward_workspace_bytes(code, BLOCK, size_total, LAYERS, start, stop, 0)
+    ws_b = lib.lwl_fht_backward_workspace_bytes(code, BLOCK, size_total, LAYERS, start, stop, 0)
+    ws = torch.empty(max(ws_f, ws_b, 1), dtype=torch.uint8, device=dev)
+    grad = torch.empty(BLOCK, device=dev, dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    def fwd():
+        st = lib.lwl_fht_forward(code, z.data_ptr(), BLOCK, size_total, LAYERS, SEED, start, stop, y.data_ptr(),
+                                 ws.data_ptr(), ws.numel(), 0, sp)
+        if st:
+            raise RuntimeError(lib.lwl_last_error().decode())
+
+    def bwd():
+        st = lib.lwl_fht_backward(code, g.data_ptr(), BLOCK, size_total, LAYERS, SEED, start, stop, grad.data_ptr(),
+                                  ws.data_ptr(), ws.numel(), 0, sp)
+        if st:
+            raise RuntimeError(lib.lwl_last_error().decode())
+        if world > 1:
+            dist.all_reduce(grad)
+
+    nf = lib.lwl_fht_launch_count(code, BLOCK, size_total, LAYERS, start, stop, 0, 0)
+    nb = lib.lwl_fht_launch_count(code, BLOCK, size_total, LAYERS, start, stop, 1, 0)
+
+    for _ in range(args.warmup):
+        fwd()
+        bwd()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(dev.index) as clk:
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for a, b, c in ev:
+            a.record(stream)
+            fwd()
+            b.record(stream)
+            bwd()
+            c.record(stream)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    total_ms = t0.elapsed_time(t1)
+    f_ms = [a.elapsed_time(b) for a, b, _ in ev]
+    b_ms = [b.elapsed_time(c) for _, b, c in ev]
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_step = total_ms / args.steps
+    value = size_total / (ms_step * 1e-3) / 1e9
+
+    # end to end through the public module API: latent from pinned host memory, forward, backward
+    # with a device-resident upstream gradient, latent gradient read back to the host.
+    mod = BlockFHT(torch.nn.Parameter(z.clone()), size=size_total, layers=LAYERS, seed=SEED)
+    grad_host = torch.empty(BLOCK, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        with torch.no_grad():
+            mod.latent.copy_(z_host, non_blocking=True)
+        mod.latent.grad = None
+        out = mod.slice(start, stop)
+        out.backward(g)
+        if world > 1:
+            dist.all_reduce(mod.latent.grad)
+        grad_host.copy_(mod.latent.grad, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    if rank == 0:
+        peaks = _peaks()
+        fm, bm = statistics.median(f_ms), statistics.median(b_ms)
+        # algorithmic HBM bytes: forward writes 2 B/coord (+ latent read); backward reads 2 B/coord.
+        f_bytes = COORDS_PER_GPU * 2 + BLOCK * 2
+        b_bytes = COORDS_PER_GPU * 2 + BLOCK * 2
+        dom_is_f = fm >= bm
+        dom_ms, dom_bytes = (fm, f_bytes) if dom_is_f else (bm, b_bytes)
+        achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+        traffic = _traffic_from_profiles("fwd" if dom_is_f else "bwd")
+        line = {
+            "metric": METRIC, "value": value, "unit": "Gcoords/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (latent ~N(0,1), upstream grad ~N(0,1))",
+            "config": _config(world),
+            "forward_gcoords_s": COORDS_PER_GPU / (fm * 1e-3) / 1e9,
+            "backward_gcoords_s": COORDS_PER_GPU / (bm * 1e-3) / 1e9,
+            "roofline": {"bound": "hbm", "kernel": "forward" if dom_is_f else "backward", "achieved": achieved,
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                         "traffic": traffic, "peak_source": peaks["source"],
+                         "bytes_per_launch": dom_bytes, "ms_per_launch": dom_ms},
+            "e2e": {"value": size_total / (e2e_ms * 1e-3) / 1e9, "unit": "Gcoords/s",
+                    "h2d_bytes_per_step": BLOCK * 2, "d2h_bytes_per_step": BLOCK * 2,
+                    "ms_per_step": e2e_ms, "api": "BlockFHT.slice + backward(upstream grad)"},
+            "gpu_launches": (nf + nb) * args.steps,
+            "clocks": clk.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            from oracle import oracle as orc
+
+            line["cpu_baseline"] = cpu_sample(orc.max_threads())
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _traffic_from_profiles(which: str):
+    """DRAM bytes per launch recorded from ncu in profiles/ (None if not captured yet)."""
+    p = REPO / "profiles" / "traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get(which)
+        except (ValueError, OSError):
+            return None
+    return None
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,89 @@
+/*
+ * lwl_b200.h -- C ABI of the B200 (sm_100a) BlockFHT library (liblwl_b200.so).
+ *
+ * Every entry point takes plain device pointers, int64 sizes and a CUDA
+ * stream (cudaStream_t passed as void*; NULL = legacy default stream).  The
+ * library never allocates device memory: callers size scratch space with the
+ * *_workspace_bytes queries and pass it in.  Calls are stateless and
+ * re-entrant; work is enqueued on the given stream and nothing synchronises
+ * the host.  Every call returns an lwl_status; lwl_last_error() gives the
+ * calling thread's message for the most recent failure.
+ *
+ * Index convention (shared with the reference): a generator with latent z of
+ * length L and padded block size B = next_pow2(L) produces `size` coordinates;
+ * coordinate i belongs to block i / B at position i % B, and block b is
+ *   y_b = S_{b,layers} Ĥ ... S_{b,1} Ĥ S_{b,0} pad_B(z),   Ĥ = H_B / sqrt(B),
+ * with H_B the natural-order Walsh-Hadamard matrix and S_{b,l} the +-1
+ * diagonal from the stateless sign hash.
+ */
+#ifndef LWL_B200_H
+#define LWL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum lwl_status {
+  LWL_OK = 0,
+  LWL_ERR_INVALID = 1,      /* bad argument: the reference raises ValueError / TORCH_CHECK here */
+  LWL_ERR_UNSUPPORTED = 2,  /* valid request outside what the kernels implement */
+  LWL_ERR_WORKSPACE = 3,    /* workspace pointer missing or smaller than required */
+  LWL_ERR_CUDA = 4,         /* a CUDA runtime call or launch failed */
+  LWL_ERR_TIMEOUT = 5       /* a bounded device-side wait gave up */
+} lwl_status;
+
+typedef enum lwl_dtype { LWL_F32 = 0, LWL_BF16 = 1, LWL_F16 = 2 } lwl_dtype;
+
+/* Flags for the transform entry points. */
+#define LWL_FLAG_EXACT 1u /* bf16/fp16: force fp32 arithmetic end to end (no tensor-core factors) */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int lwl_version(void);
+
+/* Human-readable name of a status code. */
+const char* lwl_status_string(int status);
+
+/* Message for the calling thread's most recent failure ("" if none). */
+const char* lwl_last_error(void);
+
+/* Writes `count` sign words for (seed, block, layer) starting at word
+ * `first_word` into out[count] (device memory).
+ * Replaces: sign_word_for, latent_weight_lab/block_fht.py:46-52 and the
+ * device copy csrc/block_fht_ext_cuda.cu:36-43. */
+int lwl_sign_words(uint64_t seed, int64_t block, int layer, int64_t first_word, int64_t count,
+                   uint32_t* out, void* stream);
+
+/* Workspace needed by lwl_fht_forward for these arguments (bytes; 0 if none). */
+size_t lwl_fht_forward_workspace_bytes(int dtype, int64_t latent_size, int64_t size, int layers,
+                                       int64_t start, int64_t stop, unsigned flags);
+
+/* Generated coordinates [start, stop) of the BlockFHT with latent[latent_size]
+ * (dtype) into out[stop - start] (dtype).  layers in {1,2,3}; padded block
+ * size 2^5 .. 2^23.
+ * Replaces: pybind `forward` (csrc/block_fht_ext.cpp:28-38) and
+ * block_fht_forward_cuda (csrc/block_fht_ext_cuda.cu:516-566); dtype
+ * coverage widened from fp32 to fp32/bf16/fp16. */
+int lwl_fht_forward(int dtype, const void* latent, int64_t latent_size, int64_t size, int layers,
+                    uint64_t seed, int64_t start, int64_t stop, void* out, void* workspace,
+                    size_t workspace_bytes, unsigned flags, void* stream);
+
+/* Workspace needed by lwl_fht_backward (bytes). */
+size_t lwl_fht_backward_workspace_bytes(int dtype, int64_t latent_size, int64_t size, int layers,
+                                        int64_t start, int64_t stop, unsigned flags);
+
+/* grad_latent[latent_size] (dtype, overwritten) = d/dz sum(y[start:stop] * grad_out),
+ * grad_out[stop - start] (dtype).  Accumulates in fp32, deterministically.
+ * Replaces: pybind `backward` (csrc/block_fht_ext.cpp:40-50) and
+ * block_fht_backward_cuda (csrc/block_fht_ext_cuda.cu:568-622). */
+int lwl_fht_backward(int dtype, const void* grad_out, int64_t latent_size, int64_t size,
+                     int layers, uint64_t seed, int64_t start, int64_t stop, void* grad_latent,
+                     void* workspace, size_t workspace_bytes, unsigned flags, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LWL_B200_H */

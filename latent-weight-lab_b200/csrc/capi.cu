@@ -1,0 +1,177 @@
+// capi.cu -- the extern "C" boundary of liblwl_b200.so (declared in include/lwl_b200.h).
+//
+// Argument validation mirrors the reference's checks so callers see the same
+// failures: slice bounds and layer range (latent_weight_lab/block_fht.py:92-93,
+// :609-610; csrc/block_fht_ext_cuda.cu:523-529), block-size range 2^5..2^23 is
+// widened here down to 2^0 (the reference's CPU path accepts any size).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "fht_engine.h"
+#include "lwl_b200.h"
+#include "lwl_common.cuh"
+
+namespace lwl {
+
+static thread_local char g_err[512];
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+__global__ void sign_words_kernel(uint32_t key, int64_t first_word, int64_t count, uint32_t* out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = sign_word(key, first_word + i);
+}
+
+static int validate_fht(int dtype, int64_t L, int64_t size, int layers, int64_t start, int64_t stop) {
+  if (dtype != LWL_F32 && dtype != LWL_BF16 && dtype != LWL_F16) {
+    set_error("unsupported dtype code %d (expected 0=fp32, 1=bf16, 2=fp16)", dtype);
+    return LWL_ERR_INVALID;
+  }
+  if (L <= 0) {
+    set_error("latent size must be positive");
+    return LWL_ERR_INVALID;
+  }
+  if (size <= 0) {
+    set_error("size must be positive");
+    return LWL_ERR_INVALID;
+  }
+  if (layers < 1 || layers > 3) {
+    set_error("layers must be 1, 2, or 3");
+    return LWL_ERR_INVALID;
+  }
+  if (!(0 <= start && start <= stop && stop <= size)) {
+    set_error("invalid slice [%lld, %lld) for size %lld", (long long)start, (long long)stop, (long long)size);
+    return LWL_ERR_INVALID;
+  }
+  if (next_pow2(L) > (int64_t(1) << kMaxLogB)) {
+    set_error("padded block size %lld exceeds the supported maximum 2^23", (long long)next_pow2(L));
+    return LWL_ERR_UNSUPPORTED;
+  }
+  return LWL_OK;
+}
+
+static int fht_call(bool backward, int dtype, const void* in, void* out, int64_t L, int64_t size,
+                    int layers, uint64_t seed, int64_t start, int64_t stop, void* ws, size_t ws_bytes,
+                    unsigned flags, void* stream) {
+  g_err[0] = 0;
+  int st = validate_fht(dtype, L, size, layers, start, stop);
+  if (st) return st;
+  if ((stop > start && !in) || !out) {
+    set_error("null data pointer");
+    return LWL_ERR_INVALID;
+  }
+  FhtArgs a;
+  a.dtype = dtype;
+  a.backward = backward;
+  a.in = in;
+  a.out = out;
+  a.latent_size = L;
+  a.size = size;
+  a.layers = layers;
+  a.seed = seed;
+  a.start = start;
+  a.stop = stop;
+  a.workspace = ws;
+  a.workspace_bytes = ws_bytes;
+  a.flags = flags;
+  FhtPlan plan;
+  plan_fht(a, plan);
+  if (plan.ws_bytes > 0 && (ws == nullptr || ws_bytes < plan.ws_bytes)) {
+    set_error("workspace of %zu bytes required, %zu given", plan.ws_bytes, ws ? ws_bytes : (size_t)0);
+    return LWL_ERR_WORKSPACE;
+  }
+  return run_fht(a, plan, reinterpret_cast<cudaStream_t>(stream));
+}
+
+static size_t fht_ws(bool backward, int dtype, int64_t L, int64_t size, int layers, int64_t start,
+                     int64_t stop, unsigned flags) {
+  if (validate_fht(dtype, L, size, layers, start, stop) != LWL_OK) return 0;
+  FhtArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.dtype = dtype;
+  a.backward = backward;
+  a.latent_size = L;
+  a.size = size;
+  a.layers = layers;
+  a.start = start;
+  a.stop = stop;
+  a.flags = flags;
+  FhtPlan plan;
+  plan_fht(a, plan);
+  return plan.ws_bytes;
+}
+
+}  // namespace lwl
+
+extern "C" {
+
+int lwl_version(void) { return 100; }
+
+const char* lwl_status_string(int status) {
+  switch (status) {
+    case LWL_OK: return "ok";
+    case LWL_ERR_INVALID: return "invalid argument";
+    case LWL_ERR_UNSUPPORTED: return "unsupported";
+    case LWL_ERR_WORKSPACE: return "workspace too small";
+    case LWL_ERR_CUDA: return "CUDA error";
+    case LWL_ERR_TIMEOUT: return "device wait timed out";
+    default: return "unknown status";
+  }
+}
+
+const char* lwl_last_error(void) { return lwl::g_err; }
+
+int lwl_sign_words(uint64_t seed, int64_t block, int layer, int64_t first_word, int64_t count, uint32_t* out,
+                   void* stream) {
+  lwl::g_err[0] = 0;
+  if (count < 0 || block < 0 || first_word < 0 || layer < 0) {
+    lwl::set_error("block, layer, first_word and count must be non-negative");
+    return LWL_ERR_INVALID;
+  }
+  if (count == 0) return LWL_OK;
+  if (!out) {
+    lwl::set_error("null output pointer");
+    return LWL_ERR_INVALID;
+  }
+  uint32_t key = lwl::block_layer_key(lwl::fold_seed(seed), block, layer);
+  int threads = 256;
+  int64_t blocks = (count + threads - 1) / threads;
+  if (blocks > 4096) blocks = 4096;
+  lwl::sign_words_kernel<<<(int)blocks, threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(key, first_word,
+                                                                                               count, out);
+  LWL_CUDA_TRY(cudaGetLastError());
+  return LWL_OK;
+}
+
+size_t lwl_fht_forward_workspace_bytes(int dtype, int64_t latent_size, int64_t size, int layers, int64_t start,
+                                       int64_t stop, unsigned flags) {
+  return lwl::fht_ws(false, dtype, latent_size, size, layers, start, stop, flags);
+}
+
+int lwl_fht_forward(int dtype, const void* latent, int64_t latent_size, int64_t size, int layers, uint64_t seed,
+                    int64_t start, int64_t stop, void* out, void* workspace, size_t workspace_bytes,
+                    unsigned flags, void* stream) {
+  if (stop == start && lwl::validate_fht(dtype, latent_size, size, layers, start, stop) == LWL_OK) return LWL_OK;
+  return lwl::fht_call(false, dtype, latent, out, latent_size, size, layers, seed, start, stop, workspace,
+                       workspace_bytes, flags, stream);
+}
+
+size_t lwl_fht_backward_workspace_bytes(int dtype, int64_t latent_size, int64_t size, int layers, int64_t start,
+                                        int64_t stop, unsigned flags) {
+  return lwl::fht_ws(true, dtype, latent_size, size, layers, start, stop, flags);
+}
+
+int lwl_fht_backward(int dtype, const void* grad_out, int64_t latent_size, int64_t size, int layers,
+                     uint64_t seed, int64_t start, int64_t stop, void* grad_latent, void* workspace,
+                     size_t workspace_bytes, unsigned flags, void* stream) {
+  return lwl::fht_call(true, dtype, grad_out, grad_latent, latent_size, size, layers, seed, start, stop,
+                       workspace, workspace_bytes, flags, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,298 @@
+// fht_engine.cu -- host-side planning and launch of the generic tile engine.
+//
+// Two layouts, chosen by padded block size B = 2^n:
+//  * whole-block: one tile holds entire blocks (2^m small blocks side by
+//    side when n < 12); every layer is done in shared memory, one launch.
+//    Forward for n <= 15, backward for n <= 14 (the backward also keeps an
+//    fp32 accumulator over the latent positions in shared memory).
+//  * two-pass: B = 2^a * 2^(n-a); pass P1 transforms the low a bits
+//    (contiguous runs), pass P2 the high bits (8-element columns at stride
+//    2^a).  Layers alternate P2,P1 / P1,P2 so neighbouring layers share a
+//    pass: layers+1 launches over an fp32 workspace of #blocks * B.
+// The backward runs the transposed chain (reversed sign layers) and reduces
+// the per-block results over blocks deterministically (reduce_rows_kernel).
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+
+#include "fht_engine.h"
+#include "fht_tile.cuh"
+
+namespace lwl {
+
+namespace {
+
+constexpr int kSmemLimit = 232448;  // 227 KB opt-in per CTA on sm_100
+
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+// Split `r` transform bits into ceil(r/5) balanced groups starting at tile bit `cb`.
+int make_groups(int r, int cb, int8_t* glo, int8_t* gr) {
+  int k = std::max(1, (r + 4) / 5);
+  int base = r / k, rem = r % k, at = cb;
+  for (int i = 0; i < k; ++i) {
+    int s = base + (i < rem ? 1 : 0);
+    glo[i] = (int8_t)at;
+    gr[i] = (int8_t)s;
+    at += s;
+  }
+  return k;
+}
+
+// Runs for `nseg` full transforms over the tile's transform bits, each
+// followed by sign slot seg_slot[i] (-1 = none).  The last segment walks
+// the groups upward so the final stores have consecutive lanes on
+// consecutive positions; earlier segments alternate so that neighbours
+// share a group (merged into one run).
+void build_runs(TileParams& p, const int* seg_slot, int nseg) {
+  int8_t glo[8], gr[8];
+  int k = make_groups(p.r, p.cb, glo, gr);
+  p.nruns = 0;
+  for (int s = 0; s < nseg; ++s) {
+    bool asc = ((nseg - 1 - s) % 2) == 0;
+    for (int i = 0; i < k; ++i) {
+      int g = asc ? i : k - 1 - i;
+      int slot = (i == k - 1) ? seg_slot[s] : -1;
+      RunDesc* last = p.nruns ? &p.runs[p.nruns - 1] : nullptr;
+      if (last && last->glo == glo[g] && last->gr == gr[g] && last->nfht < 3) {
+        last->slot[last->nfht] = (int8_t)slot;
+        last->nfht++;
+      } else {
+        RunDesc rd;
+        rd.glo = glo[g];
+        rd.gr = gr[g];
+        rd.nfht = 1;
+        rd.slot[0] = (int8_t)slot;
+        rd.slot[1] = rd.slot[2] = -1;
+        p.runs[p.nruns++] = rd;
+      }
+    }
+  }
+}
+
+size_t tile_smem(const TileParams& p) {
+  size_t E = size_t(1) << p.e;
+  size_t b = (E + E / 32) * 4 + size_t(p.nslots) * (E >> p.wshift) * 4;
+  if (p.dst_kind == DST_ACC) b += size_t(p.L) * 4;
+  return b;
+}
+
+int tile_threads(const TileParams& p) { return std::min(512, std::max(32, 1 << std::max(0, p.e - 5))); }
+
+template <typename T>
+int occupancy(int threads, size_t smem) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(fht_tile_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    attr_set = true;
+  }
+  int blocks = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fht_tile_kernel<T>, threads, smem) != cudaSuccess)
+    blocks = 1;
+  return std::max(1, blocks);
+}
+
+int occupancy_for(int dtype, int threads, size_t smem) {
+  if (dtype == LWL_BF16) return occupancy<__nv_bfloat16>(threads, smem);
+  if (dtype == LWL_F16) return occupancy<__half>(threads, smem);
+  return occupancy<float>(threads, smem);
+}
+
+void finish_launch(int dtype, TileLaunch& l) {
+  l.threads = tile_threads(l.p);
+  l.smem = tile_smem(l.p);
+  int64_t cap = (int64_t)sm_count() * occupancy_for(dtype, l.threads, l.smem);
+  l.grid = (int)std::max<int64_t>(1, std::min<int64_t>(l.p.ntiles, cap));
+}
+
+void common_fields(TileParams& p, const FhtArgs& a, int n) {
+  std::memset(&p, 0, sizeof(p));
+  p.n = n;
+  p.B = int64_t(1) << n;
+  p.L = a.latent_size;
+  p.seed32 = fold_seed(a.seed);
+  p.scale = (float)(1.0 / std::sqrt((double)p.B));
+  p.pre_slot = -1;
+  p.start = a.start;
+  p.stop = a.stop;
+}
+
+}  // namespace
+
+int plan_fht(const FhtArgs& a, FhtPlan& plan) {
+  std::memset(&plan, 0, sizeof(plan));
+  const int n = ilog2(next_pow2(a.latent_size));
+  const int64_t B = int64_t(1) << n;
+  const int64_t first = a.start / B, last = (a.stop + B - 1) / B;
+  const int64_t nblk = last - first;
+  plan.nblocks = nblk;
+  plan.B = B;
+  if (nblk <= 0) return 0;
+  const int L = a.layers;
+  const bool bwd = a.backward;
+  // sign layer applied before the first network, then after network i
+  auto pre_layer = [&]() { return bwd ? L : 0; };
+  auto post_layer = [&](int i) { return bwd ? L - 1 - i : i + 1; };
+
+  const bool whole = bwd ? (n <= kWholeBlockMaxLogBwd) : (n <= kWholeBlockMaxLogFwd);
+  if (whole) {
+    TileLaunch& l = plan.launches[0];
+    plan.nlaunch = 1;
+    TileParams& p = l.p;
+    common_fields(p, a, n);
+    p.e = std::max(n, 12);
+    p.cb = 0;
+    p.tlo = 0;
+    p.r = n;
+    p.m = p.e - n;
+    p.ulo = n;
+    p.ublock = 1;
+    p.rlo = 0;
+    p.wshift = std::min(5, n);
+    p.tiles_per_group = 1;
+    p.first_block = first;
+    p.nblocks = nblk;
+    p.ntiles = (nblk + (int64_t(1) << p.m) - 1) >> p.m;
+    p.nslots = L + 1;
+    p.slot_layer[0] = pre_layer();
+    int seg_slot[3];
+    for (int i = 0; i < L; ++i) {
+      p.slot_layer[i + 1] = post_layer(i);
+      seg_slot[i] = i + 1;
+    }
+    p.pre_slot = 0;
+    build_runs(p, seg_slot, L);
+    p.src_kind = bwd ? SRC_SLICE : SRC_LATENT;
+    p.dst_kind = bwd ? DST_ACC : DST_SLICE;
+    finish_launch(a.dtype, l);
+    if (bwd) {
+      plan.partial_rows = l.grid;
+      plan.ws_bytes = size_t(l.grid) * size_t(a.latent_size) * 4;
+    }
+    return 0;
+  }
+
+  // two-pass layout
+  const int abits = (n + 1) / 2;
+  const int hbits = n - abits;
+  // execution order of (part, post-layer) steps; part 1 = P1 (low bits), 2 = P2
+  int step_part[6], step_sign[6], nsteps = 0;
+  for (int i = 0; i < L; ++i) {
+    bool p2_first = ((L - 1 - i) % 2) == 0;
+    int first_part = p2_first ? 2 : 1, second_part = p2_first ? 1 : 2;
+    step_part[nsteps] = first_part;
+    step_sign[nsteps++] = -1;
+    step_part[nsteps] = second_part;
+    step_sign[nsteps++] = post_layer(i);
+  }
+  int s = 0;
+  plan.nlaunch = 0;
+  while (s < nsteps) {
+    int e_ = s;
+    while (e_ + 1 < nsteps && step_part[e_ + 1] == step_part[s]) ++e_;
+    TileLaunch& l = plan.launches[plan.nlaunch];
+    TileParams& p = l.p;
+    common_fields(p, a, n);
+    const bool is_first = (s == 0), is_last = (e_ == nsteps - 1);
+    if (step_part[s] == 1) {
+      p.cb = 0;
+      p.tlo = 0;
+      p.r = abits;
+      p.m = std::min(hbits, std::max(0, 12 - abits));
+      p.ulo = abits;
+      p.rlo = abits + p.m;
+      p.wshift = 5;
+      p.tiles_per_group = int64_t(1) << (n - abits - p.m);
+    } else {
+      p.cb = 3;
+      p.tlo = abits;
+      p.r = hbits;
+      p.m = std::min(abits - 3, std::max(0, 12 - 3 - hbits));
+      p.ulo = 3;
+      p.rlo = 3 + p.m;
+      p.wshift = 3;
+      p.tiles_per_group = int64_t(1) << (abits - 3 - p.m);
+    }
+    p.e = p.cb + p.r + p.m;
+    p.ublock = 0;
+    p.first_block = first;
+    p.nblocks = nblk;
+    p.ntiles = nblk * p.tiles_per_group;
+    p.nslots = 0;
+    if (is_first) {
+      p.slot_layer[p.nslots] = pre_layer();
+      p.pre_slot = p.nslots++;
+    }
+    int seg_slot[6], nseg = 0;
+    for (int k = s; k <= e_; ++k) {
+      if (step_sign[k] >= 0) {
+        p.slot_layer[p.nslots] = step_sign[k];
+        seg_slot[nseg++] = p.nslots++;
+      } else {
+        seg_slot[nseg++] = -1;
+      }
+    }
+    build_runs(p, seg_slot, nseg);
+    p.src_kind = is_first ? (bwd ? SRC_SLICE : SRC_LATENT) : SRC_WS;
+    p.dst_kind = (is_last && !bwd) ? DST_SLICE : DST_WS;
+    finish_launch(a.dtype, l);
+    plan.nlaunch++;
+    s = e_ + 1;
+  }
+  plan.ws_bytes = size_t(nblk) * size_t(B) * 4;
+  if (bwd) plan.partial_rows = nblk;
+  return 0;
+}
+
+template <typename T>
+__global__ void reduce_rows_kernel(const float* __restrict__ src, int64_t rows, int64_t row_stride,
+                                   int64_t L, T* __restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < L; i += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.0f;
+    for (int64_t r = 0; r < rows; ++r) s += src[r * row_stride + i];
+    out[i] = Cvt<T>::from_f(s);
+  }
+}
+
+namespace {
+template <typename T>
+int run_plan_t(const FhtArgs& a, FhtPlan& plan, cudaStream_t st) {
+  if (plan.nblocks <= 0) {
+    if (a.backward) LWL_CUDA_TRY(cudaMemsetAsync(a.out, 0, size_t(a.latent_size) * sizeof(T), st));
+    return LWL_OK;
+  }
+  for (int i = 0; i < plan.nlaunch; ++i) {
+    TileLaunch& l = plan.launches[i];
+    TileParams& p = l.p;
+    p.src = (p.src_kind == SRC_WS) ? a.workspace : a.in;
+    if (p.dst_kind == DST_SLICE) p.dst = a.out;
+    else if (p.dst_kind == DST_WS) p.dst = a.workspace;
+    else p.partial = reinterpret_cast<float*>(a.workspace);
+    fht_tile_kernel<T><<<l.grid, l.threads, l.smem, st>>>(p);
+    LWL_CUDA_TRY(cudaGetLastError());
+  }
+  if (a.backward) {
+    int64_t stride = plan.launches[0].p.dst_kind == DST_ACC ? a.latent_size : plan.B;
+    int threads = 256;
+    int64_t blocks = std::min<int64_t>((a.latent_size + threads - 1) / threads, 65535);
+    reduce_rows_kernel<T><<<(int)blocks, threads, 0, st>>>(reinterpret_cast<const float*>(a.workspace),
+                                                            plan.partial_rows, stride, a.latent_size,
+                                                            reinterpret_cast<T*>(a.out));
+    LWL_CUDA_TRY(cudaGetLastError());
+  }
+  return LWL_OK;
+}
+}  // namespace
+
+int run_fht(const FhtArgs& a, FhtPlan& plan, cudaStream_t st) {
+  if (a.dtype == LWL_BF16) return run_plan_t<__nv_bfloat16>(a, plan, st);
+  if (a.dtype == LWL_F16) return run_plan_t<__half>(a, plan, st);
+  return run_plan_t<float>(a, plan, st);
+}
+
+}  // namespace lwl

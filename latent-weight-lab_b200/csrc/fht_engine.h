@@ -1,0 +1,48 @@
+// fht_engine.h -- internal interface between the C ABI and the transform engines.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "fht_tile.cuh"
+
+namespace lwl {
+
+constexpr int kWholeBlockMaxLogFwd = 15;
+constexpr int kWholeBlockMaxLogBwd = 14;
+constexpr int kMaxLogB = 23;
+
+struct FhtArgs {
+  int dtype;
+  bool backward;
+  const void* in;       // forward: latent [L]; backward: grad_out [stop-start]
+  void* out;            // forward: y [stop-start]; backward: grad_latent [L]
+  int64_t latent_size;  // L
+  int64_t size;
+  int layers;
+  uint64_t seed;
+  int64_t start, stop;
+  void* workspace;
+  size_t workspace_bytes;
+  unsigned flags;
+};
+
+struct TileLaunch {
+  TileParams p;
+  int threads;
+  size_t smem;
+  int grid;
+};
+
+struct FhtPlan {
+  int nlaunch;
+  TileLaunch launches[4];
+  int64_t nblocks, B;
+  int64_t partial_rows;  // backward: rows reduced into grad_latent
+  size_t ws_bytes;
+};
+
+int plan_fht(const FhtArgs& a, FhtPlan& plan);
+int run_fht(const FhtArgs& a, FhtPlan& plan, cudaStream_t st);
+
+}  // namespace lwl

@@ -1,0 +1,241 @@
+// fht_tile.cuh -- the generic BlockFHT tile engine (fp32 arithmetic).
+//
+// One CTA owns a "tile": 2^e elements of the generated-coordinate space held
+// in shared memory (fp32, one pad word per 32 to spread banks).  Tile index
+// bits map onto block positions / block numbers as
+//   t = [ col : cb ][ transform : r ][ upper : m ]
+//   pos = col | transform << tlo | (upper << ulo, unless upper selects blocks)
+//         | tile-id bits << rlo
+// so the same engine covers (a) a whole block (cb=0, tlo=0, r=n) with 2^m
+// small blocks side by side, and (b) the two passes of large blocks
+// (contiguous runs of the low bits; strided columns of the high bits).
+//
+// Inside a tile the transform is a list of "runs": a run loads the 2^gr
+// elements of one radix group (gr <= 5 bits) per column into registers,
+// applies 1..3 radix-2^gr butterfly networks with a sign/scale between them
+// (adjacent layers share a group, so a layer boundary costs no extra shared
+// memory round trip), and stores them back.  The first run reads straight
+// from the source (latent, gradient slice or fp32 workspace) and the last run
+// writes straight to the sink, so a tile costs (#runs - 1) shared round trips.
+#pragma once
+#include "lwl_common.cuh"
+
+namespace lwl {
+
+constexpr int kMaxRuns = 12;
+constexpr int kMaxSlots = 4;
+
+enum SrcKind : int { SRC_LATENT = 0, SRC_SLICE = 1, SRC_WS = 2 };
+enum DstKind : int { DST_SLICE = 0, DST_WS = 1, DST_ACC = 2 };
+
+struct RunDesc {
+  int8_t glo;      // lowest tile bit of the group
+  int8_t gr;       // group bits (1..5)
+  int8_t nfht;     // butterfly networks applied in this run (1..3)
+  int8_t slot[3];  // sign slot after each network, -1 = none
+};
+
+struct TileParams {
+  int n;           // log2(B)
+  int64_t B, L;
+  int e, cb, tlo, r, m, ulo;
+  int ublock;      // upper tile bits select blocks (whole-block config)
+  int rlo;         // position of the tile-id bits inside pos
+  int wshift;      // sign-table index = t >> wshift
+  int64_t tiles_per_group;  // tiles per (block, or 2^m blocks when ublock)
+  int64_t first_block, nblocks, ntiles;
+  int nslots;
+  int slot_layer[kMaxSlots];
+  int pre_slot;    // slot applied to source values, -1 none
+  uint32_t seed32;
+  float scale;     // multiplies every post-sign (1/sqrt(B))
+  int nruns;
+  RunDesc runs[kMaxRuns];
+  int src_kind, dst_kind;
+  const void* src;
+  void* dst;
+  int64_t start, stop;
+  float* partial;  // DST_ACC: [gridDim.x][L]
+};
+
+__device__ __forceinline__ int pad_idx(int t) { return t + (t >> 5); }
+
+struct TileCtx {
+  int64_t tile_blk;   // first block of the tile
+  int64_t fixed_pos;  // tile-id bits of pos
+};
+
+__device__ __forceinline__ void tile_coords(const TileParams& p, const TileCtx& c, int t,
+                                            int64_t& pos, int64_t& blk) {
+  int col = t & ((1 << p.cb) - 1);
+  int k = (t >> p.cb) & ((1 << p.r) - 1);
+  int u = t >> (p.cb + p.r);
+  pos = (int64_t)col | ((int64_t)k << p.tlo) | c.fixed_pos;
+  blk = c.tile_blk;
+  if (p.ublock) blk += u;
+  else pos |= (int64_t)u << p.ulo;
+}
+
+template <typename T>
+__device__ __forceinline__ float load_src(const TileParams& p, int64_t pos, int64_t blk) {
+  if (p.src_kind == SRC_LATENT) {
+    return pos < p.L ? Cvt<T>::to_f(reinterpret_cast<const T*>(p.src)[pos]) : 0.0f;
+  } else if (p.src_kind == SRC_SLICE) {
+    int64_t g = blk * p.B + pos;
+    return (g >= p.start && g < p.stop) ? Cvt<T>::to_f(reinterpret_cast<const T*>(p.src)[g - p.start]) : 0.0f;
+  } else {
+    int64_t b = blk - p.first_block;
+    return b < p.nblocks ? reinterpret_cast<const float*>(p.src)[b * p.B + pos] : 0.0f;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store_dst(const TileParams& p, int64_t pos, int64_t blk, float v) {
+  if (p.dst_kind == DST_SLICE) {
+    int64_t g = blk * p.B + pos;
+    if (g >= p.start && g < p.stop) reinterpret_cast<T*>(p.dst)[g - p.start] = Cvt<T>::from_f(v);
+  } else {  // DST_WS
+    int64_t b = blk - p.first_block;
+    if (b < p.nblocks) reinterpret_cast<float*>(p.dst)[b * p.B + pos] = v;
+  }
+}
+
+template <int R>
+__device__ __forceinline__ void butterflies(float (&v)[1 << R]) {
+#pragma unroll
+  for (int h = 1; h < (1 << R); h <<= 1) {
+#pragma unroll
+    for (int i = 0; i < (1 << R); i += 2 * h) {
+#pragma unroll
+      for (int j = i; j < i + h; ++j) {
+        float a = v[j], b = v[j + h];
+        v[j] = a + b;
+        v[j + h] = a - b;
+      }
+    }
+  }
+}
+
+// One run of radix group GR over the tile.  first/last select source/sink I/O.
+template <typename T, int GR>
+__device__ void do_run(const TileParams& p, const TileCtx& c, const RunDesc& rd, float* data,
+                       const uint32_t* signs, int words_per_slot, bool first, bool last) {
+  const int glo = rd.glo;
+  const int ncols = 1 << (p.e - GR);
+  const int lowmask = (1 << glo) - 1;
+  for (int col = threadIdx.x; col < ncols; col += blockDim.x) {
+    const int base = (col & lowmask) | ((col >> glo) << (glo + GR));
+    float v[1 << GR];
+    if (first) {
+#pragma unroll
+      for (int k = 0; k < (1 << GR); ++k) {
+        int t = base | (k << glo);
+        int64_t pos, blk;
+        tile_coords(p, c, t, pos, blk);
+        float x = load_src<T>(p, pos, blk);
+        if (p.pre_slot >= 0) {
+          uint32_t w = signs[p.pre_slot * words_per_slot + (t >> p.wshift)];
+          x = ((w >> (pos & 31)) & 1u) ? x : -x;
+        }
+        v[k] = x;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < (1 << GR); ++k) v[k] = data[pad_idx(base | (k << glo))];
+    }
+    for (int f = 0; f < rd.nfht; ++f) {
+      butterflies<GR>(v);
+      int s = rd.slot[f];
+      if (s >= 0) {
+        const float sc = p.scale;
+#pragma unroll
+        for (int k = 0; k < (1 << GR); ++k) {
+          int t = base | (k << glo);
+          int64_t pos, blk;
+          tile_coords(p, c, t, pos, blk);
+          uint32_t w = signs[s * words_per_slot + (t >> p.wshift)];
+          v[k] *= ((w >> (pos & 31)) & 1u) ? sc : -sc;
+        }
+      }
+    }
+    if (last && p.dst_kind != DST_ACC) {
+#pragma unroll
+      for (int k = 0; k < (1 << GR); ++k) {
+        int t = base | (k << glo);
+        int64_t pos, blk;
+        tile_coords(p, c, t, pos, blk);
+        store_dst<T>(p, pos, blk, v[k]);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < (1 << GR); ++k) data[pad_idx(base | (k << glo))] = v[k];
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void dispatch_run(const TileParams& p, const TileCtx& c, const RunDesc& rd,
+                                             float* data, const uint32_t* signs, int wps, bool first,
+                                             bool last) {
+  switch (rd.gr) {
+    case 0: do_run<T, 0>(p, c, rd, data, signs, wps, first, last); break;
+    case 1: do_run<T, 1>(p, c, rd, data, signs, wps, first, last); break;
+    case 2: do_run<T, 2>(p, c, rd, data, signs, wps, first, last); break;
+    case 3: do_run<T, 3>(p, c, rd, data, signs, wps, first, last); break;
+    case 4: do_run<T, 4>(p, c, rd, data, signs, wps, first, last); break;
+    default: do_run<T, 5>(p, c, rd, data, signs, wps, first, last); break;
+  }
+}
+
+// Persistent tile kernel.  Shared memory: data (2^e + 2^e/32 floats), sign
+// tables (nslots * 2^(e-wshift) words), and for DST_ACC an fp32 accumulator
+// over the latent positions [L].
+template <typename T>
+__global__ void __launch_bounds__(512) fht_tile_kernel(const __grid_constant__ TileParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int E = 1 << p.e;
+  float* data = reinterpret_cast<float*>(smem_raw);
+  uint32_t* signs = reinterpret_cast<uint32_t*>(data + E + (E >> 5));
+  const int wps = E >> p.wshift;
+  float* acc = reinterpret_cast<float*>(signs + p.nslots * wps);
+
+  if (p.dst_kind == DST_ACC)
+    for (int i = threadIdx.x; i < p.L; i += blockDim.x) acc[i] = 0.0f;
+
+  for (int64_t tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x) {
+    TileCtx c;
+    int64_t grp = tile / p.tiles_per_group;
+    int64_t tib = tile - grp * p.tiles_per_group;
+    c.tile_blk = p.first_block + (p.ublock ? (grp << p.m) : grp);
+    c.fixed_pos = tib << p.rlo;
+
+    // sign words for every slot used by this tile
+    for (int i = threadIdx.x; i < p.nslots * wps; i += blockDim.x) {
+      int s = i / wps, j = i - s * wps;
+      int64_t pos, blk;
+      tile_coords(p, c, j << p.wshift, pos, blk);
+      signs[i] = sign_word(block_layer_key(p.seed32, blk, p.slot_layer[s]), pos >> 5);
+    }
+    __syncthreads();
+    for (int ri = 0; ri < p.nruns; ++ri) {
+      dispatch_run<T>(p, c, p.runs[ri], data, signs, wps, ri == 0, ri == p.nruns - 1);
+      __syncthreads();
+    }
+    if (p.dst_kind == DST_ACC) {
+      // sum the tile's blocks into the per-CTA latent-gradient accumulator
+      const int nb = 1 << p.m;
+      for (int i = threadIdx.x; i < p.L; i += blockDim.x) {
+        float s = 0.0f;
+        for (int bl = 0; bl < nb; ++bl) {
+          if (c.tile_blk + bl - p.first_block < p.nblocks) s += data[pad_idx((bl << p.n) + i)];
+        }
+        acc[i] += s;
+      }
+      __syncthreads();
+    }
+  }
+  if (p.dst_kind == DST_ACC)
+    for (int i = threadIdx.x; i < p.L; i += blockDim.x) p.partial[(int64_t)blockIdx.x * p.L + i] = acc[i];
+}
+
+}  // namespace lwl

@@ -1,0 +1,173 @@
+"""ctypes binding to liblwl_b200.so, the sm_100a BlockFHT library.
+
+This module replaces the reference's JIT-built pybind extension
+(latent_weight_lab/block_fht.py:112-146 and csrc/block_fht_ext.cpp).  Unlike
+the reference it never falls back silently: a missing or broken library, or
+a non-CUDA tensor, raises immediately.  torch supplies device memory and the
+current stream; all arithmetic happens in the library's kernels.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+_LIB_PATH = Path(__file__).resolve().parent / "_lib" / "liblwl_b200.so"
+_LOCK = threading.Lock()
+_LIB = None
+_LOAD_ERROR: Exception | None = None
+
+LWL_F32, LWL_BF16, LWL_F16 = 0, 1, 2
+FLAG_EXACT = 1
+_DTYPE_CODE = {torch.float32: LWL_F32, torch.bfloat16: LWL_BF16, torch.float16: LWL_F16}
+
+
+class NativeError(RuntimeError):
+    """A liblwl_b200 call returned a non-OK status."""
+
+
+def library_path() -> Path:
+    return Path(os.environ.get("LWL_B200_LIB", _LIB_PATH))
+
+
+def _declare(lib: ctypes.CDLL) -> None:
+    i64, u64, vp, sz, ci, cu = (ctypes.c_int64, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_size_t,
+                                ctypes.c_int, ctypes.c_uint)
+    lib.lwl_version.restype = ci
+    lib.lwl_version.argtypes = []
+    lib.lwl_status_string.restype = ctypes.c_char_p
+    lib.lwl_status_string.argtypes = [ci]
+    lib.lwl_last_error.restype = ctypes.c_char_p
+    lib.lwl_last_error.argtypes = []
+    lib.lwl_sign_words.restype = ci
+    lib.lwl_sign_words.argtypes = [u64, i64, ci, i64, i64, vp, vp]
+    for name in ("lwl_fht_forward_workspace_bytes", "lwl_fht_backward_workspace_bytes"):
+        fn = getattr(lib, name)
+        fn.restype = sz
+        fn.argtypes = [ci, i64, i64, ci, i64, i64, cu]
+    for name in ("lwl_fht_forward", "lwl_fht_backward"):
+        fn = getattr(lib, name)
+        fn.restype = ci
+        fn.argtypes = [ci, vp, i64, i64, ci, u64, i64, i64, vp, vp, sz, cu, vp]
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once; raise (and keep raising) if that fails."""
+    global _LIB, _LOAD_ERROR
+    if _LIB is not None:
+        return _LIB
+    with _LOCK:
+        if _LIB is None:
+            if _LOAD_ERROR is not None:
+                raise _LOAD_ERROR
+            path = library_path()
+            try:
+                if not path.exists():
+                    raise FileNotFoundError(
+                        f"{path} is missing; build it with `python latent-weight-lab_b200/build.py`")
+                lib = ctypes.CDLL(str(path))
+                _declare(lib)
+            except Exception as exc:  # remembered so every later call fails the same way
+                _LOAD_ERROR = RuntimeError(f"liblwl_b200 could not be loaded: {exc}")
+                raise _LOAD_ERROR from exc
+            _LIB = lib
+    return _LIB
+
+
+def load_error() -> Exception | None:
+    return _LOAD_ERROR
+
+
+def _check(status: int) -> None:
+    if status != 0:
+        lib = load()
+        msg = lib.lwl_last_error().decode(errors="replace")
+        kind = lib.lwl_status_string(status).decode()
+        if status == 1:
+            raise ValueError(msg or kind)
+        raise NativeError(f"{kind}: {msg}")
+
+
+def _seed_u64(seed: int) -> int:
+    return int(seed) & ((1 << 64) - 1)
+
+
+def _require_cuda(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(
+            f"{what} must be a CUDA tensor: this latent_weight_lab build computes on B200 GPUs only "
+            "(move the module or tensor to a CUDA device)")
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODE[dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dtype}; expected float32, bfloat16 or float16") from None
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _workspace(nbytes: int, device: torch.device) -> tuple[torch.Tensor | None, int]:
+    if nbytes == 0:
+        return None, 0
+    return torch.empty(int(nbytes), dtype=torch.uint8, device=device), 0
+
+
+def fht_forward(latent: torch.Tensor, size: int, layers: int, seed: int, start: int, stop: int,
+                flags: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y[start:stop] of the BlockFHT generator, same dtype as `latent`."""
+    _require_cuda(latent, "latent")
+    lib = load()
+    latent = latent.contiguous()
+    code = dtype_code(latent.dtype)
+    n = int(stop) - int(start)
+    if out is None:
+        out = torch.empty(max(n, 0), dtype=latent.dtype, device=latent.device)
+    with torch.cuda.device(latent.device):
+        ws_bytes = lib.lwl_fht_forward_workspace_bytes(code, latent.numel(), int(size), int(layers),
+                                                       int(start), int(stop), int(flags))
+        ws, _ = _workspace(ws_bytes, latent.device)
+        _check(lib.lwl_fht_forward(code, latent.data_ptr(), latent.numel(), int(size), int(layers),
+                                   _seed_u64(seed), int(start), int(stop), out.data_ptr(),
+                                   ws.data_ptr() if ws is not None else None, ws_bytes, int(flags),
+                                   _stream_ptr(latent.device)))
+    return out
+
+
+def fht_backward(grad_out: torch.Tensor, latent_size: int, size: int, layers: int, seed: int,
+                 start: int, stop: int, flags: int = 0) -> torch.Tensor:
+    """d/dz sum(y[start:stop] * grad_out) as a [latent_size] tensor of grad_out's dtype."""
+    _require_cuda(grad_out, "grad_out")
+    lib = load()
+    grad_out = grad_out.contiguous()
+    code = dtype_code(grad_out.dtype)
+    if grad_out.numel() != int(stop) - int(start):
+        raise ValueError("grad_out must have stop - start elements")
+    grad = torch.empty(int(latent_size), dtype=grad_out.dtype, device=grad_out.device)
+    with torch.cuda.device(grad_out.device):
+        ws_bytes = lib.lwl_fht_backward_workspace_bytes(code, int(latent_size), int(size), int(layers),
+                                                        int(start), int(stop), int(flags))
+        ws, _ = _workspace(ws_bytes, grad_out.device)
+        _check(lib.lwl_fht_backward(code, grad_out.data_ptr(), int(latent_size), int(size), int(layers),
+                                    _seed_u64(seed), int(start), int(stop), grad.data_ptr(),
+                                    ws.data_ptr() if ws is not None else None, ws_bytes, int(flags),
+                                    _stream_ptr(grad_out.device)))
+    return grad
+
+
+def sign_words(seed: int, block: int, layer: int, first_word: int, count: int,
+               device: torch.device | str = "cuda") -> torch.Tensor:
+    """Sign words [count] as int64 (values 0..2^32-1) computed on the GPU."""
+    lib = load()
+    device = torch.device(device)
+    out = torch.empty(int(count), dtype=torch.int32, device=device)
+    with torch.cuda.device(device):
+        _check(lib.lwl_sign_words(_seed_u64(seed), int(block), int(layer), int(first_word), int(count),
+                                  out.data_ptr() if count else None, _stream_ptr(device)))
+    return out.to(torch.int64) & 0xFFFFFFFF

@@ -1,0 +1,165 @@
+"""Parity of the CUDA BlockFHT transform (forward and backward) against the CPU oracle.
+
+Tolerances (relative L2 over the compared vector):
+  fp32: 1e-5 for outputs and latent gradients;
+  bf16 / fp16: 1e-2 against fp32 oracle math on the same rounded latent / grad_out.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_l2
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: 1e-5, torch.bfloat16: 1e-2, torch.float16: 1e-2}
+
+
+@pytest.fixture(scope="module")
+def nat(native_lib):
+    from latent_weight_lab import _native
+
+    return _native
+
+
+def _latent(L, seed, dtype, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    z = torch.randn(L, generator=g) * scale
+    return z.to(dtype)
+
+
+def _check_forward(nat, L, size, layers, seed, start, stop, dtype, flags=0):
+    z = _latent(L, 1000 + L + layers, dtype)
+    y = nat.fht_forward(z.cuda(), size, layers, seed, start, stop, flags=flags)
+    torch.cuda.synchronize()
+    ref = orc.fht_forward(z.float().numpy(), size, layers, seed, start, stop)
+    assert y.dtype == dtype and y.shape == (stop - start,)
+    if stop > start:
+        err = rel_l2(y.float().cpu().numpy(), ref)
+        assert err < TOL[dtype], f"forward rel-L2 {err:.3e} (L={L} size={size} layers={layers} {dtype})"
+
+
+def _check_backward(nat, L, size, layers, seed, start, stop, dtype, flags=0):
+    g = _latent(stop - start, 77 + L, dtype)
+    grad = nat.fht_backward(g.cuda(), L, size, layers, seed, start, stop, flags=flags)
+    torch.cuda.synchronize()
+    ref = orc.fht_backward(g.float().numpy(), L, size, layers, seed, start, stop)
+    assert grad.dtype == dtype and grad.shape == (L,)
+    err = rel_l2(grad.float().cpu().numpy(), ref)
+    assert err < TOL[dtype], f"backward rel-L2 {err:.3e} (L={L} size={size} layers={layers} {dtype})"
+
+
+CASES = [
+    # (L, size, layers, seed, start, stop)
+    (1, 5, 1, 3, 0, 5),
+    (7, 31, 2, 123, 3, 17),
+    (20, 1000, 3, 5, 0, 1000),
+    (32, 64, 1, 1, 0, 64),
+    (33, 200, 3, -1, 17, 199),
+    (1000, 5000, 3, 42, 0, 5000),
+    (4096, 8192, 1, 123, 17, 4099),
+    (20000, 65536, 1, 123, 111, 4096),
+    (32768, 3 * 32768 + 5, 3, 123, 0, 3 * 32768 + 5),
+    (30000, 200000, 2, 9, 12345, 190000),
+    (65536, 3 * 65536, 3, 7, 100, 3 * 65536 - 3),
+    ((1 << 20) - 3, 1 << 21, 1, 11, 1000, (1 << 21) - 7),
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"L{c[0]}_s{c[1]}_l{c[2]}" for c in CASES])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16], ids=["f32", "bf16", "f16"])
+def test_forward_parity(nat, case, dtype):
+    _check_forward(nat, *case, dtype)
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"L{c[0]}_s{c[1]}_l{c[2]}" for c in CASES])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+def test_backward_parity(nat, case, dtype):
+    _check_backward(nat, *case, dtype)
+
+
+@pytest.mark.parametrize("logb", range(5, 24))
+@pytest.mark.parametrize("layers", [1, 3])
+def test_every_block_size_fp32(nat, logb, layers):
+    B = 1 << logb
+    size = 2 * B + 17 if logb < 20 else B + 17
+    start, stop = (B // 3, size - 5) if logb < 20 else (B - 1000, B + 17)
+    _check_forward(nat, B, size, layers, 123, start, stop, torch.float32)
+    _check_backward(nat, B - 3, size, layers, 123, start, stop, torch.float32)
+
+
+def test_c1_against_reference_golden(nat, golden):
+    z = torch.from_numpy(golden["c1_latent"]).cuda()
+    y = nat.fht_forward(z, 108618, 3, 123, 0, 108618)
+    assert rel_l2(y.cpu().numpy(), golden["c1_y"]) < 1e-6
+    mid = nat.fht_forward(z, 108618, 3, 123, 1000, 2000)
+    assert torch.equal(mid, y[1000:2000])
+    g = torch.from_numpy(golden["c1_grad_out"]).cuda()
+    grad = nat.fht_backward(g, 1024, 108618, 3, 123, 0, 108618)
+    assert rel_l2(grad.cpu().numpy(), golden["c1_grad"]) < 1e-5
+
+
+@pytest.mark.parametrize("i", range(12))
+def test_reference_golden_cases(nat, golden, i):
+    L, size, layers, seed, start, stop = (int(v) for v in golden["cases"][i])
+    z = torch.from_numpy(golden[f"case{i}_latent"]).cuda()
+    y = nat.fht_forward(z, size, layers, seed, start, stop)
+    ref = golden[f"case{i}_out"]
+    if ref.size:
+        assert rel_l2(y.cpu().numpy(), ref) < 1e-6
+    g = torch.from_numpy(golden[f"case{i}_grad_out"]).cuda()
+    grad = nat.fht_backward(g, L, size, layers, seed, start, stop)
+    refg = golden[f"case{i}_grad"]
+    assert rel_l2(grad.cpu().numpy(), refg) < 1e-5 or np.abs(grad.cpu().numpy() - refg).max() < 1e-6
+
+
+def test_sign_words_bit_exact_on_device(nat, golden):
+    for point, word in zip(golden["sign_points"], golden["sign_words"]):
+        seed, block, layer, w = (int(v) for v in point)
+        got = nat.sign_words(seed, block, layer, w, 1)
+        assert int(got.item()) == int(word)
+    run = nat.sign_words(123, 77, 2, 0, 1024).cpu().numpy()
+    assert np.array_equal(run, golden["sign_run_123_77_2"].astype(np.int64))
+
+
+def test_exact_flag_bf16(nat):
+    _check_forward(nat, 32768, 4 * 32768, 3, 123, 0, 4 * 32768, torch.bfloat16, flags=nat.FLAG_EXACT)
+    _check_backward(nat, 32768, 4 * 32768, 3, 123, 0, 4 * 32768, torch.bfloat16, flags=nat.FLAG_EXACT)
+
+
+def test_empty_slice(nat):
+    z = torch.randn(300, device="cuda")
+    assert nat.fht_forward(z, 2048, 3, 77, 512, 512).numel() == 0
+    grad = nat.fht_backward(torch.empty(0, device="cuda"), 300, 2048, 3, 77, 512, 512)
+    assert torch.count_nonzero(grad) == 0
+
+
+def test_linearity_and_orthogonality_full_size(nat):
+    """Size-independent properties at the headline shape (B=32768, 2^25 coords)."""
+    B, nblk = 32768, 1024
+    z1 = torch.randn(B, device="cuda")
+    z2 = torch.randn(B, device="cuda")
+    y1 = nat.fht_forward(z1, B * nblk, 3, 123, 0, B * nblk)
+    y2 = nat.fht_forward(z2, B * nblk, 3, 123, 0, B * nblk)
+    y12 = nat.fht_forward(z1 + 2 * z2, B * nblk, 3, 123, 0, B * nblk)
+    assert rel_l2((y1 + 2 * y2).cpu().numpy(), y12.cpu().numpy()) < 1e-5
+    # every block is an orthonormal map of z: each block's norm equals |z|
+    norms = y1.view(nblk, B).norm(dim=1)
+    assert torch.allclose(norms, z1.norm().expand(nblk), rtol=1e-4)
+    # adjoint: <y(z), g> == <z, J^T g>
+    g = torch.randn(B * nblk, device="cuda")
+    grad = nat.fht_backward(g, B, B * nblk, 3, 123, 0, B * nblk)
+    lhs = torch.dot(y1.double(), g.double())
+    rhs = torch.dot(z1.double(), grad.double())
+    assert abs(lhs - rhs) / abs(lhs) < 1e-4
+
+
+def test_slice_equals_full_bf16_headline_shape(nat):
+    B = 32768
+    z = torch.randn(B, device="cuda").bfloat16()
+    full = nat.fht_forward(z, 64 * B, 3, 123, 0, 64 * B)
+    part = nat.fht_forward(z, 64 * B, 3, 123, 5 * B + 77, 9 * B + 3)
+    assert torch.equal(part, full[5 * B + 77: 9 * B + 3])

@@ -3,11 +3,11 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...           (N > 1)
 
-Workload (headline point): bf16 latent of 32768 values
-~N(0,1), padded block size 32768, layers=3, seed=123, 2^28 generated
-coordinates per GPU (8192 blocks).  One step = forward of all 2^28
+Workload (configuration 2 of the baseline, headline point): bf16 latent of
+32768 values ~N(0,1), padded block size 32768, layers=3, seed=123, 2^28
+generated coordinates per GPU (8192 blocks).  One step = forward of all 2^28
 coordinates + backward of an upstream gradient of the same size to the
-latent.  value = generated coordinates (all ranks) / step time, in Gcoords/s.
+latent.  value = generated coordinates (all ranks) / step time, Gcoords/s.
 
 Multi-GPU: blocks are independent, so rank r owns blocks
 [r*8192, (r+1)*8192) of one generator (weak scaling); the only exchange is
@@ -57,6 +57,7 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
+        self.lines: list[str] = []
 
     def __enter__(self):
         try:
@@ -68,7 +69,6 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -81,7 +81,7 @@ class ClockSampler:
     def summary(self) -> dict:
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
+        for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 8:
                 continue
@@ -98,68 +98,79 @@ class ClockSampler:
 
 
 def _dist_env():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return world, rank, local
+    return int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), \
+        int(os.environ.get("LOCAL_RANK", "0"))
 
 
-def cpu_sample(threads: int, blocks: int = 24) -> dict:
-    """Reference algorithm on the host (fp32, OpenMP): fwd+bwd of `blocks` blocks of the workload."""
+def cpu_sample(threads: int, seconds: float = 10.0, chunk_blocks: int = 64) -> dict:
+    """Reference algorithm on host cores (fp32, OpenMP): fwd+bwd over chunks of the
+    workload's blocks until about `seconds` have elapsed."""
     import numpy as np
 
     from oracle import oracle as orc
 
     rng = np.random.default_rng(0)
     z = rng.standard_normal(BLOCK).astype(np.float32)
-    size = blocks * BLOCK
+    size = chunk_blocks * BLOCK
     g = rng.standard_normal(size).astype(np.float32)
-    orc.fht_forward(z, BLOCK * 2, LAYERS, SEED, 0, BLOCK * 2, threads=threads)  # warm the library
-    t0 = time.perf_counter()
-    orc.fht_forward(z, size, LAYERS, SEED, 0, size, threads=threads)
-    orc.fht_backward(g, BLOCK, size, LAYERS, SEED, 0, size, threads=threads)
-    dt = time.perf_counter() - t0
-    return {"value": size / dt / 1e9, "unit": "Gcoords/s", "cores": threads, "kind": "port",
-            "sample": f"{blocks} blocks x {BLOCK} (fwd+bwd, fp32, layers={LAYERS}) of the bench workload, "
-                      f"{dt:.2f}s"}
-
-
-def run_reference(args) -> None:
-    world, rank, _ = _dist_env()
-    if rank != 0:
-        return
-    from oracle import oracle as orc
-
-    threads = orc.max_threads()
-    vals = []
-    for _ in range(max(args.warmup, 0)):
-        cpu_sample(threads, blocks=8)
-    t_all = []
-    for _ in range(args.steps):
-        r = cpu_sample(threads, blocks=16)
-        vals.append(r["value"])
-        t_all.append(16 * BLOCK / (r["value"] * 1e9))
-    value = statistics.median(vals)
-    line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "Gcoords/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * statistics.median(t_all),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": _config(args.gpus),
-        "cpu_baseline": {"value": value, "unit": "Gcoords/s", "cores": threads, "kind": "port",
-                         "sample": f"16 blocks x {BLOCK} per step, fwd+bwd, fp32 math (oracle/ C port, OpenMP)"},
-        "e2e": {"value": value, "unit": "Gcoords/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
+    orc.fht_forward(z, 2 * BLOCK, LAYERS, SEED, 0, 2 * BLOCK, threads=threads)  # warm the library
+    done, t0 = 0, time.perf_counter()
+    while True:
+        orc.fht_forward(z, size, LAYERS, SEED, 0, size, threads=threads)
+        orc.fht_backward(g, BLOCK, size, LAYERS, SEED, 0, size, threads=threads)
+        done += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds:
+            break
+    coords = done * size
+    return {"value": coords / dt / 1e9, "unit": "Gcoords/s", "cores": threads, "kind": "port",
+            "sample": f"{done} x {chunk_blocks} blocks of {BLOCK} (fwd+bwd, fp32 math, layers={LAYERS}) "
+                      f"of the bench workload in {dt:.1f}s"}
 
 
 def _config(n: int) -> dict:
     return {"workload": "C2 headline: BlockFHT fwd+bwd, bf16, block_size=32768, layers=3, 2^28 coords/GPU",
             "block_size": BLOCK, "layers": LAYERS, "seed": SEED, "coords_per_gpu": COORDS_PER_GPU,
-            "parallelism": f"block-sharded x{n}", "l2": "inputs and outputs (512 MiB each) exceed L2"}
+            "parallelism": f"block-sharded x{n}", "l2": "no flush: per-step output and upstream gradient "
+                                                        "(512 MiB each) exceed the 126 MB L2"}
+
+
+def run_reference(args) -> None:
+    _, rank, _ = _dist_env()
+    if rank != 0:
+        return
+    from oracle import oracle as orc
+
+    threads = orc.max_threads()
+    for _ in range(max(args.warmup, 0)):
+        cpu_sample(threads, seconds=0.5)
+    vals = [cpu_sample(threads, seconds=8.0)["value"] for _ in range(args.steps)]
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "Gcoords/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * COORDS_PER_GPU / (value * 1e9),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": _config(args.gpus),
+        "cpu_baseline": {"value": value, "unit": "Gcoords/s", "cores": threads, "kind": "port",
+                         "sample": "per step: ~8 s of fwd+bwd over 64-block chunks of the workload, fp32 math "
+                                   "(oracle/ C restatement of the reference algorithm, OpenMP)"},
+        "e2e": {"value": value, "unit": "Gcoords/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _traffic_from_profiles(which: str):
+    """DRAM bytes per launch measured with ncu, recorded in profiles/traffic.json (None if absent)."""
+    p = REPO / "profiles" / "traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get(which)
+        except (ValueError, OSError):
+            return None
+    return None
 
 
 def run_ours(args) -> None:
-    import numpy as np
     import torch
     import torch.distributed as dist
 
@@ -189,15 +200,13 @@ def run_ours(args) -> None:
     sp = stream.cuda_stream
 
     def fwd():
-        st = lib.lwl_fht_forward(code, z.data_ptr(), BLOCK, size_total, LAYERS, SEED, start, stop, y.data_ptr(),
-                                 ws.data_ptr(), ws.numel(), 0, sp)
-        if st:
+        if lib.lwl_fht_forward(code, z.data_ptr(), BLOCK, size_total, LAYERS, SEED, start, stop, y.data_ptr(),
+                               ws.data_ptr(), ws.numel(), 0, sp):
             raise RuntimeError(lib.lwl_last_error().decode())
 
     def bwd():
-        st = lib.lwl_fht_backward(code, g.data_ptr(), BLOCK, size_total, LAYERS, SEED, start, stop, grad.data_ptr(),
-                                  ws.data_ptr(), ws.numel(), 0, sp)
-        if st:
+        if lib.lwl_fht_backward(code, g.data_ptr(), BLOCK, size_total, LAYERS, SEED, start, stop, grad.data_ptr(),
+                                ws.data_ptr(), ws.numel(), 0, sp):
             raise RuntimeError(lib.lwl_last_error().decode())
         if world > 1:
             dist.all_reduce(grad)
@@ -211,12 +220,10 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
-           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    ev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index) as clk:
         torch.cuda.synchronize()
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
         t0.record(stream)
         for a, b, c in ev:
             a.record(stream)
@@ -230,14 +237,15 @@ def run_ours(args) -> None:
     f_ms = [a.elapsed_time(b) for a, b, _ in ev]
     b_ms = [b.elapsed_time(c) for _, b, c in ev]
     if world > 1:
-        t = torch.tensor([total_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
+        tt = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        total_ms = float(tt.item())
     ms_step = total_ms / args.steps
     value = size_total / (ms_step * 1e-3) / 1e9
 
-    # end to end through the public module API: latent from pinned host memory, forward, backward
-    # with a device-resident upstream gradient, latent gradient read back to the host.
+    # End to end through the public module API: latent copied from pinned host
+    # memory, forward, backward of a device-resident upstream gradient, latent
+    # gradient read back to pinned host memory.
     mod = BlockFHT(torch.nn.Parameter(z.clone()), size=size_total, layers=LAYERS, seed=SEED)
     grad_host = torch.empty(BLOCK, dtype=torch.bfloat16).pin_memory()
 
@@ -264,9 +272,9 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
     if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+        tt = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
 
     if rank == 0:
         peaks = _peaks()
@@ -277,7 +285,6 @@ def run_ours(args) -> None:
         dom_is_f = fm >= bm
         dom_ms, dom_bytes = (fm, f_bytes) if dom_is_f else (bm, b_bytes)
         achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
-        traffic = _traffic_from_profiles("fwd" if dom_is_f else "bwd")
         line = {
             "metric": METRIC, "value": value, "unit": "Gcoords/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
@@ -287,8 +294,9 @@ def run_ours(args) -> None:
             "backward_gcoords_s": COORDS_PER_GPU / (bm * 1e-3) / 1e9,
             "roofline": {"bound": "hbm", "kernel": "forward" if dom_is_f else "backward", "achieved": achieved,
                          "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
-                         "traffic": traffic, "peak_source": peaks["source"],
-                         "bytes_per_launch": dom_bytes, "ms_per_launch": dom_ms},
+                         "traffic": _traffic_from_profiles("fwd" if dom_is_f else "bwd"),
+                         "peak_source": peaks["source"], "bytes_per_launch": dom_bytes,
+                         "ms_per_launch": dom_ms},
             "e2e": {"value": size_total / (e2e_ms * 1e-3) / 1e9, "unit": "Gcoords/s",
                     "h2d_bytes_per_step": BLOCK * 2, "d2h_bytes_per_step": BLOCK * 2,
                     "ms_per_step": e2e_ms, "api": "BlockFHT.slice + backward(upstream grad)"},
@@ -305,17 +313,6 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
-def _traffic_from_profiles(which: str):
-    """DRAM bytes per launch recorded from ncu in profiles/ (None if not captured yet)."""
-    p = REPO / "profiles" / "traffic.json"
-    if p.exists():
-        try:
-            return json.loads(p.read_text()).get(which)
-        except (ValueError, OSError):
-            return None
-    return None
-
-
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -324,8 +321,6 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
-    if args.warmup < 3 and args.impl == "ours":
-        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":
         run_reference(args)
     else:

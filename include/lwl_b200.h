@@ -82,6 +82,14 @@ int lwl_fht_backward(int dtype, const void* grad_out, int64_t latent_size, int64
                      int layers, uint64_t seed, int64_t start, int64_t stop, void* grad_latent,
                      void* workspace, size_t workspace_bytes, unsigned flags, void* stream);
 
+/* Number of kernel launches one lwl_fht_forward (backward = 0) or
+ * lwl_fht_backward (backward = 1) call with these arguments enqueues; -1 on
+ * invalid arguments.  No reference counterpart (the reference launches
+ * layers*(log2 B + 1) + 2 kernels for large blocks, csrc/block_fht_ext_cuda.cu:546-564);
+ * used for launch accounting and graph-capture planning. */
+int lwl_fht_launch_count(int dtype, int64_t latent_size, int64_t size, int layers, int64_t start,
+                         int64_t stop, int backward, unsigned flags);
+
 #ifdef __cplusplus
 }
 #endif

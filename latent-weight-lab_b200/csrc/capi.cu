@@ -9,6 +9,7 @@
 #include <cstring>
 
 #include "fht_engine.h"
+#include "fht_mma.h"
 #include "lwl_b200.h"
 #include "lwl_common.cuh"
 
@@ -80,6 +81,13 @@ static int fht_call(bool backward, int dtype, const void* in, void* out, int64_t
   a.workspace = ws;
   a.workspace_bytes = ws_bytes;
   a.flags = flags;
+  if (!backward && mma_forward_supported(dtype, L, flags)) {
+    if (mma_forward(dtype, in, L, layers, seed, start, stop, out, reinterpret_cast<cudaStream_t>(stream)) != 0) {
+      set_error("tensor-core forward launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+      return LWL_ERR_CUDA;
+    }
+    return LWL_OK;
+  }
   FhtPlan plan;
   plan_fht(a, plan);
   if (plan.ws_bytes > 0 && (ws == nullptr || ws_bytes < plan.ws_bytes)) {
@@ -92,6 +100,7 @@ static int fht_call(bool backward, int dtype, const void* in, void* out, int64_t
 static size_t fht_ws(bool backward, int dtype, int64_t L, int64_t size, int layers, int64_t start,
                      int64_t stop, unsigned flags) {
   if (validate_fht(dtype, L, size, layers, start, stop) != LWL_OK) return 0;
+  if (!backward && mma_forward_supported(dtype, L, flags)) return 0;
   FhtArgs a;
   std::memset(&a, 0, sizeof(a));
   a.dtype = dtype;
@@ -172,6 +181,26 @@ int lwl_fht_backward(int dtype, const void* grad_out, int64_t latent_size, int64
                      size_t workspace_bytes, unsigned flags, void* stream) {
   return lwl::fht_call(true, dtype, grad_out, grad_latent, latent_size, size, layers, seed, start, stop,
                        workspace, workspace_bytes, flags, stream);
+}
+
+int lwl_fht_launch_count(int dtype, int64_t latent_size, int64_t size, int layers, int64_t start, int64_t stop,
+                         int backward, unsigned flags) {
+  if (lwl::validate_fht(dtype, latent_size, size, layers, start, stop) != LWL_OK) return -1;
+  if (stop == start) return 0;
+  if (!backward && lwl::mma_forward_supported(dtype, latent_size, flags)) return 1;
+  lwl::FhtArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.dtype = dtype;
+  a.backward = backward != 0;
+  a.latent_size = latent_size;
+  a.size = size;
+  a.layers = layers;
+  a.start = start;
+  a.stop = stop;
+  a.flags = flags;
+  lwl::FhtPlan plan;
+  lwl::plan_fht(a, plan);
+  return plan.nlaunch + (backward ? 1 : 0);
 }
 
 }  // extern "C"

@@ -1,0 +1,413 @@
+// fht_mma.cu -- tensor-core BlockFHT forward for 16-bit dtypes at block size 2^15.
+//
+// H_32768 is factored over the 15 position bits into 16x16 mma tiles.  A
+// block lives in the registers of 16 warps (8 tiles of 256 elements per
+// warp); two "passes" alternate:
+//   pass A transforms position bits {5,6,7,3} (tile rows, H16) and
+//          {4,9,10,11} (tile cols, H16);
+//   pass B transforms bits {0,1,2,8} (rows, H16) and {12,13,14} (cols, H8;
+//          col bit 0 = position bit 4 is carried through as an identity).
+// Within a pass, H is applied to the tile rows as H*X (data in the
+// B-operand slot) and to the columns as X*H (data in the A-operand slot);
+// the f16 accumulator fragment of one mma is directly the A fragment of the
+// next, so a pass needs no register shuffles.  Adjacent layers share a pass
+// ([A s A], [B s B]), so three layers cost three shared-memory exchanges.
+// Each exchange writes 16-byte chunks gathered across the 8 tiles a thread
+// owns (st.shared.v4) and reads them back with ldmatrix; the XOR swizzles in
+// lay_ab / lay_ba make both sides bank-conflict free.
+//
+// Arithmetic: fp16 operands and intermediates with orthonormal factors
+// (H16/4, H8/2).  The latent is pre-scaled by a power of two so its L2 norm
+// sits in [2^11, 2^12) -- every intermediate element is bounded by the
+// block's norm, so nothing overflows, and typical elements stay far from
+// subnormals.  The last column transform accumulates in fp32, is rescaled
+// and rounded once to the output dtype.  Signs are XORed into packed pairs:
+// positions p and p+16 share a register, so one shift + LOP3 flips both.
+#include <cstdio>
+
+#include "fht_mma.h"
+#include "lwl_common.cuh"
+
+namespace lwl {
+namespace fmma {
+
+constexpr int kLog = 15;
+constexpr int kB = 1 << kLog;
+constexpr int kThreads = 512;
+constexpr int kWords = kB / 32;
+
+// position of element (warp w, tile k, tile row R, tile col C) in each pass
+__device__ __forceinline__ int dep_a(int w, int k, int R, int C) {
+  return k | ((R >> 3) & 1) << 3 | (C & 1) << 4 | (R & 7) << 5 | (w & 1) << 8 | ((C >> 1) & 3) << 9 |
+         ((C >> 3) & 1) << 11 | (w >> 1) << 12;
+}
+__device__ __forceinline__ int dep_b(int w, int k, int R, int C) {
+  return (R & 7) | (w & 1) << 3 | (C & 1) << 4 | k << 5 | ((R >> 3) & 1) << 8 | (w >> 1) << 9 | (C >> 1) << 12;
+}
+// shared-memory element offset of position p in the two exchange layouts
+__device__ __forceinline__ int lay_ab(int p) {  // 8-element chunks along bits 0-2
+  int c = p >> 3;
+  int s = (((p >> 9) ^ (p >> 12)) & 1) | ((p >> 10) & 1) << 1 | ((p >> 13) & 1) << 2;
+  return ((c ^ s) << 3) | (p & 7);
+}
+__device__ __forceinline__ int lay_ba(int p) {  // 8-element chunks along bits 5-7
+  int c = (p & 31) | ((p >> 8) << 5);
+  int s = ((p >> 4) & 1) | (((p >> 9) ^ (p >> 12)) & 1) << 1 | (((p >> 10) ^ (p >> 13)) & 1) << 2;
+  return ((c ^ s) << 3) | ((p >> 5) & 7);
+}
+
+template <int PASS> struct Pass;
+template <> struct Pass<0> {  // A: reads the B->A layout, writes the A->B layout
+  static __device__ __forceinline__ int dep(int w, int k, int R, int C) { return dep_a(w, k, R, C); }
+  static __device__ __forceinline__ int lay_in(int p) { return lay_ba(p); }
+  static __device__ __forceinline__ int lay_out(int p) { return lay_ab(p); }
+};
+template <> struct Pass<1> {  // B
+  static __device__ __forceinline__ int dep(int w, int k, int R, int C) { return dep_b(w, k, R, C); }
+  static __device__ __forceinline__ int lay_in(int p) { return lay_ab(p); }
+  static __device__ __forceinline__ int lay_out(int p) { return lay_ba(p); }
+};
+
+__device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ uint32_t movt(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(d) : "r"(a));
+  return d;
+}
+// D(16x8, f16) = A(16x16, f16) * B(16x8, f16)
+__device__ __forceinline__ void mma16(uint32_t& d0, uint32_t& d1, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                      uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f16.f16.f16.f16 {%0,%1}, {%2,%3,%4,%5}, {%6,%7}, {%8,%8};\n"
+      : "=r"(d0), "=r"(d1)
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0u));
+}
+// D(16x8, f32) = A * B
+__device__ __forceinline__ void mma32(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                      uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ int hsign(int i, int j) { return (__popc(i & j) & 1) ? -1 : 1; }
+
+template <typename T> __device__ __forceinline__ uint32_t pack_out(float lo, float hi);
+template <> __device__ __forceinline__ uint32_t pack_out<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <> __device__ __forceinline__ uint32_t pack_out<__half>(float lo, float hi) { return pack_h2(lo, hi); }
+
+struct Frags {
+  uint32_t hA[4];      // H16/4 as the A operand (row transform H*X)
+  uint32_t h16[2][2];  // H16/4 as the B operand, per 8-column half (column transform X*H)
+  uint32_t h8[2][2];   // (H8 (x) I2)/2 as the B operand
+};
+
+__device__ __forceinline__ void make_frags(Frags& f, int g, int t) {
+  const float q = 0.25f;
+  f.hA[0] = pack_h2(q * hsign(g, 2 * t), q * hsign(g, 2 * t + 1));
+  f.hA[1] = pack_h2(q * hsign(g + 8, 2 * t), q * hsign(g + 8, 2 * t + 1));
+  f.hA[2] = pack_h2(q * hsign(g, 2 * t + 8), q * hsign(g, 2 * t + 9));
+  f.hA[3] = pack_h2(q * hsign(g + 8, 2 * t + 8), q * hsign(g + 8, 2 * t + 9));
+#pragma unroll
+  for (int nh = 0; nh < 2; ++nh) {
+    int n = g + 8 * nh;
+    f.h16[nh][0] = pack_h2(q * hsign(2 * t, n), q * hsign(2 * t + 1, n));
+    f.h16[nh][1] = pack_h2(q * hsign(2 * t + 8, n), q * hsign(2 * t + 9, n));
+    auto h8 = [&](int c, int cp) -> float { return ((c & 1) == (cp & 1)) ? 0.5f * hsign(c >> 1, cp >> 1) : 0.0f; };
+    f.h8[nh][0] = pack_h2(h8(2 * t, n), h8(2 * t + 1, n));
+    f.h8[nh][1] = pack_h2(h8(2 * t + 8, n), h8(2 * t + 9, n));
+  }
+}
+
+// Row transform (H*X): X as B-operand fragments {x0,x1} (cols 0-7), {x2,x3}
+// (cols 8-15); result in accumulator (= A operand) layout.
+__device__ __forceinline__ void row_tf(const Frags& f, const uint32_t* x, uint32_t* a) {
+  mma16(a[0], a[1], f.hA[0], f.hA[1], f.hA[2], f.hA[3], x[0], x[1]);
+  mma16(a[2], a[3], f.hA[0], f.hA[1], f.hA[2], f.hA[3], x[2], x[3]);
+}
+// Column transform (X*Hc): A layout -> A layout.
+template <int PASS>
+__device__ __forceinline__ void col_tf(const Frags& f, uint32_t* a) {
+  const uint32_t(*h)[2] = PASS == 0 ? f.h16 : f.h8;
+  uint32_t d0, d1, d2, d3;
+  mma16(d0, d1, a[0], a[1], a[2], a[3], h[0][0], h[0][1]);
+  mma16(d2, d3, a[0], a[1], a[2], a[3], h[1][0], h[1][1]);
+  a[0] = d0;
+  a[1] = d1;
+  a[2] = d2;
+  a[3] = d3;
+}
+// A layout -> B-operand layout of the same tile (8x8 transposes)
+__device__ __forceinline__ void to_bop(const uint32_t* a, uint32_t* x) {
+  x[0] = movt(a[0]);
+  x[1] = movt(a[1]);
+  x[2] = movt(a[2]);
+  x[3] = movt(a[3]);
+}
+
+// XOR the signs of one layer into accumulator-layout registers of tile k.
+// Register j holds (R = g + 8(j&1), C = 2t + 8(j>>1) + {0,1}); the pair sits
+// at positions p and p+16 (C bit 0 is position bit 4).
+template <int PASS>
+__device__ __forceinline__ void sign_acc(uint32_t* a, const uint32_t* sw, int w, int k, int g, int t) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    int p = Pass<PASS>::dep(w, k, g + 8 * (j & 1), 2 * t + 8 * (j >> 1));
+    uint32_t u = ~sw[p >> 5];
+    a[j] ^= (u << (15 - (p & 15))) & 0x80008000u;
+  }
+}
+
+// Signs applied to B-operand fragments (first run): register m holds
+// (R = 2t + 8(m&1) + {0,1}, C = g + 8(m>>1)).
+template <int PASS>
+__device__ __forceinline__ void sign_bop(uint32_t* x, const uint32_t* sw, int w, int k, int g, int t) {
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    int R = 2 * t + 8 * (m & 1), C = g + 8 * (m >> 1);
+    int p0 = Pass<PASS>::dep(w, k, R, C);
+    int p1 = Pass<PASS>::dep(w, k, R + 1, C);
+    uint32_t b0 = (sw[p0 >> 5] >> (p0 & 31)) & 1u;
+    uint32_t b1 = (sw[p1 >> 5] >> (p1 & 31)) & 1u;
+    x[m] ^= ((b0 ^ 1u) << 15) | ((b1 ^ 1u) << 31);
+  }
+}
+
+// Gather the thread's 8 tiles into 16-byte chunks in the next pass's layout.
+template <int PASS>
+__device__ __forceinline__ void write_exchange(uint32_t (*d)[4], uint32_t base, int w, int g, int t) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t sel = h ? 0x7632u : 0x5410u;
+      int p = Pass<PASS>::dep(w, 0, g + 8 * (j & 1), 2 * t + h + 8 * (j >> 1));
+      uint32_t addr = base + 2u * (uint32_t)Pass<PASS>::lay_out(p);
+      uint32_t v0 = prmt(d[0][j], d[1][j], sel), v1 = prmt(d[2][j], d[3][j], sel);
+      uint32_t v2 = prmt(d[4][j], d[5][j], sel), v3 = prmt(d[6][j], d[7][j], sel);
+      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};\n" ::"r"(addr), "r"(v0), "r"(v1), "r"(v2), "r"(v3));
+    }
+  }
+}
+
+template <int PASS>
+__device__ __forceinline__ void load_tile(uint32_t base, int w, int k, int lane, uint32_t* x) {
+  int mm = lane >> 3, rr = lane & 7;
+  int p = Pass<PASS>::dep(w, k, 8 * (mm & 1), rr + 8 * (mm >> 1));
+  ldsm4(base + 2u * (uint32_t)Pass<PASS>::lay_in(p), x[0], x[1], x[2], x[3]);
+}
+
+// One run of pass PASS: read the input buffer, row + col transforms (and for
+// DOUBLE runs sign + col + row of the next layer), write the output buffer.
+template <int PASS, bool DOUBLE, bool PRESIGN>
+__device__ __forceinline__ void run(const Frags& f, uint32_t in_base, uint32_t out_base, const uint32_t* pre_sw,
+                                    const uint32_t* mid_sw, int w, int lane, int g, int t) {
+  uint32_t d[8][4];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    uint32_t x[4];
+    load_tile<PASS>(in_base, w, k, lane, x);
+    if (PRESIGN) sign_bop<PASS>(x, pre_sw, w, k, g, t);
+    row_tf(f, x, d[k]);
+    col_tf<PASS>(f, d[k]);
+    if (DOUBLE) {
+      sign_acc<PASS>(d[k], mid_sw, w, k, g, t);
+      col_tf<PASS>(f, d[k]);
+      uint32_t y[4];
+      to_bop(d[k], y);
+      row_tf(f, y, d[k]);
+    }
+  }
+  write_exchange<PASS>(d, out_base, w, g, t);
+}
+
+// Final run (pass A): row transform, column transform accumulated in fp32,
+// rescale, round to the output dtype, last sign, store to global memory.
+template <typename T>
+__device__ __forceinline__ void run_final(const Frags& f, uint32_t in_base, const uint32_t* sw, float scale,
+                                          T* out, int64_t blk, int64_t start, int64_t stop, bool vec_ok, int w,
+                                          int lane, int g, int t) {
+  uint32_t o[8][4];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    uint32_t x[4], a[4];
+    load_tile<0>(in_base, w, k, lane, x);
+    row_tf(f, x, a);
+    float c0[4], c1[4];
+    mma32(c0, a[0], a[1], a[2], a[3], f.h16[0][0], f.h16[0][1]);
+    mma32(c1, a[0], a[1], a[2], a[3], f.h16[1][0], f.h16[1][1]);
+    o[k][0] = pack_out<T>(c0[0] * scale, c0[1] * scale);
+    o[k][1] = pack_out<T>(c0[2] * scale, c0[3] * scale);
+    o[k][2] = pack_out<T>(c1[0] * scale, c1[1] * scale);
+    o[k][3] = pack_out<T>(c1[2] * scale, c1[3] * scale);
+    sign_acc<0>(o[k], sw, w, k, g, t);
+  }
+  const int64_t bbase = blk * kB;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t sel = h ? 0x7632u : 0x5410u;
+      int p = dep_a(w, 0, g + 8 * (j & 1), 2 * t + h + 8 * (j >> 1));
+      uint32_t v0 = prmt(o[0][j], o[1][j], sel), v1 = prmt(o[2][j], o[3][j], sel);
+      uint32_t v2 = prmt(o[4][j], o[5][j], sel), v3 = prmt(o[6][j], o[7][j], sel);
+      int64_t gi = bbase + p;  // this chunk covers coordinates gi .. gi+7
+      if (vec_ok && gi >= start && gi + 8 <= stop) {
+        *reinterpret_cast<uint4*>(out + (gi - start)) = make_uint4(v0, v1, v2, v3);
+      } else {
+        uint32_t vv[4] = {v0, v1, v2, v3};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          int64_t gg = gi + e;
+          if (gg >= start && gg < stop)
+            reinterpret_cast<uint16_t*>(out)[gg - start] = (uint16_t)(vv[e >> 1] >> (16 * (e & 1)));
+        }
+      }
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    fht15_forward_kernel(const T* __restrict__ latent, int64_t L, int layers, uint32_t seed32, int64_t first_block,
+                         int64_t nblocks, int64_t start, int64_t stop, T* __restrict__ out) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint16_t* zbuf = reinterpret_cast<uint16_t*>(smem);   // scaled fp16 latent copy (64 KB)
+  uint16_t* xbuf = zbuf + kB;                           // exchange buffers (64 KB each)
+  uint16_t* ybuf = xbuf + kB;
+  uint32_t* sw = reinterpret_cast<uint32_t*>(ybuf + kB);  // sign words [layers+1][1024]
+  __shared__ float red[kThreads / 32];
+  __shared__ int k0_shared;
+
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
+  Frags f;
+  make_frags(f, g, t);
+
+  // power-of-two prescale: latent L2 norm into [2^11, 2^12)
+  float ss = 0.0f;
+  for (int64_t i = tid; i < L; i += kThreads) {
+    float v = Cvt<T>::to_f(latent[i]);
+    ss += v * v;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) red[w] = ss;
+  __syncthreads();
+  if (tid == 0) {
+    float s = 0.0f;
+    for (int i = 0; i < kThreads / 32; ++i) s += red[i];
+    int e = 0;
+    if (s > 0.0f) {
+      frexpf(sqrtf(s), &e);  // norm = m * 2^e with m in [0.5, 1)
+      e -= 12;
+    }
+    k0_shared = e;
+  }
+  __syncthreads();
+  const int k0 = k0_shared;
+  const float in_scale = ldexpf(1.0f, -k0);
+  // the first run is pass B for layers 1 and 3, pass A for layers 2
+  const bool first_is_b = (layers != 2);
+  for (int p = tid; p < kB; p += kThreads) {
+    float v = p < L ? Cvt<T>::to_f(latent[p]) * in_scale : 0.0f;
+    __half h = __float2half_rn(v);
+    zbuf[first_is_b ? lay_ab(p) : lay_ba(p)] = *reinterpret_cast<uint16_t*>(&h);
+  }
+  // per layer the factors are orthonormal up to sqrt(2) (the H8/2 factor)
+  const float out_scale = ldexpf(1.0f, k0) * (layers == 1   ? 0.70710678118654752f
+                                              : layers == 2 ? 0.5f
+                                                            : 0.35355339059327376f);
+  const uint32_t zb = (uint32_t)__cvta_generic_to_shared(zbuf);
+  const uint32_t xb = (uint32_t)__cvta_generic_to_shared(xbuf);
+  const uint32_t yb = (uint32_t)__cvta_generic_to_shared(ybuf);
+  const bool vec_ok = ((start & 7) == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+
+  for (int64_t bi = blockIdx.x; bi < nblocks; bi += gridDim.x) {
+    const int64_t blk = first_block + bi;
+    __syncthreads();  // the previous block is done with the sign table and buffers
+    for (int i = tid; i < (layers + 1) * kWords; i += kThreads) {
+      int l = i / kWords, wd = i - l * kWords;
+      sw[i] = sign_word(block_layer_key(seed32, blk, l), wd);
+    }
+    __syncthreads();
+    if (layers == 1) {
+      run<1, false, true>(f, zb, xb, sw, nullptr, w, lane, g, t);
+      __syncthreads();
+      run_final<T>(f, xb, sw + 1 * kWords, out_scale, out, blk, start, stop, vec_ok, w, lane, g, t);
+    } else if (layers == 2) {
+      run<0, false, true>(f, zb, yb, sw, nullptr, w, lane, g, t);
+      __syncthreads();
+      run<1, true, false>(f, yb, xb, nullptr, sw + 1 * kWords, w, lane, g, t);
+      __syncthreads();
+      run_final<T>(f, xb, sw + 2 * kWords, out_scale, out, blk, start, stop, vec_ok, w, lane, g, t);
+    } else {
+      run<1, false, true>(f, zb, xb, sw, nullptr, w, lane, g, t);
+      __syncthreads();
+      run<0, true, false>(f, xb, yb, nullptr, sw + 1 * kWords, w, lane, g, t);
+      __syncthreads();
+      run<1, true, false>(f, yb, xb, nullptr, sw + 2 * kWords, w, lane, g, t);
+      __syncthreads();
+      run_final<T>(f, xb, sw + 3 * kWords, out_scale, out, blk, start, stop, vec_ok, w, lane, g, t);
+    }
+  }
+}
+
+constexpr size_t kSmem = 3 * kB * 2 + 4 * kWords * 4;
+
+template <typename T>
+int launch_forward_t(const void* latent, int64_t L, int layers, uint32_t seed32, int64_t first_block,
+                     int64_t nblocks, int64_t start, int64_t stop, void* out, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(fht15_forward_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem) !=
+        cudaSuccess)
+      return -1;
+    attr = true;
+  }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int grid = (int)(nblocks < sms ? nblocks : sms);
+  fht15_forward_kernel<T><<<grid, kThreads, kSmem, st>>>(reinterpret_cast<const T*>(latent), L, layers, seed32,
+                                                         first_block, nblocks, start, stop,
+                                                         reinterpret_cast<T*>(out));
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace fmma
+
+bool mma_forward_supported(int dtype, int64_t latent_size, unsigned flags) {
+  if (flags & LWL_FLAG_EXACT) return false;
+  if (dtype != LWL_BF16 && dtype != LWL_F16) return false;
+  return next_pow2(latent_size) == fmma::kB;
+}
+
+int mma_forward(int dtype, const void* latent, int64_t L, int layers, uint64_t seed, int64_t start, int64_t stop,
+                void* out, cudaStream_t st) {
+  const int64_t B = fmma::kB;
+  int64_t first = start / B, last = (stop + B - 1) / B;
+  if (last <= first) return 0;
+  uint32_t s32 = fold_seed(seed);
+  if (dtype == LWL_BF16)
+    return fmma::launch_forward_t<__nv_bfloat16>(latent, L, layers, s32, first, last - first, start, stop, out, st);
+  return fmma::launch_forward_t<__half>(latent, L, layers, s32, first, last - first, start, stop, out, st);
+}
+
+}  // namespace lwl

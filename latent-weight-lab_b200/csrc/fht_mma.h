@@ -1,0 +1,14 @@
+// fht_mma.h -- tensor-core transform paths (16-bit dtypes) selected by the C ABI.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace lwl {
+
+// True when lwl_fht_forward with these arguments runs on the tensor-core kernel.
+bool mma_forward_supported(int dtype, int64_t latent_size, unsigned flags);
+// Tensor-core forward for padded block size 2^15; returns 0 or -1 (launch failure).
+int mma_forward(int dtype, const void* latent, int64_t latent_size, int layers, uint64_t seed, int64_t start,
+                int64_t stop, void* out, cudaStream_t st);
+
+}  // namespace lwl

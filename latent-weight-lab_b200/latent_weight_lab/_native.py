@@ -48,6 +48,8 @@ def _declare(lib: ctypes.CDLL) -> None:
         fn = getattr(lib, name)
         fn.restype = sz
         fn.argtypes = [ci, i64, i64, ci, i64, i64, cu]
+    lib.lwl_fht_launch_count.restype = ci
+    lib.lwl_fht_launch_count.argtypes = [ci, i64, i64, ci, i64, i64, ci, cu]
     for name in ("lwl_fht_forward", "lwl_fht_backward"):
         fn = getattr(lib, name)
         fn.restype = ci

@@ -90,6 +90,23 @@ int lwl_fht_backward(int dtype, const void* grad_out, int64_t latent_size, int64
 int lwl_fht_launch_count(int dtype, int64_t latent_size, int64_t size, int layers, int64_t start,
                          int64_t stop, int backward, unsigned flags);
 
+/* Same result as lwl_fht_backward, for callers that cannot allocate device
+ * memory (no workspace argument).  No counterpart in the reference.
+ * Intended for code that has no device allocator at hand, e.g. a plugin
+ * called from a host runtime that owns all device memory, or a callback whose
+ * memory policy forbids allocating.  The per-CTA partial gradients live in a
+ * fixed 8 MiB device array inside the library instead of a workspace:
+ *  - padded block size at most 2^14, else LWL_ERR_UNSUPPORTED;
+ *  - every GPU that loads the library holds the 8 MiB until the process exits;
+ *  - the first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress with that device current); make that first call
+ *    before any stream capture;
+ *  - all calls on a device share the array; calls that overlap on the GPU
+ *    race on it and give wrong results: order them on one stream. */
+int lwl_fht_backward_noalloc(int dtype, const void* grad_out, int64_t latent_size, int64_t size,
+                             int layers, uint64_t seed, int64_t start, int64_t stop, void* grad_latent,
+                             unsigned flags, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

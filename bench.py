@@ -63,7 +63,10 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            first = self.proc.stdout.readline()  # sampler is running before the timed region starts
+            if first.strip():
+                self.lines.append(first)
         except OSError:
             self.proc = None
         return self
@@ -76,7 +79,7 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+            self.lines = self.lines[1:] + [ln for ln in out.splitlines() if ln.strip()]
 
     def summary(self) -> dict:
         sm, mx, reasons = [], 0.0, set()
@@ -316,7 +319,7 @@ def run_ours(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")

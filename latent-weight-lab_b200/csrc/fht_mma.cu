@@ -238,47 +238,68 @@ __device__ __forceinline__ void run(const Frags& f, uint32_t in_base, uint32_t o
   write_exchange<PASS>(d, out_base, w, g, t);
 }
 
-// Final run (pass A): row transform, column transform accumulated in fp32,
-// rescale, round to the output dtype, last sign, store to global memory.
+// Natural-order staging layout for the output: chunk c = p >> 3 of 8
+// consecutive positions, XOR-swizzled so both the gathering writer (varies
+// chunk bits 2,6,7 within a phase) and the linear copy-out reader (bits 0-2)
+// are bank-conflict free.
+__device__ __forceinline__ int lay_nat_chunk(int c) { return c ^ ((c >> 6) & 3); }
+
+// Last row transform + column transform of pass A accumulated in fp32 for
+// tile k; f[0..3] / f[4..7] = column halves 0 / 1 in accumulator layout.
+__device__ __forceinline__ void final_tile(const Frags& f, uint32_t in_base, int w, int k, int lane, float* c) {
+  uint32_t x[4], a[4];
+  load_tile<0>(in_base, w, k, lane, x);
+  row_tf(f, x, a);
+  mma32(c, a[0], a[1], a[2], a[3], f.h16[0][0], f.h16[0][1]);
+  mma32(c + 4, a[0], a[1], a[2], a[3], f.h16[1][0], f.h16[1][1]);
+}
+
+// Final run (pass A): transforms, rescale, round to the output dtype, last
+// sign, then stage the block in natural order in shared memory and copy it
+// out with full 16-byte-per-lane contiguous stores.
 template <typename T>
-__device__ __forceinline__ void run_final(const Frags& f, uint32_t in_base, const uint32_t* sw, float scale,
-                                          T* out, int64_t blk, int64_t start, int64_t stop, bool vec_ok, int w,
-                                          int lane, int g, int t) {
+__device__ __forceinline__ void run_final(const Frags& f, uint32_t in_base, uint32_t stage_base,
+                                          const uint16_t* stage, const uint32_t* sw, float scale, T* out,
+                                          int64_t blk, int64_t start, int64_t stop, bool vec_ok, int w, int lane,
+                                          int g, int t) {
   uint32_t o[8][4];
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    uint32_t x[4], a[4];
-    load_tile<0>(in_base, w, k, lane, x);
-    row_tf(f, x, a);
-    float c0[4], c1[4];
-    mma32(c0, a[0], a[1], a[2], a[3], f.h16[0][0], f.h16[0][1]);
-    mma32(c1, a[0], a[1], a[2], a[3], f.h16[1][0], f.h16[1][1]);
-    o[k][0] = pack_out<T>(c0[0] * scale, c0[1] * scale);
-    o[k][1] = pack_out<T>(c0[2] * scale, c0[3] * scale);
-    o[k][2] = pack_out<T>(c1[0] * scale, c1[1] * scale);
-    o[k][3] = pack_out<T>(c1[2] * scale, c1[3] * scale);
+    float c[8];
+    final_tile(f, in_base, w, k, lane, c);
+    o[k][0] = pack_out<T>(c[0] * scale, c[1] * scale);
+    o[k][1] = pack_out<T>(c[2] * scale, c[3] * scale);
+    o[k][2] = pack_out<T>(c[4] * scale, c[5] * scale);
+    o[k][3] = pack_out<T>(c[6] * scale, c[7] * scale);
     sign_acc<0>(o[k], sw, w, k, g, t);
   }
-  const int64_t bbase = blk * kB;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const uint32_t sel = h ? 0x7632u : 0x5410u;
       int p = dep_a(w, 0, g + 8 * (j & 1), 2 * t + h + 8 * (j >> 1));
+      uint32_t addr = stage_base + 16u * (uint32_t)lay_nat_chunk(p >> 3);
       uint32_t v0 = prmt(o[0][j], o[1][j], sel), v1 = prmt(o[2][j], o[3][j], sel);
       uint32_t v2 = prmt(o[4][j], o[5][j], sel), v3 = prmt(o[6][j], o[7][j], sel);
-      int64_t gi = bbase + p;  // this chunk covers coordinates gi .. gi+7
-      if (vec_ok && gi >= start && gi + 8 <= stop) {
-        *reinterpret_cast<uint4*>(out + (gi - start)) = make_uint4(v0, v1, v2, v3);
-      } else {
-        uint32_t vv[4] = {v0, v1, v2, v3};
+      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};\n" ::"r"(addr), "r"(v0), "r"(v1), "r"(v2), "r"(v3));
+    }
+  }
+  __syncthreads();
+  const int64_t bbase = blk * kB;
+  const uint4* st4 = reinterpret_cast<const uint4*>(stage);
+  for (int c = threadIdx.x; c < kB / 8; c += kThreads) {
+    uint4 v = st4[lay_nat_chunk(c)];
+    int64_t gi = bbase + 8 * c;
+    if (vec_ok && gi >= start && gi + 8 <= stop) {
+      *reinterpret_cast<uint4*>(out + (gi - start)) = v;
+    } else {
+      uint32_t vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          int64_t gg = gi + e;
-          if (gg >= start && gg < stop)
-            reinterpret_cast<uint16_t*>(out)[gg - start] = (uint16_t)(vv[e >> 1] >> (16 * (e & 1)));
-        }
+      for (int e = 0; e < 8; ++e) {
+        int64_t gg = gi + e;
+        if (gg >= start && gg < stop)
+          reinterpret_cast<uint16_t*>(out)[gg - start] = (uint16_t)(vv[e >> 1] >> (16 * (e & 1)));
       }
     }
   }
@@ -350,13 +371,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (layers == 1) {
       run<1, false, true>(f, zb, xb, sw, nullptr, w, lane, g, t);
       __syncthreads();
-      run_final<T>(f, xb, sw + 1 * kWords, out_scale, out, blk, start, stop, vec_ok, w, lane, g, t);
+      run_final<T>(f, xb, yb, ybuf, sw + 1 * kWords, out_scale, out, blk, start, stop, vec_ok, w, lane, g, t);
     } else if (layers == 2) {
       run<0, false, true>(f, zb, yb, sw, nullptr, w, lane, g, t);
       __syncthreads();
       run<1, true, false>(f, yb, xb, nullptr, sw + 1 * kWords, w, lane, g, t);
       __syncthreads();
-      run_final<T>(f, xb, sw + 2 * kWords, out_scale, out, blk, start, stop, vec_ok, w, lane, g, t);
+      run_final<T>(f, xb, yb, ybuf, sw + 2 * kWords, out_scale, out, blk, start, stop, vec_ok, w, lane, g, t);
     } else {
       run<1, false, true>(f, zb, xb, sw, nullptr, w, lane, g, t);
       __syncthreads();
@@ -364,7 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncthreads();
       run<1, true, false>(f, yb, xb, nullptr, sw + 2 * kWords, w, lane, g, t);
       __syncthreads();
-      run_final<T>(f, xb, sw + 3 * kWords, out_scale, out, blk, start, stop, vec_ok, w, lane, g, t);
+      run_final<T>(f, xb, yb, ybuf, sw + 3 * kWords, out_scale, out, blk, start, stop, vec_ok, w, lane, g, t);
     }
   }
 }
@@ -391,6 +412,243 @@ int launch_forward_t(const void* latent, int64_t L, int layers, uint32_t seed32,
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
+
+// ---------------------------------------------------------------------------
+// Backward: grad_z = sum_b [S0 Ĥ S1 ... Ĥ S_layers g_b][0:L].  Same runs as the
+// forward with the sign layers reversed; the per-block result (fp32, from the
+// last column transform) is accumulated across the blocks a CTA processes in
+// tensor memory: 128 lanes x 256 columns hold the 32768 fp32 partial sums,
+// each thread owning the 64 values of its final-run fragments.  At the end
+// every CTA writes its partial [L] row; fht15_reduce_kernel sums the rows.
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const float* v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(taddr),
+               "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+               "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+               "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])));
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+
+// f32 sign flip for the accumulator element at position p (bit p&31 of its word)
+__device__ __forceinline__ float fsign(float v, const uint32_t* sw, int p) {
+  uint32_t b = (sw[p >> 5] >> (p & 31)) & 1u;
+  return __uint_as_float(__float_as_uint(v) ^ ((b ^ 1u) << 31));
+}
+
+// Final backward run (pass A): transforms, scale, sign of layer 0, add into TMEM.
+__device__ __forceinline__ void run_final_acc(const Frags& f, uint32_t in_base, const uint32_t* sw, float scale,
+                                              uint32_t tbase, int w, int lane, int g, int t) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    float c[8];
+    final_tile(f, in_base, w, k, lane, c);
+    float acc[8];
+    tmem_ld8(tbase + 8 * k, acc);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      // c[i]: column half i>>2, row g + 8*((i>>1)&1), column 2t + (i&1)
+      int R = g + 8 * ((i >> 1) & 1), C = 2 * t + (i & 1) + 8 * (i >> 2);
+      acc[i] += fsign(c[i] * scale, sw, dep_a(w, k, R, C));
+    }
+    tmem_st8(tbase + 8 * k, acc);
+  }
+  tmem_wait_st();
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    fht15_backward_kernel(const T* __restrict__ grad, int64_t L, int layers, uint32_t seed32, int64_t first_block,
+                          int64_t nblocks, int64_t start, int64_t stop, float* __restrict__ partial) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint16_t* xbuf = reinterpret_cast<uint16_t*>(smem);
+  uint16_t* ybuf = xbuf + kB;
+  uint32_t* sw = reinterpret_cast<uint32_t*>(ybuf + kB);
+  __shared__ float red[kThreads / 32];
+  __shared__ int k0_shared;
+  __shared__ uint32_t tmem_base_shared;
+
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
+  Frags f;
+  make_frags(f, g, t);
+
+  if (w == 0) {
+    uint32_t dst = (uint32_t)__cvta_generic_to_shared(&tmem_base_shared);
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;\n" ::"r"(dst));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;\n");
+  // warp w uses lanes 32*(w%4).. and columns 64*(w/4) .. +63
+  const uint32_t tbase = tmem_base_shared + ((uint32_t)(32 * (w & 3)) << 16) + (uint32_t)(64 * (w >> 2));
+  {
+    float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tmem_st8(tbase + 8 * k, z);
+    tmem_wait_st();
+  }
+
+  const float layer_scale = layers == 1 ? 0.70710678118654752f : layers == 2 ? 0.5f : 0.35355339059327376f;
+  const uint32_t xb = (uint32_t)__cvta_generic_to_shared(xbuf);
+  const uint32_t yb = (uint32_t)__cvta_generic_to_shared(ybuf);
+  // landing buffer for the gradient: read by the first run (pass B via the
+  // A->B layout for layers 1 and 3, pass A via the B->A layout for layers 2)
+  const bool first_is_b = (layers != 2);
+  uint16_t* land = first_is_b ? ybuf : xbuf;
+  const bool vec_ok = ((start & 7) == 0) && ((reinterpret_cast<uintptr_t>(grad) & 15) == 0);
+
+  for (int64_t bi = blockIdx.x; bi < nblocks; bi += gridDim.x) {
+    const int64_t blk = first_block + bi;
+    const int64_t bbase = blk * kB;
+    __syncthreads();
+    for (int i = tid; i < (layers + 1) * kWords; i += kThreads) {
+      int l = i / kWords, wd = i - l * kWords;
+      sw[i] = sign_word(block_layer_key(seed32, blk, l), wd);
+    }
+    // gradient chunks of this block into registers, with their squared norm
+    uint4 raw[8];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      int c = tid + kThreads * i;
+      int64_t gi = bbase + 8 * c;
+      if (vec_ok && gi >= start && gi + 8 <= stop) {
+        raw[i] = __ldg(reinterpret_cast<const uint4*>(grad + (gi - start)));
+      } else {
+        uint32_t vv[4] = {0, 0, 0, 0};
+        for (int e = 0; e < 8; ++e) {
+          int64_t gg = gi + e;
+          if (gg >= start && gg < stop)
+            vv[e >> 1] |= (uint32_t)reinterpret_cast<const uint16_t*>(grad)[gg - start] << (16 * (e & 1));
+        }
+        raw[i] = make_uint4(vv[0], vv[1], vv[2], vv[3]);
+      }
+      const T* ev = reinterpret_cast<const T*>(&raw[i]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float v = Cvt<T>::to_f(ev[e]);
+        ss += v * v;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[w] = ss;
+    __syncthreads();
+    if (tid == 0) {
+      float s = 0.0f;
+      for (int i = 0; i < kThreads / 32; ++i) s += red[i];
+      int e = 0;
+      if (s > 0.0f) {
+        frexpf(sqrtf(s), &e);
+        e -= 12;
+      }
+      k0_shared = e;
+    }
+    __syncthreads();
+    const int k0 = k0_shared;
+    const float in_scale = ldexpf(1.0f, -k0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      int c = tid + kThreads * i;
+      const T* ev = reinterpret_cast<const T*>(&raw[i]);
+      uint32_t hv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        hv[e] = pack_h2(Cvt<T>::to_f(ev[2 * e]) * in_scale, Cvt<T>::to_f(ev[2 * e + 1]) * in_scale);
+      if (first_is_b) {
+        *reinterpret_cast<uint4*>(land + lay_ab(8 * c)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) land[lay_ba(8 * c + e)] = (uint16_t)(hv[e >> 1] >> (16 * (e & 1)));
+      }
+    }
+    __syncthreads();
+    const float scale = ldexpf(1.0f, k0) * layer_scale;
+    if (layers == 1) {
+      run<1, false, true>(f, yb, xb, sw + 1 * kWords, nullptr, w, lane, g, t);
+      __syncthreads();
+      run_final_acc(f, xb, sw, scale, tbase, w, lane, g, t);
+    } else if (layers == 2) {
+      run<0, false, true>(f, xb, yb, sw + 2 * kWords, nullptr, w, lane, g, t);
+      __syncthreads();
+      run<1, true, false>(f, yb, xb, nullptr, sw + 1 * kWords, w, lane, g, t);
+      __syncthreads();
+      run_final_acc(f, xb, sw, scale, tbase, w, lane, g, t);
+    } else {
+      run<1, false, true>(f, yb, xb, sw + 3 * kWords, nullptr, w, lane, g, t);
+      __syncthreads();
+      run<0, true, false>(f, xb, yb, nullptr, sw + 2 * kWords, w, lane, g, t);
+      __syncthreads();
+      run<1, true, false>(f, yb, xb, nullptr, sw + 1 * kWords, w, lane, g, t);
+      __syncthreads();
+      run_final_acc(f, xb, sw, scale, tbase, w, lane, g, t);
+    }
+  }
+  // this CTA's partial gradient row
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    float acc[8];
+    tmem_ld8(tbase + 8 * k, acc);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      int R = g + 8 * ((i >> 1) & 1), C = 2 * t + (i & 1) + 8 * (i >> 2);
+      int p = dep_a(w, k, R, C);
+      if (p < L) partial[(int64_t)blockIdx.x * L + p] = acc[i];
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;\n");
+  if (w == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;\n" ::"r"(tmem_base_shared));
+}
+
+template <typename T>
+__global__ void fht15_reduce_kernel(const float* __restrict__ partial, int rows, int64_t L, T* __restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < L; i += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.0f;
+    for (int r = 0; r < rows; ++r) s += partial[(int64_t)r * L + i];
+    out[i] = Cvt<T>::from_f(s);
+  }
+}
+
+constexpr size_t kSmemBwd = 2 * kB * 2 + 4 * kWords * 4;
+
+inline int sm_count() {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+template <typename T>
+int launch_backward_t(const void* grad, int64_t L, int layers, uint32_t seed32, int64_t first_block, int64_t nblocks,
+                      int64_t start, int64_t stop, void* grad_latent, float* partial, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(fht15_backward_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSmemBwd) != cudaSuccess)
+      return -1;
+    attr = true;
+  }
+  int sms = sm_count();
+  int grid = (int)(nblocks < sms ? nblocks : sms);
+  fht15_backward_kernel<T><<<grid, kThreads, kSmemBwd, st>>>(reinterpret_cast<const T*>(grad), L, layers, seed32,
+                                                             first_block, nblocks, start, stop, partial);
+  if (cudaGetLastError() != cudaSuccess) return -1;
+  int rb = (int)((L + 255) / 256);
+  fht15_reduce_kernel<T><<<rb, 256, 0, st>>>(partial, grid, L, reinterpret_cast<T*>(grad_latent));
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
 }  // namespace fmma
 
 bool mma_forward_supported(int dtype, int64_t latent_size, unsigned flags) {
@@ -408,6 +666,38 @@ int mma_forward(int dtype, const void* latent, int64_t L, int layers, uint64_t s
   if (dtype == LWL_BF16)
     return fmma::launch_forward_t<__nv_bfloat16>(latent, L, layers, s32, first, last - first, start, stop, out, st);
   return fmma::launch_forward_t<__half>(latent, L, layers, s32, first, last - first, start, stop, out, st);
+}
+
+}  // namespace lwl
+
+namespace lwl {
+
+bool mma_backward_supported(int dtype, int64_t latent_size, unsigned flags) {
+  return mma_forward_supported(dtype, latent_size, flags);
+}
+
+size_t mma_backward_workspace_bytes(int64_t latent_size, int64_t start, int64_t stop) {
+  const int64_t B = fmma::kB;
+  int64_t nblk = (stop + B - 1) / B - start / B;
+  if (nblk <= 0) return 0;
+  int64_t grid = nblk < fmma::sm_count() ? nblk : fmma::sm_count();
+  return size_t(grid) * size_t(latent_size) * 4;
+}
+
+int mma_backward(int dtype, const void* grad, int64_t L, int layers, uint64_t seed, int64_t start, int64_t stop,
+                 void* grad_latent, void* workspace, cudaStream_t st) {
+  const int64_t B = fmma::kB;
+  int64_t first = start / B, last = (stop + B - 1) / B;
+  if (last <= first) {
+    return cudaMemsetAsync(grad_latent, 0, size_t(L) * 2, st) == cudaSuccess ? 0 : -1;
+  }
+  uint32_t s32 = fold_seed(seed);
+  float* partial = reinterpret_cast<float*>(workspace);
+  if (dtype == LWL_BF16)
+    return fmma::launch_backward_t<__nv_bfloat16>(grad, L, layers, s32, first, last - first, start, stop, grad_latent,
+                                                  partial, st);
+  return fmma::launch_backward_t<__half>(grad, L, layers, s32, first, last - first, start, stop, grad_latent, partial,
+                                         st);
 }
 
 }  // namespace lwl

@@ -11,4 +11,11 @@ bool mma_forward_supported(int dtype, int64_t latent_size, unsigned flags);
 int mma_forward(int dtype, const void* latent, int64_t latent_size, int layers, uint64_t seed, int64_t start,
                 int64_t stop, void* out, cudaStream_t st);
 
+// Tensor-core backward for padded block size 2^15 (fp32 partials in TMEM,
+// one [L] row per CTA in the workspace, then a row reduction).
+bool mma_backward_supported(int dtype, int64_t latent_size, unsigned flags);
+size_t mma_backward_workspace_bytes(int64_t latent_size, int64_t start, int64_t stop);
+int mma_backward(int dtype, const void* grad, int64_t latent_size, int layers, uint64_t seed, int64_t start,
+                 int64_t stop, void* grad_latent, void* workspace, cudaStream_t st);
+
 }  // namespace lwl

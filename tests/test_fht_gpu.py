@@ -63,6 +63,9 @@ CASES = [
     (4096, 8192, 1, 123, 17, 4099),
     (20000, 65536, 1, 123, 111, 4096),
     (32768, 3 * 32768 + 5, 3, 123, 0, 3 * 32768 + 5),
+    (32768, 2 * 32768, 1, 5, 3, 2 * 32768 - 1),
+    (20000, 3 * 32768, 2, 6, 1000, 3 * 32768),
+    (32768, 300 * 32768, 3, 77, 8, 300 * 32768 - 8),
     (30000, 200000, 2, 9, 12345, 190000),
     (65536, 3 * 65536, 3, 7, 100, 3 * 65536 - 3),
     ((1 << 20) - 3, 1 << 21, 1, 11, 1000, (1 << 21) - 7),

@@ -35,6 +35,11 @@ constexpr int kLog = 15;
 constexpr int kB = 1 << kLog;
 constexpr int kThreads = 512;
 constexpr int kWords = kB / 32;
+// Sign words of one layer live at stride kWordsPad, word w at w + (w >> 7):
+// the padding spreads the words that the lanes of pass B read (128 apart)
+// over different banks.
+constexpr int kWordsPad = kWords + kWords / 128 + 8;
+__device__ __forceinline__ int spad(int w) { return w + (w >> 7); }
 
 // position of element (warp w, tile k, tile row R, tile col C) in each pass
 __device__ __forceinline__ int dep_a(int w, int k, int R, int C) {
@@ -164,29 +169,54 @@ __device__ __forceinline__ void to_bop(const uint32_t* a, uint32_t* x) {
 
 // XOR the signs of one layer into accumulator-layout registers of tile k.
 // Register j holds (R = g + 8(j&1), C = 2t + 8(j>>1) + {0,1}); the pair sits
-// at positions p and p+16 (C bit 0 is position bit 4).
+// at positions p and p+16 (C bit 0 is position bit 4), so one shifted copy of
+// the inverted sign word gives both sign bits (bit 15 and bit 31).
+//   pass A: p = base + k + 8(j&1) + 2048(j>>1), base bits 0-4 clear
+//   pass B: p = base + 32k + 256(j&1) + 16384(j>>1), p & 15 = base & 15
 template <int PASS>
 __device__ __forceinline__ void sign_acc(uint32_t* a, const uint32_t* sw, int w, int k, int g, int t) {
+  const int base = Pass<PASS>::dep(w, 0, g, 2 * t);
+  const int wb = base >> 5;
+  if (PASS == 0) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    int p = Pass<PASS>::dep(w, k, g + 8 * (j & 1), 2 * t + 8 * (j >> 1));
-    uint32_t u = ~sw[p >> 5];
-    a[j] ^= (u << (15 - (p & 15))) & 0x80008000u;
+    for (int j = 0; j < 4; ++j) {
+      uint32_t u = ~sw[spad(wb + 64 * (j >> 1))];
+      a[j] ^= (u << (15 - k - 8 * (j & 1))) & 0x80008000u;
+    }
+  } else {
+    const int sh = 15 - (base & 15);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t u = ~sw[spad(wb + k + 8 * (j & 1) + 512 * (j >> 1))];
+      a[j] ^= (u << sh) & 0x80008000u;
+    }
   }
 }
 
 // Signs applied to B-operand fragments (first run): register m holds
-// (R = 2t + 8(m&1) + {0,1}, C = g + 8(m>>1)).
+// (R = 2t + 8(m&1) + {0,1}, C = g + 8(m>>1)).  In pass B the pair is two
+// neighbouring positions (p, p+1) of one word; the multiply moves bit 0 to
+// bit 15 and bit 1 to bit 31 (no carries: the two partial products do not overlap).
 template <int PASS>
 __device__ __forceinline__ void sign_bop(uint32_t* x, const uint32_t* sw, int w, int k, int g, int t) {
+  if (PASS == 1) {
+    const int base = dep_b(w, 0, 2 * t, g);
+    const int wb = base >> 5, q = base & 31;
 #pragma unroll
-  for (int m = 0; m < 4; ++m) {
-    int R = 2 * t + 8 * (m & 1), C = g + 8 * (m >> 1);
-    int p0 = Pass<PASS>::dep(w, k, R, C);
-    int p1 = Pass<PASS>::dep(w, k, R + 1, C);
-    uint32_t b0 = (sw[p0 >> 5] >> (p0 & 31)) & 1u;
-    uint32_t b1 = (sw[p1 >> 5] >> (p1 & 31)) & 1u;
-    x[m] ^= ((b0 ^ 1u) << 15) | ((b1 ^ 1u) << 31);
+    for (int m = 0; m < 4; ++m) {
+      uint32_t u = ~sw[spad(wb + k + 8 * (m & 1) + 512 * (m >> 1))];
+      x[m] ^= (((u >> q) & 3u) * 0x40008000u) & 0x80008000u;
+    }
+  } else {
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      int R = 2 * t + 8 * (m & 1), C = g + 8 * (m >> 1);
+      int p0 = dep_a(w, k, R, C);
+      int p1 = dep_a(w, k, R + 1, C);
+      uint32_t b0 = (sw[spad(p0 >> 5)] >> (p0 & 31)) & 1u;
+      uint32_t b1 = (sw[spad(p1 >> 5)] >> (p1 & 31)) & 1u;
+      x[m] ^= ((b0 ^ 1u) << 15) | ((b1 ^ 1u) << 31);
+    }
   }
 }
 
@@ -365,32 +395,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();  // the previous block is done with the sign table and buffers
     for (int i = tid; i < (layers + 1) * kWords; i += kThreads) {
       int l = i / kWords, wd = i - l * kWords;
-      sw[i] = sign_word(block_layer_key(seed32, blk, l), wd);
+      sw[l * kWordsPad + spad(wd)] = sign_word(block_layer_key(seed32, blk, l), wd);
     }
     __syncthreads();
     if (layers == 1) {
       run<1, false, true>(f, zb, xb, sw, nullptr, w, lane, g, t);
       __syncthreads();
-      run_final<T>(f, xb, yb, ybuf, sw + 1 * kWords, out_scale, out, blk, start, stop, vec_ok, w, lane, g, t);
+      run_final<T>(f, xb, yb, ybuf, sw + 1 * kWordsPad, out_scale, out, blk, start, stop, vec_ok, w, lane, g, t);
     } else if (layers == 2) {
       run<0, false, true>(f, zb, yb, sw, nullptr, w, lane, g, t);
       __syncthreads();
-      run<1, true, false>(f, yb, xb, nullptr, sw + 1 * kWords, w, lane, g, t);
+      run<1, true, false>(f, yb, xb, nullptr, sw + 1 * kWordsPad, w, lane, g, t);
       __syncthreads();
-      run_final<T>(f, xb, yb, ybuf, sw + 2 * kWords, out_scale, out, blk, start, stop, vec_ok, w, lane, g, t);
+      run_final<T>(f, xb, yb, ybuf, sw + 2 * kWordsPad, out_scale, out, blk, start, stop, vec_ok, w, lane, g, t);
     } else {
       run<1, false, true>(f, zb, xb, sw, nullptr, w, lane, g, t);
       __syncthreads();
-      run<0, true, false>(f, xb, yb, nullptr, sw + 1 * kWords, w, lane, g, t);
+      run<0, true, false>(f, xb, yb, nullptr, sw + 1 * kWordsPad, w, lane, g, t);
       __syncthreads();
-      run<1, true, false>(f, yb, xb, nullptr, sw + 2 * kWords, w, lane, g, t);
+      run<1, true, false>(f, yb, xb, nullptr, sw + 2 * kWordsPad, w, lane, g, t);
       __syncthreads();
-      run_final<T>(f, xb, yb, ybuf, sw + 3 * kWords, out_scale, out, blk, start, stop, vec_ok, w, lane, g, t);
+      run_final<T>(f, xb, yb, ybuf, sw + 3 * kWordsPad, out_scale, out, blk, start, stop, vec_ok, w, lane, g, t);
     }
   }
 }
 
-constexpr size_t kSmem = 3 * kB * 2 + 4 * kWords * 4;
+constexpr size_t kSmem = 3 * kB * 2 + 4 * kWordsPad * 4;
 
 template <typename T>
 int launch_forward_t(const void* latent, int64_t L, int layers, uint32_t seed32, int64_t first_block,
@@ -438,11 +468,6 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const float* v) {
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 
-// f32 sign flip for the accumulator element at position p (bit p&31 of its word)
-__device__ __forceinline__ float fsign(float v, const uint32_t* sw, int p) {
-  uint32_t b = (sw[p >> 5] >> (p & 31)) & 1u;
-  return __uint_as_float(__float_as_uint(v) ^ ((b ^ 1u) << 31));
-}
 
 // Final backward run (pass A): transforms, scale, sign of layer 0, add into TMEM.
 __device__ __forceinline__ void run_final_acc(const Frags& f, uint32_t in_base, const uint32_t* sw, float scale,
@@ -453,11 +478,15 @@ __device__ __forceinline__ void run_final_acc(const Frags& f, uint32_t in_base, 
     final_tile(f, in_base, w, k, lane, c);
     float acc[8];
     tmem_ld8(tbase + 8 * k, acc);
+    // c[i]: row g + 8((i>>1)&1), column 2t + (i&1) + 8(i>>2) of pass A, i.e.
+    // position base + k + 8((i>>1)&1) + 16(i&1) + 2048(i>>2)
+    const int wb = dep_a(w, 0, g, 2 * t) >> 5;
+    const uint32_t u0 = ~sw[spad(wb)], u1 = ~sw[spad(wb + 64)];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      // c[i]: column half i>>2, row g + 8*((i>>1)&1), column 2t + (i&1)
-      int R = g + 8 * ((i >> 1) & 1), C = 2 * t + (i & 1) + 8 * (i >> 2);
-      acc[i] += fsign(c[i] * scale, sw, dep_a(w, k, R, C));
+      const int bit = k + 8 * ((i >> 1) & 1) + 16 * (i & 1);
+      const uint32_t u = (i >> 2) ? u1 : u0;
+      acc[i] += __uint_as_float(__float_as_uint(c[i] * scale) ^ ((u << (31 - bit)) & 0x80000000u));
     }
     tmem_st8(tbase + 8 * k, acc);
   }
@@ -467,12 +496,17 @@ __device__ __forceinline__ void run_final_acc(const Frags& f, uint32_t in_base, 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     fht15_backward_kernel(const T* __restrict__ grad, int64_t L, int layers, uint32_t seed32, int64_t first_block,
-                          int64_t nblocks, int64_t start, int64_t stop, float* __restrict__ partial) {
+                          int64_t nblocks, int64_t start, int64_t stop, float* __restrict__ partial,
+                          int* __restrict__ err) {
   extern __shared__ __align__(128) unsigned char smem[];
   uint16_t* xbuf = reinterpret_cast<uint16_t*>(smem);
   uint16_t* ybuf = xbuf + kB;
-  uint32_t* sw = reinterpret_cast<uint32_t*>(ybuf + kB);
+  uint16_t* stage = ybuf + kB;  // raw gradient of the next block (bulk copy target)
+  uint32_t* sw = reinterpret_cast<uint32_t*>(stage + kB);
   __shared__ float red[kThreads / 32];
+  __shared__ __align__(8) uint64_t mbar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) abort_flag = 0;
   __shared__ int k0_shared;
   __shared__ uint32_t tmem_base_shared;
 
@@ -500,11 +534,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   const float layer_scale = layers == 1 ? 0.70710678118654752f : layers == 2 ? 0.5f : 0.35355339059327376f;
   const uint32_t xb = (uint32_t)__cvta_generic_to_shared(xbuf);
   const uint32_t yb = (uint32_t)__cvta_generic_to_shared(ybuf);
+  const uint32_t stage_s = (uint32_t)__cvta_generic_to_shared(stage);
+  const uint32_t mbar_s = (uint32_t)__cvta_generic_to_shared(&mbar);
   // landing buffer for the gradient: read by the first run (pass B via the
   // A->B layout for layers 1 and 3, pass A via the B->A layout for layers 2)
   const bool first_is_b = (layers != 2);
   uint16_t* land = first_is_b ? ybuf : xbuf;
   const bool vec_ok = ((start & 7) == 0) && ((reinterpret_cast<uintptr_t>(grad) & 15) == 0);
+  // whole blocks inside the slice arrive by one 64 KB bulk copy into `stage`,
+  // issued one block ahead; edge blocks are read with bounds checks instead
+  auto bulk_ok = [&](int64_t blk) { return vec_ok && blk * kB >= start && (blk + 1) * kB <= stop; };
+  auto issue = [&](int64_t blk) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(mbar_s), "r"((uint32_t)(kB * 2)));
+    const T* src = grad + (blk * kB - start);
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(stage_s),
+        "l"(src), "r"((uint32_t)(kB * 2)), "r"(mbar_s)
+        : "memory");
+  };
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(mbar_s));
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncthreads();
+  uint32_t phase = 0;
+  if (tid == 0 && blockIdx.x < nblocks && bulk_ok(first_block + blockIdx.x)) issue(first_block + blockIdx.x);
 
   for (int64_t bi = blockIdx.x; bi < nblocks; bi += gridDim.x) {
     const int64_t blk = first_block + bi;
@@ -512,17 +566,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     for (int i = tid; i < (layers + 1) * kWords; i += kThreads) {
       int l = i / kWords, wd = i - l * kWords;
-      sw[i] = sign_word(block_layer_key(seed32, blk, l), wd);
+      sw[l * kWordsPad + spad(wd)] = sign_word(block_layer_key(seed32, blk, l), wd);
     }
     // gradient chunks of this block into registers, with their squared norm
     uint4 raw[8];
     float ss = 0.0f;
+    const bool bulk = bulk_ok(blk);
+    if (bulk) {
+      // bounded wait for the bulk copy; on time-out record the failure and stop
+      uint32_t done = 0;
+      for (int it = 0; it < (1 << 22) && !done; ++it) {
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(mbar_s), "r"(phase)
+            : "memory");
+      }
+      if (!done) {
+        abort_flag = 1;
+        atomicExch(err, 1);
+      }
+      phase ^= 1u;
+    }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       int c = tid + kThreads * i;
       int64_t gi = bbase + 8 * c;
-      if (vec_ok && gi >= start && gi + 8 <= stop) {
-        raw[i] = __ldg(reinterpret_cast<const uint4*>(grad + (gi - start)));
+      if (bulk) {
+        raw[i] = reinterpret_cast<const uint4*>(stage)[c];
       } else {
         uint32_t vv[4] = {0, 0, 0, 0};
         for (int e = 0; e < 8; ++e) {
@@ -543,7 +614,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     if (lane == 0) red[w] = ss;
     __syncthreads();
+    if (abort_flag) break;  // uniform: set before the barrier above
+    // the stage buffer is free again: fetch the next block while this one runs
     if (tid == 0) {
+      int64_t nb = bi + gridDim.x;
+      if (nb < nblocks && bulk_ok(first_block + nb)) {
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        issue(first_block + nb);
+      }
       float s = 0.0f;
       for (int i = 0; i < kThreads / 32; ++i) s += red[i];
       int e = 0;
@@ -574,23 +652,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     const float scale = ldexpf(1.0f, k0) * layer_scale;
     if (layers == 1) {
-      run<1, false, true>(f, yb, xb, sw + 1 * kWords, nullptr, w, lane, g, t);
+      run<1, false, true>(f, yb, xb, sw + 1 * kWordsPad, nullptr, w, lane, g, t);
       __syncthreads();
       run_final_acc(f, xb, sw, scale, tbase, w, lane, g, t);
     } else if (layers == 2) {
-      run<0, false, true>(f, xb, yb, sw + 2 * kWords, nullptr, w, lane, g, t);
+      run<0, false, true>(f, xb, yb, sw + 2 * kWordsPad, nullptr, w, lane, g, t);
       __syncthreads();
-      run<1, true, false>(f, yb, xb, nullptr, sw + 1 * kWords, w, lane, g, t);
+      run<1, true, false>(f, yb, xb, nullptr, sw + 1 * kWordsPad, w, lane, g, t);
       __syncthreads();
       run_final_acc(f, xb, sw, scale, tbase, w, lane, g, t);
     } else {
-      run<1, false, true>(f, yb, xb, sw + 3 * kWords, nullptr, w, lane, g, t);
+      run<1, false, true>(f, yb, xb, sw + 3 * kWordsPad, nullptr, w, lane, g, t);
       __syncthreads();
-      run<0, true, false>(f, xb, yb, nullptr, sw + 2 * kWords, w, lane, g, t);
+      run<0, true, false>(f, xb, yb, nullptr, sw + 2 * kWordsPad, w, lane, g, t);
       __syncthreads();
-      run<1, true, false>(f, yb, xb, nullptr, sw + 1 * kWords, w, lane, g, t);
+      run<1, true, false>(f, yb, xb, nullptr, sw + 1 * kWordsPad, w, lane, g, t);
       __syncthreads();
       run_final_acc(f, xb, sw, scale, tbase, w, lane, g, t);
+    }
+  }
+  if (abort_flag && tid == 0) {
+    // let an outstanding copy land before the CTA exits (bounded)
+    uint32_t done = 0;
+    for (int it = 0; it < (1 << 22) && !done; ++it) {
+      asm volatile(
+          "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+          : "=r"(done)
+          : "r"(mbar_s), "r"(phase ^ 1u)
+          : "memory");
     }
   }
   // this CTA's partial gradient row
@@ -611,16 +700,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (w == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;\n" ::"r"(tmem_base_shared));
 }
 
+// Sum of the per-CTA rows; a failed bulk-copy wait (err != 0) poisons the
+// gradient with NaN so the failure cannot pass silently.
 template <typename T>
-__global__ void fht15_reduce_kernel(const float* __restrict__ partial, int rows, int64_t L, T* __restrict__ out) {
+__global__ void fht15_reduce_kernel(const float* __restrict__ partial, int rows, int64_t L, const int* __restrict__ err,
+                                    T* __restrict__ out) {
+  const bool bad = *err != 0;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < L; i += (int64_t)gridDim.x * blockDim.x) {
     float s = 0.0f;
     for (int r = 0; r < rows; ++r) s += partial[(int64_t)r * L + i];
-    out[i] = Cvt<T>::from_f(s);
+    out[i] = Cvt<T>::from_f(bad ? __int_as_float(0x7fc00000) : s);
   }
 }
 
-constexpr size_t kSmemBwd = 2 * kB * 2 + 4 * kWords * 4;
+constexpr size_t kSmemBwd = 3 * kB * 2 + 4 * kWordsPad * 4;
+constexpr size_t kBwdHeader = 256;  // workspace: [error word | pad] then the partial rows
 
 inline int sm_count() {
   int dev = 0, sms = 148;
@@ -631,7 +725,10 @@ inline int sm_count() {
 
 template <typename T>
 int launch_backward_t(const void* grad, int64_t L, int layers, uint32_t seed32, int64_t first_block, int64_t nblocks,
-                      int64_t start, int64_t stop, void* grad_latent, float* partial, cudaStream_t st) {
+                      int64_t start, int64_t stop, void* grad_latent, void* workspace, cudaStream_t st) {
+  int* err = reinterpret_cast<int*>(workspace);
+  float* partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kBwdHeader);
+  if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess) return -1;
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(fht15_backward_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -642,10 +739,10 @@ int launch_backward_t(const void* grad, int64_t L, int layers, uint32_t seed32, 
   int sms = sm_count();
   int grid = (int)(nblocks < sms ? nblocks : sms);
   fht15_backward_kernel<T><<<grid, kThreads, kSmemBwd, st>>>(reinterpret_cast<const T*>(grad), L, layers, seed32,
-                                                             first_block, nblocks, start, stop, partial);
+                                                             first_block, nblocks, start, stop, partial, err);
   if (cudaGetLastError() != cudaSuccess) return -1;
   int rb = (int)((L + 255) / 256);
-  fht15_reduce_kernel<T><<<rb, 256, 0, st>>>(partial, grid, L, reinterpret_cast<T*>(grad_latent));
+  fht15_reduce_kernel<T><<<rb, 256, 0, st>>>(partial, grid, L, err, reinterpret_cast<T*>(grad_latent));
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -681,7 +778,7 @@ size_t mma_backward_workspace_bytes(int64_t latent_size, int64_t start, int64_t 
   int64_t nblk = (stop + B - 1) / B - start / B;
   if (nblk <= 0) return 0;
   int64_t grid = nblk < fmma::sm_count() ? nblk : fmma::sm_count();
-  return size_t(grid) * size_t(latent_size) * 4;
+  return fmma::kBwdHeader + size_t(grid) * size_t(latent_size) * 4;
 }
 
 int mma_backward(int dtype, const void* grad, int64_t L, int layers, uint64_t seed, int64_t start, int64_t stop,
@@ -692,12 +789,11 @@ int mma_backward(int dtype, const void* grad, int64_t L, int layers, uint64_t se
     return cudaMemsetAsync(grad_latent, 0, size_t(L) * 2, st) == cudaSuccess ? 0 : -1;
   }
   uint32_t s32 = fold_seed(seed);
-  float* partial = reinterpret_cast<float*>(workspace);
   if (dtype == LWL_BF16)
     return fmma::launch_backward_t<__nv_bfloat16>(grad, L, layers, s32, first, last - first, start, stop, grad_latent,
-                                                  partial, st);
-  return fmma::launch_backward_t<__half>(grad, L, layers, s32, first, last - first, start, stop, grad_latent, partial,
-                                         st);
+                                                  workspace, st);
+  return fmma::launch_backward_t<__half>(grad, L, layers, s32, first, last - first, start, stop, grad_latent,
+                                         workspace, st);
 }
 
 }  // namespace lwl

@@ -378,10 +378,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   const float in_scale = ldexpf(1.0f, -k0);
   // the first run is pass B for layers 1 and 3, pass A for layers 2
   const bool first_is_b = (layers != 2);
-  for (int p = tid; p < kB; p += kThreads) {
-    float v = p < L ? Cvt<T>::to_f(latent[p]) * in_scale : 0.0f;
-    __half h = __float2half_rn(v);
-    zbuf[first_is_b ? lay_ab(p) : lay_ba(p)] = *reinterpret_cast<uint16_t*>(&h);
+  for (int c = tid; c < kB / 8; c += kThreads) {  // 8 consecutive positions per step
+    float v[8];
+    const int p0 = 8 * c;
+    if (p0 + 8 <= L && (reinterpret_cast<uintptr_t>(latent) & 15) == 0) {
+      uint4 raw = __ldg(reinterpret_cast<const uint4*>(latent + p0));
+      const T* ev = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = Cvt<T>::to_f(ev[e]) * in_scale;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = (p0 + e < L) ? Cvt<T>::to_f(latent[p0 + e]) * in_scale : 0.0f;
+    }
+    uint32_t hv[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) hv[e] = pack_h2(v[2 * e], v[2 * e + 1]);
+    if (first_is_b) {
+      *reinterpret_cast<uint4*>(zbuf + lay_ab(p0)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) zbuf[lay_ba(p0 + e)] = (uint16_t)(hv[e >> 1] >> (16 * (e & 1)));
+    }
   }
   // per layer the factors are orthonormal up to sqrt(2) (the H8/2 factor)
   const float out_scale = ldexpf(1.0f, k0) * (layers == 1   ? 0.70710678118654752f
@@ -684,7 +701,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           : "memory");
     }
   }
-  // this CTA's partial gradient row
+  // this CTA's partial gradient row, staged in natural order through the two
+  // exchange buffers (128 KB = 32768 fp32) for coalesced stores
+  __syncthreads();
+  float* prow = reinterpret_cast<float*>(smem);
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     float acc[8];
@@ -692,10 +712,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       int R = g + 8 * ((i >> 1) & 1), C = 2 * t + (i & 1) + 8 * (i >> 2);
-      int p = dep_a(w, k, R, C);
-      if (p < L) partial[(int64_t)blockIdx.x * L + p] = acc[i];
+      prow[dep_a(w, k, R, C)] = acc[i];
     }
   }
+  __syncthreads();
+  for (int64_t p = tid; p < L; p += kThreads) partial[(int64_t)blockIdx.x * L + p] = prow[p];
   asm volatile("tcgen05.fence::before_thread_sync;\n");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;\n");
@@ -709,8 +730,14 @@ __global__ void fht15_reduce_kernel(const float* __restrict__ partial, int rows,
                                     T* __restrict__ out) {
   const bool bad = *err != 0;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < L; i += (int64_t)gridDim.x * blockDim.x) {
-    float s = 0.0f;
-    for (int r = 0; r < rows; ++r) s += partial[(int64_t)r * L + i];
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // eight loads in flight, fixed summation order
+    int r = 0;
+    for (; r + 8 <= rows; r += 8) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc[u] += partial[(int64_t)(r + u) * L + i];
+    }
+    for (; r < rows; ++r) acc[0] += partial[(int64_t)r * L + i];
+    float s = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
     out[i] = Cvt<T>::from_f(bad ? __int_as_float(0x7fc00000) : s);
   }
 }

@@ -157,7 +157,8 @@ class _BlockFHTLinearFn(torch.autograd.Function):
                 modulation_alpha):
         with torch.no_grad():
             w = _native.fht_forward(latent.detach(), size, layers, seed, 0, size, flags=_flags())
-            w = w * float(weight_scale)
+            if float(weight_scale) != 1.0:
+                w = w * float(weight_scale)
             if float(modulation_alpha) != 0.0:
                 w = w + float(modulation_alpha) * latent.detach().square().sum()
             weight = w.view(int(out_features), int(in_features)).to(dtype=input.dtype)
@@ -179,7 +180,8 @@ class _BlockFHTLinearFn(torch.autograd.Function):
         x2 = input.reshape(-1, in_features)
         if ctx.needs_input_grad[0]:
             w = _native.fht_forward(latent.detach(), size, layers, seed, 0, size, flags=ctx.flags)
-            w = w * ctx.weight_scale
+            if ctx.weight_scale != 1.0:
+                w = w * ctx.weight_scale
             if ctx.modulation_alpha != 0.0:
                 w = w + ctx.modulation_alpha * latent.detach().square().sum()
             grad_input = g2.matmul(w.view(out_features, in_features).to(dtype=grad_output.dtype)).reshape_as(input)
@@ -187,7 +189,8 @@ class _BlockFHTLinearFn(torch.autograd.Function):
             grad_weight = g2.transpose(0, 1).to(dtype=latent.dtype).matmul(x2.to(dtype=latent.dtype))
             grad_latent = _native.fht_backward(grad_weight.reshape(-1), latent.numel(), size, layers, seed, 0, size,
                                                flags=ctx.flags)
-            grad_latent = grad_latent * ctx.weight_scale
+            if ctx.weight_scale != 1.0:
+                grad_latent = grad_latent * ctx.weight_scale
             if ctx.modulation_alpha != 0.0:
                 grad_latent = grad_latent + 2.0 * ctx.modulation_alpha * latent * grad_weight.sum()
         if ctx.has_bias and ctx.needs_input_grad[2]:

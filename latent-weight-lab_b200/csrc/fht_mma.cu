@@ -23,6 +23,7 @@
 // subnormals.  The last column transform accumulates in fp32, is rescaled
 // and rounded once to the output dtype.  Signs are XORed into packed pairs:
 // positions p and p+16 share a register, so one shift + LOP3 flips both.
+#include <cmath>
 #include <cstdio>
 
 #include "fht_mma.h"
@@ -120,39 +121,78 @@ template <> __device__ __forceinline__ uint32_t pack_out<__nv_bfloat16>(float lo
 }
 template <> __device__ __forceinline__ uint32_t pack_out<__half>(float lo, float hi) { return pack_h2(lo, hi); }
 
+// Tile axes and the position bits they carry (bit 0 first):
+//   pass A rows {5,6,7,3}, pass A cols {4,9,10,11},
+//   pass B rows {0,1,2,8}, pass B cols {4,12,13,14} (col bit 0 = position 4 is
+//   an identity in pass B: pass A transforms it).
+// For block size 2^n a 2^15 tile holds 2^(15-n) consecutive blocks and the
+// position bits >= n select the block, so their factor is the identity.  An
+// axis with m transformed bits applies (tensor product of H2 / I2) scaled by
+// 2^-floor(m/2), which is exact in fp16 and grows norms by at most sqrt(2).
+__host__ __device__ inline int axis_mask(int axis, int n) {
+  const int pos[4][4] = {{5, 6, 7, 3}, {4, 9, 10, 11}, {0, 1, 2, 8}, {4, 12, 13, 14}};
+  int m = 0;
+  for (int b = 0; b < 4; ++b)
+    if (pos[axis][b] < n && !(axis == 3 && b == 0)) m |= 1 << b;
+  return m;
+}
+__host__ __device__ inline int popc4(int m) { return (m & 1) + ((m >> 1) & 1) + ((m >> 2) & 1) + ((m >> 3) & 1); }
+__device__ __forceinline__ float axis_val(int i, int j, int mask) {
+  float v = ldexpf(1.0f, -(popc4(mask) >> 1));
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    int ib = (i >> b) & 1, jb = (j >> b) & 1;
+    if ((mask >> b) & 1) {
+      if (ib & jb) v = -v;
+    } else if (ib != jb) {
+      v = 0.0f;
+    }
+  }
+  return v;
+}
+
 struct Frags {
-  uint32_t hA[4];      // H16/4 as the A operand (row transform H*X)
-  uint32_t h16[2][2];  // H16/4 as the B operand, per 8-column half (column transform X*H)
-  uint32_t h8[2][2];   // (H8 (x) I2)/2 as the B operand
+  uint32_t hA[2][4];    // per pass: row-axis matrix as the A operand (row transform H*X)
+  uint32_t hc[2][2][2]; // per pass: column-axis matrix as the B operand, per 8-column half
 };
 
-__device__ __forceinline__ void make_frags(Frags& f, int g, int t) {
-  const float q = 0.25f;
-  f.hA[0] = pack_h2(q * hsign(g, 2 * t), q * hsign(g, 2 * t + 1));
-  f.hA[1] = pack_h2(q * hsign(g + 8, 2 * t), q * hsign(g + 8, 2 * t + 1));
-  f.hA[2] = pack_h2(q * hsign(g, 2 * t + 8), q * hsign(g, 2 * t + 9));
-  f.hA[3] = pack_h2(q * hsign(g + 8, 2 * t + 8), q * hsign(g + 8, 2 * t + 9));
+__device__ __forceinline__ void make_frags(Frags& f, int g, int t, int n) {
 #pragma unroll
-  for (int nh = 0; nh < 2; ++nh) {
-    int n = g + 8 * nh;
-    f.h16[nh][0] = pack_h2(q * hsign(2 * t, n), q * hsign(2 * t + 1, n));
-    f.h16[nh][1] = pack_h2(q * hsign(2 * t + 8, n), q * hsign(2 * t + 9, n));
-    auto h8 = [&](int c, int cp) -> float { return ((c & 1) == (cp & 1)) ? 0.5f * hsign(c >> 1, cp >> 1) : 0.0f; };
-    f.h8[nh][0] = pack_h2(h8(2 * t, n), h8(2 * t + 1, n));
-    f.h8[nh][1] = pack_h2(h8(2 * t + 8, n), h8(2 * t + 9, n));
+  for (int ps = 0; ps < 2; ++ps) {
+    const int rm = axis_mask(ps == 0 ? 0 : 2, n), cm = axis_mask(ps == 0 ? 1 : 3, n);
+    f.hA[ps][0] = pack_h2(axis_val(g, 2 * t, rm), axis_val(g, 2 * t + 1, rm));
+    f.hA[ps][1] = pack_h2(axis_val(g + 8, 2 * t, rm), axis_val(g + 8, 2 * t + 1, rm));
+    f.hA[ps][2] = pack_h2(axis_val(g, 2 * t + 8, rm), axis_val(g, 2 * t + 9, rm));
+    f.hA[ps][3] = pack_h2(axis_val(g + 8, 2 * t + 8, rm), axis_val(g + 8, 2 * t + 9, rm));
+#pragma unroll
+    for (int nh = 0; nh < 2; ++nh) {
+      int c = g + 8 * nh;
+      f.hc[ps][nh][0] = pack_h2(axis_val(2 * t, c, cm), axis_val(2 * t + 1, c, cm));
+      f.hc[ps][nh][1] = pack_h2(axis_val(2 * t + 8, c, cm), axis_val(2 * t + 9, c, cm));
+    }
   }
+}
+
+// Product over the 2^n transform of the exact power-of-two axis scales,
+// relative to the required 2^(-n/2) per layer.
+inline double layer_correction(int n) {
+  int applied = 0;
+  for (int a = 0; a < 4; ++a) applied += popc4(axis_mask(a, n)) >> 1;
+  return std::pow(2.0, applied - 0.5 * n);
 }
 
 // Row transform (H*X): X as B-operand fragments {x0,x1} (cols 0-7), {x2,x3}
 // (cols 8-15); result in accumulator (= A operand) layout.
+template <int PASS>
 __device__ __forceinline__ void row_tf(const Frags& f, const uint32_t* x, uint32_t* a) {
-  mma16(a[0], a[1], f.hA[0], f.hA[1], f.hA[2], f.hA[3], x[0], x[1]);
-  mma16(a[2], a[3], f.hA[0], f.hA[1], f.hA[2], f.hA[3], x[2], x[3]);
+  const uint32_t* h = f.hA[PASS];
+  mma16(a[0], a[1], h[0], h[1], h[2], h[3], x[0], x[1]);
+  mma16(a[2], a[3], h[0], h[1], h[2], h[3], x[2], x[3]);
 }
 // Column transform (X*Hc): A layout -> A layout.
 template <int PASS>
 __device__ __forceinline__ void col_tf(const Frags& f, uint32_t* a) {
-  const uint32_t(*h)[2] = PASS == 0 ? f.h16 : f.h8;
+  const uint32_t(*h)[2] = f.hc[PASS];
   uint32_t d0, d1, d2, d3;
   mma16(d0, d1, a[0], a[1], a[2], a[3], h[0][0], h[0][1]);
   mma16(d2, d3, a[0], a[1], a[2], a[3], h[1][0], h[1][1]);
@@ -257,14 +297,14 @@ __device__ __forceinline__ void run(const Frags& f, uint32_t in_base, uint32_t o
     uint32_t x[4];
     load_tile<PASS>(in_base, w, k, lane, x);
     if (PRESIGN) sign_bop<PASS>(x, pre_sw, w, k, g, t);
-    row_tf(f, x, d[k]);
+    row_tf<PASS>(f, x, d[k]);
     col_tf<PASS>(f, d[k]);
     if (DOUBLE) {
       sign_acc<PASS>(d[k], mid_sw, w, k, g, t);
       col_tf<PASS>(f, d[k]);
       uint32_t y[4];
       to_bop(d[k], y);
-      row_tf(f, y, d[k]);
+      row_tf<PASS>(f, y, d[k]);
     }
   }
   write_exchange<PASS>(d, out_base, w, g, t);
@@ -281,9 +321,9 @@ __device__ __forceinline__ int lay_nat_chunk(int c) { return c ^ ((c >> 6) & 3);
 __device__ __forceinline__ void final_tile(const Frags& f, uint32_t in_base, int w, int k, int lane, float* c) {
   uint32_t x[4], a[4];
   load_tile<0>(in_base, w, k, lane, x);
-  row_tf(f, x, a);
-  mma32(c, a[0], a[1], a[2], a[3], f.h16[0][0], f.h16[0][1]);
-  mma32(c + 4, a[0], a[1], a[2], a[3], f.h16[1][0], f.h16[1][1]);
+  row_tf<0>(f, x, a);
+  mma32(c, a[0], a[1], a[2], a[3], f.hc[0][0][0], f.hc[0][0][1]);
+  mma32(c + 4, a[0], a[1], a[2], a[3], f.hc[0][1][0], f.hc[0][1][1]);
 }
 
 // Final run (pass A): transforms, rescale, round to the output dtype, last
@@ -339,8 +379,10 @@ __device__ __forceinline__ void run_final(const Frags& f, uint32_t in_base, uint
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
-    fht15_forward_kernel(const T* __restrict__ latent, int64_t L, int layers, uint32_t seed32, int64_t first_block,
-                         int64_t nblocks, int64_t start, int64_t stop, T* __restrict__ out) {
+    fht15_forward_kernel(const T* __restrict__ latent, int64_t L, int layers, int n, uint32_t seed32,
+                         int64_t first_block, int64_t nblocks, int64_t start, int64_t stop, float corr,
+                         T* __restrict__ out) {
+  // "block" below is a 2^15-coordinate tile = 2^(15-n) consecutive generator blocks
   extern __shared__ __align__(128) unsigned char smem[];
   uint16_t* zbuf = reinterpret_cast<uint16_t*>(smem);   // scaled fp16 latent copy (64 KB)
   uint16_t* xbuf = zbuf + kB;                           // exchange buffers (64 KB each)
@@ -351,9 +393,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
   Frags f;
-  make_frags(f, g, t);
+  make_frags(f, g, t, n);
+  const int Bm = (1 << n) - 1;
 
-  // power-of-two prescale: latent L2 norm into [2^11, 2^12)
+  // power-of-two prescale: tile L2 norm into [2^11, 2^12)
   float ss = 0.0f;
   for (int64_t i = tid; i < L; i += kThreads) {
     float v = Cvt<T>::to_f(latent[i]);
@@ -366,6 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     float s = 0.0f;
     for (int i = 0; i < kThreads / 32; ++i) s += red[i];
+    s *= (float)(kB >> n);  // the tile holds 2^(15-n) copies of the latent
     int e = 0;
     if (s > 0.0f) {
       frexpf(sqrtf(s), &e);  // norm = m * 2^e with m in [0.5, 1)
@@ -380,15 +424,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool first_is_b = (layers != 2);
   for (int c = tid; c < kB / 8; c += kThreads) {  // 8 consecutive positions per step
     float v[8];
-    const int p0 = 8 * c;
-    if (p0 + 8 <= L && (reinterpret_cast<uintptr_t>(latent) & 15) == 0) {
-      uint4 raw = __ldg(reinterpret_cast<const uint4*>(latent + p0));
+    const int p0 = 8 * c, q0 = p0 & Bm;  // q0: position inside its block
+    if (q0 + 8 <= L && (reinterpret_cast<uintptr_t>(latent) & 15) == 0) {
+      uint4 raw = __ldg(reinterpret_cast<const uint4*>(latent + q0));
       const T* ev = reinterpret_cast<const T*>(&raw);
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[e] = Cvt<T>::to_f(ev[e]) * in_scale;
     } else {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = (p0 + e < L) ? Cvt<T>::to_f(latent[p0 + e]) * in_scale : 0.0f;
+      for (int e = 0; e < 8; ++e) v[e] = (q0 + e < L) ? Cvt<T>::to_f(latent[q0 + e]) * in_scale : 0.0f;
     }
     uint32_t hv[4];
 #pragma unroll
@@ -400,10 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int e = 0; e < 8; ++e) zbuf[lay_ba(p0 + e)] = (uint16_t)(hv[e >> 1] >> (16 * (e & 1)));
     }
   }
-  // per layer the factors are orthonormal up to sqrt(2) (the H8/2 factor)
-  const float out_scale = ldexpf(1.0f, k0) * (layers == 1   ? 0.70710678118654752f
-                                              : layers == 2 ? 0.5f
-                                                            : 0.35355339059327376f);
+  const float out_scale = ldexpf(1.0f, k0) * corr;
   const uint32_t zb = (uint32_t)__cvta_generic_to_shared(zbuf);
   const uint32_t xb = (uint32_t)__cvta_generic_to_shared(xbuf);
   const uint32_t yb = (uint32_t)__cvta_generic_to_shared(ybuf);
@@ -414,7 +455,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();  // the previous block is done with the sign table and buffers
     for (int i = tid; i < (layers + 1) * kWords; i += kThreads) {
       int l = i / kWords, wd = i - l * kWords;
-      sw[l * kWordsPad + spad(wd)] = sign_word(block_layer_key(seed32, blk, l), wd);
+      const int p = 32 * wd;
+      sw[l * kWordsPad + spad(wd)] =
+          sign_word(block_layer_key(seed32, (blk << (kLog - n)) + (p >> n), l), (p & Bm) >> 5);
     }
     __syncthreads();
     if (layers == 1) {
@@ -442,7 +485,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr size_t kSmem = 3 * kB * 2 + 4 * kWordsPad * 4;
 
 template <typename T>
-int launch_forward_t(const void* latent, int64_t L, int layers, uint32_t seed32, int64_t first_block,
+int launch_forward_t(const void* latent, int64_t L, int layers, int n, uint32_t seed32, int64_t first_block,
                      int64_t nblocks, int64_t start, int64_t stop, void* out, cudaStream_t st) {
   static bool attr = false;
   if (!attr) {
@@ -455,8 +498,9 @@ int launch_forward_t(const void* latent, int64_t L, int layers, uint32_t seed32,
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   int grid = (int)(nblocks < sms ? nblocks : sms);
-  fht15_forward_kernel<T><<<grid, kThreads, kSmem, st>>>(reinterpret_cast<const T*>(latent), L, layers, seed32,
-                                                         first_block, nblocks, start, stop,
+  const float corr = (float)std::pow(layer_correction(n), layers);
+  fht15_forward_kernel<T><<<grid, kThreads, kSmem, st>>>(reinterpret_cast<const T*>(latent), L, layers, n, seed32,
+                                                         first_block, nblocks, start, stop, corr,
                                                          reinterpret_cast<T*>(out));
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
@@ -514,7 +558,8 @@ __device__ __forceinline__ void run_final_acc(const Frags& f, uint32_t in_base, 
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
-    fht15_backward_kernel(const T* __restrict__ grad, int64_t L, int layers, uint32_t seed32, int64_t first_block,
+    fht15_backward_kernel(const T* __restrict__ grad, int64_t L, int layers, int n, uint32_t seed32, float corr,
+                          int64_t first_block,
                           int64_t nblocks, int64_t start, int64_t stop, float* __restrict__ partial,
                           int* __restrict__ err) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -531,7 +576,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
   Frags f;
-  make_frags(f, g, t);
+  make_frags(f, g, t, n);
+  const int Bm = (1 << n) - 1;
 
   if (w == 0) {
     uint32_t dst = (uint32_t)__cvta_generic_to_shared(&tmem_base_shared);
@@ -550,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_wait_st();
   }
 
-  const float layer_scale = layers == 1 ? 0.70710678118654752f : layers == 2 ? 0.5f : 0.35355339059327376f;
+  const float layer_scale = corr;
   const uint32_t xb = (uint32_t)__cvta_generic_to_shared(xbuf);
   const uint32_t yb = (uint32_t)__cvta_generic_to_shared(ybuf);
   const uint32_t stage_s = (uint32_t)__cvta_generic_to_shared(stage);
@@ -585,7 +631,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     for (int i = tid; i < (layers + 1) * kWords; i += kThreads) {
       int l = i / kWords, wd = i - l * kWords;
-      sw[l * kWordsPad + spad(wd)] = sign_word(block_layer_key(seed32, blk, l), wd);
+      const int p = 32 * wd;
+      sw[l * kWordsPad + spad(wd)] =
+          sign_word(block_layer_key(seed32, (blk << (kLog - n)) + (p >> n), l), (p & Bm) >> 5);
     }
     // gradient chunks of this block into registers, with their squared norm
     uint4 raw[8];
@@ -716,7 +764,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   __syncthreads();
-  for (int64_t p = tid; p < L; p += kThreads) partial[(int64_t)blockIdx.x * L + p] = prow[p];
+  // fold the 2^(15-n) blocks of the tile onto the latent positions
+  for (int64_t p = tid; p < L; p += kThreads) {
+    float v = 0.0f;
+    for (int j = 0; j < (kB >> n); ++j) v += prow[(j << n) + p];
+    partial[(int64_t)blockIdx.x * L + p] = v;
+  }
   asm volatile("tcgen05.fence::before_thread_sync;\n");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;\n");
@@ -753,7 +806,8 @@ inline int sm_count() {
 }
 
 template <typename T>
-int launch_backward_t(const void* grad, int64_t L, int layers, uint32_t seed32, int64_t first_block, int64_t nblocks,
+int launch_backward_t(const void* grad, int64_t L, int layers, int n, uint32_t seed32, int64_t first_block,
+                      int64_t nblocks,
                       int64_t start, int64_t stop, void* grad_latent, void* workspace, cudaStream_t st) {
   int* err = reinterpret_cast<int*>(workspace);
   float* partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kBwdHeader);
@@ -767,7 +821,9 @@ int launch_backward_t(const void* grad, int64_t L, int layers, uint32_t seed32, 
   }
   int sms = sm_count();
   int grid = (int)(nblocks < sms ? nblocks : sms);
-  fht15_backward_kernel<T><<<grid, kThreads, kSmemBwd, st>>>(reinterpret_cast<const T*>(grad), L, layers, seed32,
+  const float corr = (float)std::pow(layer_correction(n), layers);
+  fht15_backward_kernel<T><<<grid, kThreads, kSmemBwd, st>>>(reinterpret_cast<const T*>(grad), L, layers, n, seed32,
+                                                             corr,
                                                              first_block, nblocks, start, stop, partial, err);
   if (cudaGetLastError() != cudaSuccess) return -1;
   int rb = (int)((L + 255) / 256);
@@ -780,7 +836,9 @@ int launch_backward_t(const void* grad, int64_t L, int layers, uint32_t seed32, 
 bool mma_forward_supported(int dtype, int64_t latent_size, unsigned flags) {
   if (flags & LWL_FLAG_EXACT) return false;
   if (dtype != LWL_BF16 && dtype != LWL_F16) return false;
-  return next_pow2(latent_size) == fmma::kB;
+  // block sizes 2^5 .. 2^15; smaller blocks share a 2^15 tile
+  const int64_t B = next_pow2(latent_size);
+  return B >= 32 && B <= fmma::kB;
 }
 
 int mma_forward(int dtype, const void* latent, int64_t L, int layers, uint64_t seed, int64_t start, int64_t stop,
@@ -790,8 +848,8 @@ int mma_forward(int dtype, const void* latent, int64_t L, int layers, uint64_t s
   if (last <= first) return 0;
   uint32_t s32 = fold_seed(seed);
   if (dtype == LWL_BF16)
-    return fmma::launch_forward_t<__nv_bfloat16>(latent, L, layers, s32, first, last - first, start, stop, out, st);
-  return fmma::launch_forward_t<__half>(latent, L, layers, s32, first, last - first, start, stop, out, st);
+    return fmma::launch_forward_t<__nv_bfloat16>(latent, L, layers, ilog2(next_pow2(L)), s32, first, last - first, start, stop, out, st);
+  return fmma::launch_forward_t<__half>(latent, L, layers, ilog2(next_pow2(L)), s32, first, last - first, start, stop, out, st);
 }
 
 }  // namespace lwl
@@ -819,9 +877,9 @@ int mma_backward(int dtype, const void* grad, int64_t L, int layers, uint64_t se
   }
   uint32_t s32 = fold_seed(seed);
   if (dtype == LWL_BF16)
-    return fmma::launch_backward_t<__nv_bfloat16>(grad, L, layers, s32, first, last - first, start, stop, grad_latent,
+    return fmma::launch_backward_t<__nv_bfloat16>(grad, L, layers, ilog2(next_pow2(L)), s32, first, last - first, start, stop, grad_latent,
                                                   workspace, st);
-  return fmma::launch_backward_t<__half>(grad, L, layers, s32, first, last - first, start, stop, grad_latent,
+  return fmma::launch_backward_t<__half>(grad, L, layers, ilog2(next_pow2(L)), s32, first, last - first, start, stop, grad_latent,
                                          workspace, st);
 }
 

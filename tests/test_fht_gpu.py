@@ -166,3 +166,17 @@ def test_slice_equals_full_bf16_headline_shape(nat):
     full = nat.fht_forward(z, 64 * B, 3, 123, 0, 64 * B)
     part = nat.fht_forward(z, 64 * B, 3, 123, 5 * B + 77, 9 * B + 3)
     assert torch.equal(part, full[5 * B + 77: 9 * B + 3])
+
+
+@pytest.mark.parametrize("logb", range(5, 17))
+@pytest.mark.parametrize("layers", [1, 2, 3])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+def test_every_block_size_half(nat, logb, layers, dtype):
+    """16-bit generators at every padded block size (tensor-core path up to 2^15),
+    with partial first/last blocks and a latent shorter than the block."""
+    B = 1 << logb
+    L = B - B // 5 if B > 32 else B
+    size = max(4 * B, 65536) + 13
+    start, stop = B // 3, size - 7
+    _check_forward(nat, L, size, layers, 321, start, stop, dtype)
+    _check_backward(nat, L, size, layers, 321, start, stop, dtype)

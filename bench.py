@@ -370,6 +370,59 @@ def run_mlp(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_sweep(args) -> None:
+    """C2 sweep: every padded block size 2^5..2^23, layers 1 and 3, bf16 and fp32,
+    2^28 coordinates per call (latent length = block size); forward and backward
+    Gcoords/s, one JSON line per point."""
+    import torch
+
+    from latent_weight_lab import _native
+
+    lib = _native.load()
+    dev = torch.device("cuda", 0)
+    N = COORDS_PER_GPU
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    for dt_name, dt, code in (("bf16", torch.bfloat16, _native.LWL_BF16), ("fp32", torch.float32, _native.LWL_F32)):
+        y = torch.empty(N, device=dev, dtype=dt)
+        g = torch.randn(N, device=dev, dtype=dt)
+        for layers in (1, 3):
+            for k in range(args.min_log, args.max_log + 1):
+                B = 1 << k
+                z = torch.randn(B, device=dev, dtype=dt)
+                grad = torch.empty(B, device=dev, dtype=dt)
+                wsb = max(lib.lwl_fht_forward_workspace_bytes(code, B, N, layers, 0, N, 0),
+                          lib.lwl_fht_backward_workspace_bytes(code, B, N, layers, 0, N, 0), 1)
+                ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+
+                def fwd():
+                    assert lib.lwl_fht_forward(code, z.data_ptr(), B, N, layers, SEED, 0, N, y.data_ptr(),
+                                               ws.data_ptr(), wsb, 0, stream) == 0
+
+                def bwd():
+                    assert lib.lwl_fht_backward(code, g.data_ptr(), B, N, layers, SEED, 0, N, grad.data_ptr(),
+                                                ws.data_ptr(), wsb, 0, stream) == 0
+
+                res = {}
+                for name, fn in (("forward", fwd), ("backward", bwd)):
+                    for _ in range(2):
+                        fn()
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    reps = 3
+                    a.record()
+                    for _ in range(reps):
+                        fn()
+                    b.record()
+                    torch.cuda.synchronize()
+                    ms = a.elapsed_time(b) / reps
+                    res[name] = N / (ms * 1e-3) / 1e9
+                print(json.dumps({"sweep": "C2", "dtype": dt_name, "layers": layers, "block_size": B,
+                                  "coords": N, "forward_gcoords_s": res["forward"],
+                                  "backward_gcoords_s": res["backward"],
+                                  "forward_hbm_frac": res["forward"] * 1e9 * y.element_size() / 1e9
+                                  / _peaks()["hbm_gbs"]}), flush=True)
+                del ws
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -377,11 +430,15 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["fht", "mlp"], default="fht")
+    ap.add_argument("--workload", choices=["fht", "mlp", "sweep"], default="fht")
+    ap.add_argument("--min-log", type=int, default=5)
+    ap.add_argument("--max-log", type=int, default=23)
     ap.add_argument("--latent", type=int, default=32768, help="latent size for --workload mlp")
     args = ap.parse_args()
     if args.workload == "mlp":
         run_mlp(args)
+    elif args.workload == "sweep":
+        run_sweep(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

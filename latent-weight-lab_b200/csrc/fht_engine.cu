@@ -18,6 +18,7 @@
 
 #include "fht_engine.h"
 #include "fht_tile.cuh"
+#include "fht_mma.h"
 
 namespace lwl {
 
@@ -177,8 +178,11 @@ int plan_fht(const FhtArgs& a, FhtPlan& plan) {
     return 0;
   }
 
-  // two-pass layout
-  const int abits = (n + 1) / 2;
+  // two-pass layout.  For 16-bit dtypes the low pass is exactly 15 bits and
+  // runs on the tensor-core tile kernel (fht_lo_kernel); the high n-15 bits
+  // stay on the tile engine.
+  const bool use_lo = mma_lo_supported(a.dtype, n, a.flags);
+  const int abits = use_lo ? 15 : (n + 1) / 2;
   const int hbits = n - abits;
   // execution order of (part, post-layer) steps; part 1 = P1 (low bits), 2 = P2
   int step_part[6], step_sign[6], nsteps = 0;
@@ -241,6 +245,13 @@ int plan_fht(const FhtArgs& a, FhtPlan& plan) {
     p.src_kind = is_first ? (bwd ? SRC_SLICE : SRC_LATENT) : SRC_WS;
     p.dst_kind = (is_last && !bwd) ? DST_SLICE : DST_WS;
     finish_launch(a.dtype, l);
+    if (use_lo && step_part[s] == 1 && nseg <= 2) {
+      p.lo = 1;
+      p.lo_nseg = nseg;
+      p.lo_seg_slot[0] = seg_slot[0];
+      p.lo_seg_slot[1] = nseg > 1 ? seg_slot[1] : -1;
+      l.grid = mma_lo_grid(p);
+    }
     plan.nlaunch++;
     s = e_ + 1;
   }
@@ -273,6 +284,13 @@ int run_plan_t(const FhtArgs& a, FhtPlan& plan, cudaStream_t st) {
     if (p.dst_kind == DST_SLICE) p.dst = a.out;
     else if (p.dst_kind == DST_WS) p.dst = a.workspace;
     else p.partial = reinterpret_cast<float*>(a.workspace);
+    if (p.lo) {
+      if (mma_lo_launch(a.dtype, p, l.grid, st) != 0) {
+        set_error("tensor-core low-pass launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return LWL_ERR_CUDA;
+      }
+      continue;
+    }
     fht_tile_kernel<T><<<l.grid, l.threads, l.smem, st>>>(p);
     LWL_CUDA_TRY(cudaGetLastError());
   }

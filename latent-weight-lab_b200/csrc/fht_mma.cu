@@ -831,6 +831,193 @@ int launch_backward_t(const void* grad, int64_t L, int layers, int n, uint32_t s
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
+
+// ---------------------------------------------------------------------------
+// Low pass of large blocks: one work item = one 2^15 tile (positions
+// [j*2^15, (j+1)*2^15) of block b).  The planner's two-pass launch describes
+// input (latent / gradient slice / fp32 workspace), signs and output (dtype
+// slice / fp32 workspace); the transform is 1 or 2 applications of H_32768
+// on the tile, exactly normalised on output (the high bits are done by the
+// tile engine in fp32).
+
+// fp32 staging of a whole tile in natural order (X and Y buffers, 128 KB);
+// the XOR on bits 0-4 keeps both the scattered writer and the linear reader
+// bank-conflict free.
+__device__ __forceinline__ int lay_f32(int p) { return p ^ (((p >> 5) & 7) | (((p >> 9) & 3) << 3)); }
+
+template <typename T>
+__device__ __forceinline__ void lo_load8(const TileParams& p, int64_t b, int64_t pos0, float* v) {
+  if (p.src_kind == SRC_WS) {
+    const float* src = reinterpret_cast<const float*>(p.src) + (b - p.first_block) * p.B + pos0;
+    float4 a = __ldg(reinterpret_cast<const float4*>(src));
+    float4 c = __ldg(reinterpret_cast<const float4*>(src + 4));
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+    return;
+  }
+  const T* src = reinterpret_cast<const T*>(p.src);
+  int64_t off;
+  bool full;
+  if (p.src_kind == SRC_LATENT) {
+    off = pos0;
+    full = pos0 + 8 <= p.L;
+  } else {  // SRC_SLICE
+    int64_t g0 = b * p.B + pos0;
+    off = g0 - p.start;
+    full = g0 >= p.start && g0 + 8 <= p.stop;
+  }
+  if (full && (((reinterpret_cast<uintptr_t>(src + off)) & 15) == 0)) {
+    uint4 raw = __ldg(reinterpret_cast<const uint4*>(src + off));
+    const T* ev = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = Cvt<T>::to_f(ev[e]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      bool in;
+      if (p.src_kind == SRC_LATENT) {
+        in = pos0 + e < p.L;
+      } else {
+        int64_t g = b * p.B + pos0 + e;
+        in = g >= p.start && g < p.stop;
+      }
+      v[e] = in ? Cvt<T>::to_f(src[off + e]) : 0.0f;
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_constant__ TileParams p, float corr1) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint16_t* xbuf = reinterpret_cast<uint16_t*>(smem);
+  uint16_t* ybuf = xbuf + kB;
+  uint32_t* sw = reinterpret_cast<uint32_t*>(ybuf + kB);  // [slot][kWordsPad]
+  float* fstage = reinterpret_cast<float*>(smem);          // X+Y as 32768 fp32 (final fp32 output)
+  __shared__ float red[kThreads / 32];
+  __shared__ int k0_shared;
+
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
+  Frags f;
+  make_frags(f, g, t, kLog);
+  const uint32_t xb = (uint32_t)__cvta_generic_to_shared(xbuf);
+  const uint32_t yb = (uint32_t)__cvta_generic_to_shared(ybuf);
+  const int tpb = (int)(p.B >> kLog);
+  const int64_t ntiles = p.nblocks * tpb;
+  const int nseg = p.lo_nseg;
+  const int pre = p.pre_slot;
+  const int post = p.lo_seg_slot[nseg - 1];
+  const int mid = nseg == 2 ? p.lo_seg_slot[0] : -1;
+  (void)corr1;  // the 2^-0.5 per application is folded into the exact 2^7 below
+
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int64_t b = p.first_block + tile / tpb;
+    const int j = (int)(tile % tpb);
+    const int64_t tbase = (int64_t)j << kLog;  // first position of the tile in its block
+    __syncthreads();
+    for (int i = tid; i < p.nslots * kWords; i += kThreads) {
+      int sl = i / kWords, wd = i - sl * kWords;
+      sw[sl * kWordsPad + spad(wd)] = sign_word(block_layer_key(p.seed32, b, p.slot_layer[sl]), j * kWords + wd);
+    }
+    // tile norm (first read), then scaled fp16 landing in the first run's layout (second read, from L2)
+    float ss = 0.0f;
+    for (int c = tid; c < kB / 8; c += kThreads) {
+      float v[8];
+      lo_load8<T>(p, b, tbase + 8 * c, v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[w] = ss;
+    __syncthreads();
+    if (tid == 0) {
+      float s = 0.0f;
+      for (int i = 0; i < kThreads / 32; ++i) s += red[i];
+      int e = 0;
+      if (s > 0.0f) {
+        frexpf(sqrtf(s), &e);
+        e -= 12;
+      }
+      k0_shared = e;
+    }
+    __syncthreads();
+    const int k0 = k0_shared;
+    const float in_scale = ldexpf(1.0f, -k0);
+    uint16_t* land = nseg == 1 ? ybuf : xbuf;
+    for (int c = tid; c < kB / 8; c += kThreads) {
+      float v[8];
+      lo_load8<T>(p, b, tbase + 8 * c, v);
+      uint32_t hv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) hv[e] = pack_h2(v[2 * e] * in_scale, v[2 * e + 1] * in_scale);
+      if (nseg == 1) {
+        *reinterpret_cast<uint4*>(land + lay_ab(8 * c)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) land[lay_ba(8 * c + e)] = (uint16_t)(hv[e >> 1] >> (16 * (e & 1)));
+      }
+    }
+    __syncthreads();
+    const uint32_t* pre_sw = pre >= 0 ? sw + pre * kWordsPad : nullptr;
+    if (nseg == 1) {
+      if (pre_sw) run<1, false, true>(f, yb, xb, pre_sw, nullptr, w, lane, g, t);
+      else run<1, false, false>(f, yb, xb, nullptr, nullptr, w, lane, g, t);
+    } else {
+      if (pre_sw) run<0, false, true>(f, xb, yb, pre_sw, nullptr, w, lane, g, t);
+      else run<0, false, false>(f, xb, yb, nullptr, nullptr, w, lane, g, t);
+      __syncthreads();
+      run<1, true, false>(f, yb, xb, nullptr, sw + mid * kWordsPad, w, lane, g, t);
+    }
+    __syncthreads();
+    // The tile engine normalises once per layer (1/sqrt(B) with the sign that
+    // ends the layer) and leaves the other part of the layer unnormalised, so
+    // this pass outputs the unnormalised H_32768 result -- the fp16 internal
+    // value times 2^(k0 + 7 per application), exactly -- times 1/sqrt(B) for
+    // each application that ends a layer.
+    float scale = ldexpf(1.0f, k0 + 7 * nseg);
+    for (int sg = 0; sg < nseg; ++sg)
+      if (p.lo_seg_slot[sg] >= 0) scale *= p.scale;
+    if (p.dst_kind == DST_SLICE) {
+      // the post sign is always present on the final launch of a forward
+      run_final<T>(f, xb, yb, ybuf, sw + post * kWordsPad, scale, reinterpret_cast<T*>(p.dst), b * (p.B >> kLog) + j,
+                   p.start, p.stop, ((p.start & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.dst) & 15) == 0), w,
+                   lane, g, t);
+    } else {
+      // fp32 workspace: inputs of all 8 tiles to registers, then the X/Y buffers become a natural-order fp32 stage
+      uint32_t xin[8][4];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) load_tile<0>(xb, w, k, lane, xin[k]);
+      __syncthreads();
+      const uint32_t* psw = post >= 0 ? sw + post * kWordsPad : nullptr;
+      const int wb = dep_a(w, 0, g, 2 * t) >> 5;
+      const uint32_t u0 = psw ? ~psw[spad(wb)] : 0u, u1 = psw ? ~psw[spad(wb + 64)] : 0u;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        uint32_t a[4];
+        row_tf<0>(f, xin[k], a);
+        float c[8];
+        mma32(c, a[0], a[1], a[2], a[3], f.hc[0][0][0], f.hc[0][0][1]);
+        mma32(c + 4, a[0], a[1], a[2], a[3], f.hc[0][1][0], f.hc[0][1][1]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int R = g + 8 * ((i >> 1) & 1), C = 2 * t + (i & 1) + 8 * (i >> 2);
+          float v = c[i] * scale;
+          if (psw) {
+            const int bit = k + 8 * ((i >> 1) & 1) + 16 * (i & 1);
+            const uint32_t u = (i >> 2) ? u1 : u0;
+            v = __uint_as_float(__float_as_uint(v) ^ ((u << (31 - bit)) & 0x80000000u));
+          }
+          fstage[lay_f32(dep_a(w, k, R, C))] = v;
+        }
+      }
+      __syncthreads();
+      float* dst = reinterpret_cast<float*>(p.dst) + (b - p.first_block) * p.B + tbase;
+      for (int q = tid; q < kB; q += kThreads) dst[q] = fstage[lay_f32(q)];
+    }
+  }
+}
+
+constexpr size_t kSmemLo = 2 * kB * 2 + 4 * kWordsPad * 4;
+
 }  // namespace fmma
 
 bool mma_forward_supported(int dtype, int64_t latent_size, unsigned flags) {
@@ -881,6 +1068,46 @@ int mma_backward(int dtype, const void* grad, int64_t L, int layers, uint64_t se
                                                   workspace, st);
   return fmma::launch_backward_t<__half>(grad, L, layers, ilog2(next_pow2(L)), s32, first, last - first, start, stop, grad_latent,
                                          workspace, st);
+}
+
+}  // namespace lwl
+
+namespace lwl {
+
+bool mma_lo_supported(int dtype, int n, unsigned flags) {
+  if (flags & LWL_FLAG_EXACT) return false;
+  if (dtype != LWL_BF16 && dtype != LWL_F16) return false;
+  return n > fmma::kLog && n <= fmma::kLog + 8;
+}
+
+int mma_lo_grid(const TileParams& p) {
+  int64_t ntiles = p.nblocks * (p.B >> fmma::kLog);
+  int sms = fmma::sm_count();
+  return (int)(ntiles < sms ? ntiles : sms);
+}
+
+int mma_lo_launch(int dtype, const TileParams& p, int grid, cudaStream_t st) {
+  const float corr1 = (float)fmma::layer_correction(fmma::kLog);
+  if (dtype == LWL_BF16) {
+    static bool attr = false;
+    if (!attr) {
+      if (cudaFuncSetAttribute(fmma::fht_lo_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)fmma::kSmemLo) != cudaSuccess)
+        return -1;
+      attr = true;
+    }
+    fmma::fht_lo_kernel<__nv_bfloat16><<<grid, fmma::kThreads, fmma::kSmemLo, st>>>(p, corr1);
+  } else {
+    static bool attr = false;
+    if (!attr) {
+      if (cudaFuncSetAttribute(fmma::fht_lo_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)fmma::kSmemLo) != cudaSuccess)
+        return -1;
+      attr = true;
+    }
+    fmma::fht_lo_kernel<__half><<<grid, fmma::kThreads, fmma::kSmemLo, st>>>(p, corr1);
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 }  // namespace lwl

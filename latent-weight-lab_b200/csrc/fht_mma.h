@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "fht_tile.cuh"
+
 namespace lwl {
 
 // True when lwl_fht_forward with these arguments runs on the tensor-core kernel.
@@ -17,5 +19,12 @@ bool mma_backward_supported(int dtype, int64_t latent_size, unsigned flags);
 size_t mma_backward_workspace_bytes(int64_t latent_size, int64_t start, int64_t stop);
 int mma_backward(int dtype, const void* grad, int64_t latent_size, int layers, uint64_t seed, int64_t start,
                  int64_t stop, void* grad_latent, void* workspace, cudaStream_t st);
+
+// Low-15-bit pass of large blocks (B = 2^16 .. 2^23, 16-bit dtypes) on the
+// tensor-core tile kernel: one 2^15 tile per work item, input/output and signs
+// described by a two-pass TileParams launch of the planner (p.lo = 1).
+bool mma_lo_supported(int dtype, int n, unsigned flags);
+int mma_lo_grid(const TileParams& p);
+int mma_lo_launch(int dtype, const TileParams& p, int grid, cudaStream_t st);
 
 }  // namespace lwl

@@ -180,3 +180,14 @@ def test_every_block_size_half(nat, logb, layers, dtype):
     start, stop = B // 3, size - 7
     _check_forward(nat, L, size, layers, 321, start, stop, dtype)
     _check_backward(nat, L, size, layers, 321, start, stop, dtype)
+
+
+@pytest.mark.parametrize("logb", range(17, 24))
+@pytest.mark.parametrize("layers", [1, 2, 3])
+def test_large_block_sizes_bf16(nat, logb, layers):
+    """bf16 generators with blocks above 2^15: tensor-core low pass + fp32 high pass."""
+    B = 1 << logb
+    L = B - 1000
+    size = 2 * B + 13
+    _check_forward(nat, L, size, layers, 99, 17, size - 3, torch.bfloat16)
+    _check_backward(nat, L, size, layers, 99, 17, size - 3, torch.bfloat16)

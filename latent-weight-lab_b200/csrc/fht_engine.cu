@@ -85,29 +85,38 @@ size_t tile_smem(const TileParams& p) {
 
 int tile_threads(const TileParams& p) { return std::min(512, std::max(32, 1 << std::max(0, p.e - 5))); }
 
+using TileKernel = void (*)(TileParams);
+
+// The planner's (source, sink) combinations, each a separate instantiation.
 template <typename T>
-int occupancy(int threads, size_t smem) {
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(fht_tile_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-    attr_set = true;
-  }
+TileKernel tile_kernel_for(int src, int dst) {
+  if (src == SRC_LATENT && dst == DST_SLICE) return fht_tile_kernel<T, SRC_LATENT, DST_SLICE>;
+  if (src == SRC_LATENT && dst == DST_WS) return fht_tile_kernel<T, SRC_LATENT, DST_WS>;
+  if (src == SRC_SLICE && dst == DST_ACC) return fht_tile_kernel<T, SRC_SLICE, DST_ACC>;
+  if (src == SRC_SLICE && dst == DST_WS) return fht_tile_kernel<T, SRC_SLICE, DST_WS>;
+  if (src == SRC_WS && dst == DST_SLICE) return fht_tile_kernel<T, SRC_WS, DST_SLICE>;
+  return fht_tile_kernel<T, SRC_WS, DST_WS>;
+}
+
+template <typename T>
+int occupancy(int src, int dst, int threads, size_t smem) {
+  TileKernel k = tile_kernel_for<T>(src, dst);
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
   int blocks = 1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fht_tile_kernel<T>, threads, smem) != cudaSuccess)
-    blocks = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k, threads, smem) != cudaSuccess) blocks = 1;
   return std::max(1, blocks);
 }
 
-int occupancy_for(int dtype, int threads, size_t smem) {
-  if (dtype == LWL_BF16) return occupancy<__nv_bfloat16>(threads, smem);
-  if (dtype == LWL_F16) return occupancy<__half>(threads, smem);
-  return occupancy<float>(threads, smem);
+int occupancy_for(int dtype, int src, int dst, int threads, size_t smem) {
+  if (dtype == LWL_BF16) return occupancy<__nv_bfloat16>(src, dst, threads, smem);
+  if (dtype == LWL_F16) return occupancy<__half>(src, dst, threads, smem);
+  return occupancy<float>(src, dst, threads, smem);
 }
 
 void finish_launch(int dtype, TileLaunch& l) {
   l.threads = tile_threads(l.p);
   l.smem = tile_smem(l.p);
-  int64_t cap = (int64_t)sm_count() * occupancy_for(dtype, l.threads, l.smem);
+  int64_t cap = (int64_t)sm_count() * occupancy_for(dtype, l.p.src_kind, l.p.dst_kind, l.threads, l.smem);
   l.grid = (int)std::max<int64_t>(1, std::min<int64_t>(l.p.ntiles, cap));
 }
 
@@ -291,7 +300,7 @@ int run_plan_t(const FhtArgs& a, FhtPlan& plan, cudaStream_t st) {
       }
       continue;
     }
-    fht_tile_kernel<T><<<l.grid, l.threads, l.smem, st>>>(p);
+    tile_kernel_for<T>(p.src_kind, p.dst_kind)<<<l.grid, l.threads, l.smem, st>>>(p);
     LWL_CUDA_TRY(cudaGetLastError());
   }
   if (a.backward) {

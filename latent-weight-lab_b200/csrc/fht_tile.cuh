@@ -80,30 +80,6 @@ __device__ __forceinline__ void tile_coords(const TileParams& p, const TileCtx& 
   else pos |= (int64_t)u << p.ulo;
 }
 
-template <typename T>
-__device__ __forceinline__ float load_src(const TileParams& p, int64_t pos, int64_t blk) {
-  if (p.src_kind == SRC_LATENT) {
-    return pos < p.L ? Cvt<T>::to_f(reinterpret_cast<const T*>(p.src)[pos]) : 0.0f;
-  } else if (p.src_kind == SRC_SLICE) {
-    int64_t g = blk * p.B + pos;
-    return (g >= p.start && g < p.stop) ? Cvt<T>::to_f(reinterpret_cast<const T*>(p.src)[g - p.start]) : 0.0f;
-  } else {
-    int64_t b = blk - p.first_block;
-    return b < p.nblocks ? reinterpret_cast<const float*>(p.src)[b * p.B + pos] : 0.0f;
-  }
-}
-
-template <typename T>
-__device__ __forceinline__ void store_dst(const TileParams& p, int64_t pos, int64_t blk, float v) {
-  if (p.dst_kind == DST_SLICE) {
-    int64_t g = blk * p.B + pos;
-    if (g >= p.start && g < p.stop) reinterpret_cast<T*>(p.dst)[g - p.start] = Cvt<T>::from_f(v);
-  } else {  // DST_WS
-    int64_t b = blk - p.first_block;
-    if (b < p.nblocks) reinterpret_cast<float*>(p.dst)[b * p.B + pos] = v;
-  }
-}
-
 template <int R>
 __device__ __forceinline__ void butterflies(float (&v)[1 << R]) {
 #pragma unroll
@@ -120,24 +96,39 @@ __device__ __forceinline__ void butterflies(float (&v)[1 << R]) {
   }
 }
 
-// One run of radix group GR over the tile.  first/last select source/sink I/O.
-template <typename T, int GR>
+// One run of radix group GR over the tile.  first/last select source/sink I/O
+// (SRC/DST are compile-time).  A group's bits are transform bits, so within a
+// column the block is fixed and the position of element k is pos0 + (k << kshift).
+template <typename T, int SRC, int DST, int GR>
 __device__ void do_run(const TileParams& p, const TileCtx& c, const RunDesc& rd, float* data,
                        const uint32_t* signs, int words_per_slot, bool first, bool last) {
   const int glo = rd.glo;
   const int ncols = 1 << (p.e - GR);
   const int lowmask = (1 << glo) - 1;
+  const int kshift = glo - p.cb + p.tlo;
   for (int col = threadIdx.x; col < ncols; col += blockDim.x) {
     const int base = (col & lowmask) | ((col >> glo) << (glo + GR));
+    int64_t pos0, blk;
+    tile_coords(p, c, base, pos0, blk);
     float v[1 << GR];
     if (first) {
+      const int64_t bb = blk * p.B;
+      const int64_t wrow = (blk - p.first_block) * p.B;
+      const bool brow_ok = (blk - p.first_block) < p.nblocks;
 #pragma unroll
       for (int k = 0; k < (1 << GR); ++k) {
-        int t = base | (k << glo);
-        int64_t pos, blk;
-        tile_coords(p, c, t, pos, blk);
-        float x = load_src<T>(p, pos, blk);
+        const int64_t pos = pos0 + ((int64_t)k << kshift);
+        float x;
+        if (SRC == SRC_LATENT) {
+          x = pos < p.L ? Cvt<T>::to_f(reinterpret_cast<const T*>(p.src)[pos]) : 0.0f;
+        } else if (SRC == SRC_SLICE) {
+          const int64_t g = bb + pos;
+          x = (g >= p.start && g < p.stop) ? Cvt<T>::to_f(reinterpret_cast<const T*>(p.src)[g - p.start]) : 0.0f;
+        } else {
+          x = brow_ok ? reinterpret_cast<const float*>(p.src)[wrow + pos] : 0.0f;
+        }
         if (p.pre_slot >= 0) {
+          const int t = base + (k << glo);
           uint32_t w = signs[p.pre_slot * words_per_slot + (t >> p.wshift)];
           x = ((w >> (pos & 31)) & 1u) ? x : -x;
         }
@@ -145,56 +136,62 @@ __device__ void do_run(const TileParams& p, const TileCtx& c, const RunDesc& rd,
       }
     } else {
 #pragma unroll
-      for (int k = 0; k < (1 << GR); ++k) v[k] = data[pad_idx(base | (k << glo))];
+      for (int k = 0; k < (1 << GR); ++k) v[k] = data[pad_idx(base + (k << glo))];
     }
     for (int f = 0; f < rd.nfht; ++f) {
       butterflies<GR>(v);
       int s = rd.slot[f];
       if (s >= 0) {
         const float sc = p.scale;
+        const uint32_t* sws = signs + s * words_per_slot;
 #pragma unroll
         for (int k = 0; k < (1 << GR); ++k) {
-          int t = base | (k << glo);
-          int64_t pos, blk;
-          tile_coords(p, c, t, pos, blk);
-          uint32_t w = signs[s * words_per_slot + (t >> p.wshift)];
+          const int t = base + (k << glo);
+          const int64_t pos = pos0 + ((int64_t)k << kshift);
+          uint32_t w = sws[t >> p.wshift];
           v[k] *= ((w >> (pos & 31)) & 1u) ? sc : -sc;
         }
       }
     }
-    if (last && p.dst_kind != DST_ACC) {
+    if (last && DST != DST_ACC) {
+      const int64_t bb = blk * p.B;
+      const int64_t wrow = (blk - p.first_block) * p.B;
+      const bool brow_ok = (blk - p.first_block) < p.nblocks;
 #pragma unroll
       for (int k = 0; k < (1 << GR); ++k) {
-        int t = base | (k << glo);
-        int64_t pos, blk;
-        tile_coords(p, c, t, pos, blk);
-        store_dst<T>(p, pos, blk, v[k]);
+        const int64_t pos = pos0 + ((int64_t)k << kshift);
+        if (DST == DST_SLICE) {
+          const int64_t g = bb + pos;
+          if (g >= p.start && g < p.stop) reinterpret_cast<T*>(p.dst)[g - p.start] = Cvt<T>::from_f(v[k]);
+        } else if (brow_ok) {
+          reinterpret_cast<float*>(p.dst)[wrow + pos] = v[k];
+        }
       }
     } else {
 #pragma unroll
-      for (int k = 0; k < (1 << GR); ++k) data[pad_idx(base | (k << glo))] = v[k];
+      for (int k = 0; k < (1 << GR); ++k) data[pad_idx(base + (k << glo))] = v[k];
     }
   }
 }
 
-template <typename T>
+template <typename T, int SRC, int DST>
 __device__ __forceinline__ void dispatch_run(const TileParams& p, const TileCtx& c, const RunDesc& rd,
                                              float* data, const uint32_t* signs, int wps, bool first,
                                              bool last) {
   switch (rd.gr) {
-    case 0: do_run<T, 0>(p, c, rd, data, signs, wps, first, last); break;
-    case 1: do_run<T, 1>(p, c, rd, data, signs, wps, first, last); break;
-    case 2: do_run<T, 2>(p, c, rd, data, signs, wps, first, last); break;
-    case 3: do_run<T, 3>(p, c, rd, data, signs, wps, first, last); break;
-    case 4: do_run<T, 4>(p, c, rd, data, signs, wps, first, last); break;
-    default: do_run<T, 5>(p, c, rd, data, signs, wps, first, last); break;
+    case 0: do_run<T, SRC, DST, 0>(p, c, rd, data, signs, wps, first, last); break;
+    case 1: do_run<T, SRC, DST, 1>(p, c, rd, data, signs, wps, first, last); break;
+    case 2: do_run<T, SRC, DST, 2>(p, c, rd, data, signs, wps, first, last); break;
+    case 3: do_run<T, SRC, DST, 3>(p, c, rd, data, signs, wps, first, last); break;
+    case 4: do_run<T, SRC, DST, 4>(p, c, rd, data, signs, wps, first, last); break;
+    default: do_run<T, SRC, DST, 5>(p, c, rd, data, signs, wps, first, last); break;
   }
 }
 
 // Persistent tile kernel.  Shared memory: data (2^e + 2^e/32 floats), sign
 // tables (nslots * 2^(e-wshift) words), and for DST_ACC an fp32 accumulator
 // over the latent positions [L].
-template <typename T>
+template <typename T, int SRC, int DST>
 __global__ void __launch_bounds__(512) fht_tile_kernel(const __grid_constant__ TileParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int E = 1 << p.e;
@@ -203,7 +200,7 @@ __global__ void __launch_bounds__(512) fht_tile_kernel(const __grid_constant__ T
   const int wps = E >> p.wshift;
   float* acc = reinterpret_cast<float*>(signs + p.nslots * wps);
 
-  if (p.dst_kind == DST_ACC)
+  if (DST == DST_ACC)
     for (int i = threadIdx.x; i < p.L; i += blockDim.x) acc[i] = 0.0f;
 
   for (int64_t tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x) {
@@ -222,10 +219,10 @@ __global__ void __launch_bounds__(512) fht_tile_kernel(const __grid_constant__ T
     }
     __syncthreads();
     for (int ri = 0; ri < p.nruns; ++ri) {
-      dispatch_run<T>(p, c, p.runs[ri], data, signs, wps, ri == 0, ri == p.nruns - 1);
+      dispatch_run<T, SRC, DST>(p, c, p.runs[ri], data, signs, wps, ri == 0, ri == p.nruns - 1);
       __syncthreads();
     }
-    if (p.dst_kind == DST_ACC) {
+    if (DST == DST_ACC) {
       // sum the tile's blocks into the per-CTA latent-gradient accumulator
       const int nb = 1 << p.m;
       for (int i = threadIdx.x; i < p.L; i += blockDim.x) {
@@ -238,7 +235,7 @@ __global__ void __launch_bounds__(512) fht_tile_kernel(const __grid_constant__ T
       __syncthreads();
     }
   }
-  if (p.dst_kind == DST_ACC)
+  if (DST == DST_ACC)
     for (int i = threadIdx.x; i < p.L; i += blockDim.x) p.partial[(int64_t)blockIdx.x * p.L + i] = acc[i];
 }
 

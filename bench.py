@@ -423,6 +423,89 @@ def run_sweep(args) -> None:
                 del ws
 
 
+def run_gpt2(args) -> None:
+    """C4: GPT-2-small-shaped decoder inference (12 layers, d=768, 12 heads, seq 1024,
+    batch 8, vocab 50257 padded to 50304) with every qkv / attn-proj / fc / fc-proj
+    weight regenerated from its own BlockFHT latent on each forward (bf16, layers=3,
+    per-matrix seeds).  Embeddings and LayerNorms are dense random-init; the LM head
+    is tied to the token embedding.  Reports logits tokens/s on 1 GPU.
+
+    --latent-mode ratio: latent = 1% of the weight (the reference default
+    latent_ratio=0.01; block sizes 32768/8192/32768/32768); --latent-mode literal:
+    latent = 1/16 of the weight (block sizes 131072/65536/262144/262144)."""
+    import torch
+    import torch.nn.functional as F
+
+    from latent_weight_lab import BlockFHTLinear, _native
+
+    _native.load()
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    n_layer, d, n_head, T, Bsz, vocab = 12, 768, 12, 1024, 8, 50304
+
+    def lin(i, o, seed):
+        lat = max(1, round(i * o * (0.01 if args.latent_mode == "ratio" else 1 / 16)))
+        return BlockFHTLinear(i, o, bias=True, latent_dim=lat, layers=3, seed=seed).to(dev, torch.bfloat16)
+
+    class Block(torch.nn.Module):
+        def __init__(self, k):
+            super().__init__()
+            self.ln1 = torch.nn.LayerNorm(d).to(dev, torch.bfloat16)
+            self.ln2 = torch.nn.LayerNorm(d).to(dev, torch.bfloat16)
+            self.qkv, self.proj = lin(d, 3 * d, 4 * k), lin(d, d, 4 * k + 1)
+            self.fc, self.fcp = lin(d, 4 * d, 4 * k + 2), lin(4 * d, d, 4 * k + 3)
+
+        def forward(self, x):
+            b, t, _ = x.shape
+            q, k_, v = self.qkv(self.ln1(x)).split(d, dim=2)
+            q, k_, v = (u.view(b, t, n_head, d // n_head).transpose(1, 2) for u in (q, k_, v))
+            a = F.scaled_dot_product_attention(q, k_, v, is_causal=True).transpose(1, 2).reshape(b, t, d)
+            x = x + self.proj(a)
+            return x + self.fcp(F.gelu(self.fc(self.ln2(x))))
+
+    wte = (torch.randn(vocab, d, device=dev) * 0.02).bfloat16()
+    wpe = (torch.randn(T, d, device=dev) * 0.01).bfloat16()
+    blocks = [Block(k) for k in range(n_layer)]
+    lnf = torch.nn.LayerNorm(d).to(dev, torch.bfloat16)
+    g = torch.Generator(device="cpu").manual_seed(0)
+    idx_host = torch.randint(0, 50257, (Bsz, T), generator=g).pin_memory()
+
+    def forward(idx):
+        x = wte[idx] + wpe
+        for blk in blocks:
+            x = blk(x)
+        return F.linear(lnf(x), wte)
+
+    with torch.inference_mode():
+        idx = idx_host.to(dev)
+        for _ in range(args.warmup):
+            forward(idx)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(0) as clk:
+            a.record()
+            for _ in range(args.steps):
+                idx = idx_host.to(dev, non_blocking=True)
+                logits = forward(idx)
+                last = logits[:, -1, :].argmax(-1).cpu()  # result read back every step
+            b.record()
+            torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    lin_flops = 2 * Bsz * T * n_layer * (d * 3 * d + d * d + 2 * d * 4 * d)
+    line = {
+        "metric": "GPT-2-small inference logits tokens/s, BlockFHT-generated linears (C4)",
+        "value": Bsz * T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic token ids (uniform, seed 0), random-init weights",
+        "config": {"workload": f"C4 GPT-2-small inference, latent mode {args.latent_mode}", "batch": Bsz,
+                   "seq_len": T, "layers": n_layer, "d_model": d, "vocab_padded": vocab,
+                   "e2e": "token ids copied from pinned host memory and next-token argmax read back each step"},
+        "linear_tflops": lin_flops / (ms * 1e-3) / 1e12,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -430,7 +513,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["fht", "mlp", "sweep"], default="fht")
+    ap.add_argument("--workload", choices=["fht", "mlp", "sweep", "gpt2"], default="fht")
+    ap.add_argument("--latent-mode", choices=["ratio", "literal"], default="ratio")
     ap.add_argument("--min-log", type=int, default=5)
     ap.add_argument("--max-log", type=int, default=23)
     ap.add_argument("--latent", type=int, default=32768, help="latent size for --workload mlp")
@@ -439,6 +523,8 @@ def main() -> None:
         run_mlp(args)
     elif args.workload == "sweep":
         run_sweep(args)
+    elif args.workload == "gpt2":
+        run_gpt2(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

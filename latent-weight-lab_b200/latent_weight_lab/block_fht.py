@@ -163,7 +163,9 @@ class _BlockFHTLinearFn(torch.autograd.Function):
                 w = w + float(modulation_alpha) * latent.detach().square().sum()
             weight = w.view(int(out_features), int(in_features)).to(dtype=input.dtype)
             output = F.linear(input, weight, bias)
-        ctx.save_for_backward(input, latent)
+        # The reference regenerates W in backward to save memory (block_fht.py:330-337).
+        # W is small next to the activations here, so it is kept for grad_input.
+        ctx.save_for_backward(input, latent, weight)
         ctx.has_bias = bias is not None
         ctx.dims = (int(in_features), int(out_features), int(size), int(layers), int(seed))
         ctx.weight_scale = float(weight_scale)
@@ -173,18 +175,13 @@ class _BlockFHTLinearFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_output):
-        input, latent = ctx.saved_tensors
+        input, latent, weight = ctx.saved_tensors
         in_features, out_features, size, layers, seed = ctx.dims
         grad_input = grad_latent = grad_bias = None
         g2 = grad_output.reshape(-1, out_features)
         x2 = input.reshape(-1, in_features)
         if ctx.needs_input_grad[0]:
-            w = _native.fht_forward(latent.detach(), size, layers, seed, 0, size, flags=ctx.flags)
-            if ctx.weight_scale != 1.0:
-                w = w * ctx.weight_scale
-            if ctx.modulation_alpha != 0.0:
-                w = w + ctx.modulation_alpha * latent.detach().square().sum()
-            grad_input = g2.matmul(w.view(out_features, in_features).to(dtype=grad_output.dtype)).reshape_as(input)
+            grad_input = g2.matmul(weight.to(dtype=grad_output.dtype)).reshape_as(input)
         if ctx.needs_input_grad[1]:
             grad_weight = g2.transpose(0, 1).to(dtype=latent.dtype).matmul(x2.to(dtype=latent.dtype))
             grad_latent = _native.fht_backward(grad_weight.reshape(-1), latent.numel(), size, layers, seed, 0, size,

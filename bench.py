@@ -470,24 +470,46 @@ def run_gpt2(args) -> None:
     g = torch.Generator(device="cpu").manual_seed(0)
     idx_host = torch.randint(0, 50257, (Bsz, T), generator=g).pin_memory()
 
+    model = torch.nn.ModuleList(blocks)
+    from latent_weight_lab import prepare_block_fht_weight_cache
+
     def forward(idx):
+        # every generated weight of the model in one grouped library launch, then the dense compute
+        prepare_block_fht_weight_cache(model)
         x = wte[idx] + wpe
         for blk in blocks:
             x = blk(x)
+        for m in model.modules():
+            if hasattr(m, "_cached_weight"):
+                m._cached_weight = None
         return F.linear(lnf(x), wte)
 
-    with torch.inference_mode():
+    with torch.no_grad():
         idx = idx_host.to(dev)
         for _ in range(args.warmup):
             forward(idx)
+        torch.cuda.synchronize()
+        # the whole forward (generation + dense compute) replays as one CUDA graph
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            forward(idx)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        with torch.cuda.graph(graph):
+            logits = forward(idx)
+            last_dev = logits[:, -1, :].argmax(-1)
+        last = torch.empty_like(last_dev, device="cpu").pin_memory()
+        for _ in range(args.warmup):
+            graph.replay()
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(0) as clk:
             a.record()
             for _ in range(args.steps):
-                idx = idx_host.to(dev, non_blocking=True)
-                logits = forward(idx)
-                last = logits[:, -1, :].argmax(-1).cpu()  # result read back every step
+                idx.copy_(idx_host, non_blocking=True)  # token ids from pinned host memory
+                graph.replay()
+                last.copy_(last_dev, non_blocking=True)  # next-token ids read back every step
             b.record()
             torch.cuda.synchronize()
     ms = a.elapsed_time(b) / args.steps
@@ -499,7 +521,8 @@ def run_gpt2(args) -> None:
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic token ids (uniform, seed 0), random-init weights",
         "config": {"workload": f"C4 GPT-2-small inference, latent mode {args.latent_mode}", "batch": Bsz,
                    "seq_len": T, "layers": n_layer, "d_model": d, "vocab_padded": vocab,
-                   "e2e": "token ids copied from pinned host memory and next-token argmax read back each step"},
+                   "e2e": "token ids copied from pinned host memory and next-token argmax read back each step",
+                   "execution": "one CUDA graph per forward (grouped weight generation + dense compute)"},
         "linear_tflops": lin_flops / (ms * 1e-3) / 1e12,
         "clocks": clk.summary(),
     }

@@ -70,6 +70,28 @@ int lwl_fht_forward(int dtype, const void* latent, int64_t latent_size, int64_t 
                     uint64_t seed, int64_t start, int64_t stop, void* out, void* workspace,
                     size_t workspace_bytes, unsigned flags, void* stream);
 
+/* One generator call of a grouped forward. */
+typedef struct lwl_fht_forward_desc {
+  const void* latent;  /* [latent_size], the group's dtype */
+  int64_t latent_size;
+  int64_t size;
+  int layers;
+  uint64_t seed;
+  int64_t start, stop;  /* coordinates [start, stop) */
+  void* out;            /* [stop - start], the group's dtype */
+} lwl_fht_forward_desc;
+
+/* count lwl_fht_forward calls in as few kernel launches as possible (one
+ * launch per 96 generators): the tiles of all generators share one persistent
+ * grid, so many small weights (the linears of a model) fill the GPU.
+ * 16-bit dtypes with padded block size <= 2^15 take the grouped path; other
+ * descriptors are run one by one and must need no workspace (else
+ * LWL_ERR_UNSUPPORTED).  No direct reference counterpart: replaces the
+ * per-module generation loop of prepare_block_fht_weight_cache /
+ * materialize_weight_cache (latent_weight_lab/block_fht.py:503-512, 560-563). */
+int lwl_fht_forward_grouped(int dtype, int count, const lwl_fht_forward_desc* descs, unsigned flags,
+                            void* stream);
+
 /* Workspace needed by lwl_fht_backward (bytes). */
 size_t lwl_fht_backward_workspace_bytes(int dtype, int64_t latent_size, int64_t size, int layers,
                                         int64_t start, int64_t stop, unsigned flags);

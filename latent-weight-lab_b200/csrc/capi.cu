@@ -196,6 +196,45 @@ int lwl_fht_backward(int dtype, const void* grad_out, int64_t latent_size, int64
                        workspace, workspace_bytes, flags, stream);
 }
 
+int lwl_fht_forward_grouped(int dtype, int count, const lwl_fht_forward_desc* descs, unsigned flags,
+                            void* stream) {
+  lwl::g_err[0] = 0;
+  if (count < 0 || (count > 0 && !descs)) {
+    lwl::set_error("invalid descriptor array");
+    return LWL_ERR_INVALID;
+  }
+  bool all_fast = true;
+  for (int i = 0; i < count; ++i) {
+    const lwl_fht_forward_desc& q = descs[i];
+    int st = lwl::validate_fht(dtype, q.latent_size, q.size, q.layers, q.start, q.stop);
+    if (st) return st;
+    if (q.stop > q.start && (!q.latent || !q.out)) {
+      lwl::set_error("descriptor %d: null data pointer", i);
+      return LWL_ERR_INVALID;
+    }
+    if (!lwl::mma_forward_supported(dtype, q.latent_size, flags)) all_fast = false;
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (all_fast) {
+    if (lwl::mma_forward_grouped(dtype, count, descs, st) != 0) {
+      lwl::set_error("grouped forward launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+      return LWL_ERR_CUDA;
+    }
+    return LWL_OK;
+  }
+  for (int i = 0; i < count; ++i) {
+    const lwl_fht_forward_desc& q = descs[i];
+    if (lwl::fht_ws(false, dtype, q.latent_size, q.size, q.layers, q.start, q.stop, flags) > 0) {
+      lwl::set_error("descriptor %d needs a workspace; call lwl_fht_forward for it", i);
+      return LWL_ERR_UNSUPPORTED;
+    }
+    int rc = lwl_fht_forward(dtype, q.latent, q.latent_size, q.size, q.layers, q.seed, q.start, q.stop, q.out,
+                             nullptr, 0, flags, stream);
+    if (rc) return rc;
+  }
+  return LWL_OK;
+}
+
 int lwl_fht_launch_count(int dtype, int64_t latent_size, int64_t size, int layers, int64_t start, int64_t stop,
                          int backward, unsigned flags) {
   if (lwl::validate_fht(dtype, latent_size, size, layers, start, stop) != LWL_OK) return -1;

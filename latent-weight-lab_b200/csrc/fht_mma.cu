@@ -42,6 +42,24 @@ constexpr int kWords = kB / 32;
 constexpr int kWordsPad = kWords + kWords / 128 + 8;
 __device__ __forceinline__ int spad(int w) { return w + (w >> 7); }
 
+// One generator of a grouped forward launch (passed by value as a kernel parameter).
+struct FwdDesc {
+  const void* latent;
+  void* out;
+  int64_t L, start, stop;
+  int64_t first_tile;   // first 2^15-coordinate tile touched by [start, stop)
+  int64_t tile_prefix;  // work items of the descriptors before this one
+  uint32_t seed32;
+  int n, layers;
+  float corr;  // exact-power-of-two factor scales -> 2^(-n/2) per layer
+};
+constexpr int kMaxGroup = 96;
+struct FwdGroup {
+  int count;
+  int64_t total_tiles;
+  FwdDesc d[kMaxGroup];
+};
+
 // position of element (warp w, tile k, tile row R, tile col C) in each pass
 __device__ __forceinline__ int dep_a(int w, int k, int R, int C) {
   return k | ((R >> 3) & 1) << 3 | (C & 1) << 4 | (R & 7) << 5 | (w & 1) << 8 | ((C >> 1) & 3) << 9 |
@@ -377,99 +395,108 @@ __device__ __forceinline__ void run_final(const Frags& f, uint32_t in_base, uint
   }
 }
 
+// Forward kernel over a group of generators: work item = one 2^15-coordinate
+// tile of one descriptor (a single call is a group of one).  The scaled fp16
+// latent copy and the constant fragments are rebuilt only when a CTA moves to
+// the next descriptor.
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1)
-    fht15_forward_kernel(const T* __restrict__ latent, int64_t L, int layers, int n, uint32_t seed32,
-                         int64_t first_block, int64_t nblocks, int64_t start, int64_t stop, float corr,
-                         T* __restrict__ out) {
-  // "block" below is a 2^15-coordinate tile = 2^(15-n) consecutive generator blocks
+__global__ void __launch_bounds__(kThreads, 1) fht15_forward_kernel(const __grid_constant__ FwdGroup G) {
   extern __shared__ __align__(128) unsigned char smem[];
   uint16_t* zbuf = reinterpret_cast<uint16_t*>(smem);   // scaled fp16 latent copy (64 KB)
   uint16_t* xbuf = zbuf + kB;                           // exchange buffers (64 KB each)
   uint16_t* ybuf = xbuf + kB;
-  uint32_t* sw = reinterpret_cast<uint32_t*>(ybuf + kB);  // sign words [layers+1][1024]
+  uint32_t* sw = reinterpret_cast<uint32_t*>(ybuf + kB);  // sign words [layers+1][kWordsPad]
   __shared__ float red[kThreads / 32];
   __shared__ int k0_shared;
 
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
-  Frags f;
-  make_frags(f, g, t, n);
-  const int Bm = (1 << n) - 1;
-
-  // power-of-two prescale: tile L2 norm into [2^11, 2^12)
-  float ss = 0.0f;
-  for (int64_t i = tid; i < L; i += kThreads) {
-    float v = Cvt<T>::to_f(latent[i]);
-    ss += v * v;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if (lane == 0) red[w] = ss;
-  __syncthreads();
-  if (tid == 0) {
-    float s = 0.0f;
-    for (int i = 0; i < kThreads / 32; ++i) s += red[i];
-    s *= (float)(kB >> n);  // the tile holds 2^(15-n) copies of the latent
-    int e = 0;
-    if (s > 0.0f) {
-      frexpf(sqrtf(s), &e);  // norm = m * 2^e with m in [0.5, 1)
-      e -= 12;
-    }
-    k0_shared = e;
-  }
-  __syncthreads();
-  const int k0 = k0_shared;
-  const float in_scale = ldexpf(1.0f, -k0);
-  // the first run is pass B for layers 1 and 3, pass A for layers 2
-  const bool first_is_b = (layers != 2);
-  for (int c = tid; c < kB / 8; c += kThreads) {  // 8 consecutive positions per step
-    float v[8];
-    const int p0 = 8 * c, q0 = p0 & Bm;  // q0: position inside its block
-    if (q0 + 8 <= L && (reinterpret_cast<uintptr_t>(latent) & 15) == 0) {
-      uint4 raw = __ldg(reinterpret_cast<const uint4*>(latent + q0));
-      const T* ev = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = Cvt<T>::to_f(ev[e]) * in_scale;
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = (q0 + e < L) ? Cvt<T>::to_f(latent[q0 + e]) * in_scale : 0.0f;
-    }
-    uint32_t hv[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) hv[e] = pack_h2(v[2 * e], v[2 * e + 1]);
-    if (first_is_b) {
-      *reinterpret_cast<uint4*>(zbuf + lay_ab(p0)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) zbuf[lay_ba(p0 + e)] = (uint16_t)(hv[e >> 1] >> (16 * (e & 1)));
-    }
-  }
-  const float out_scale = ldexpf(1.0f, k0) * corr;
   const uint32_t zb = (uint32_t)__cvta_generic_to_shared(zbuf);
   const uint32_t xb = (uint32_t)__cvta_generic_to_shared(xbuf);
   const uint32_t yb = (uint32_t)__cvta_generic_to_shared(ybuf);
-  const bool vec_ok = ((start & 7) == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+  Frags f;
+  int cur = -1, k0 = 0;
 
-  for (int64_t bi = blockIdx.x; bi < nblocks; bi += gridDim.x) {
-    const int64_t blk = first_block + bi;
-    __syncthreads();  // the previous block is done with the sign table and buffers
+  for (int64_t item = blockIdx.x; item < G.total_tiles; item += gridDim.x) {
+    int di = 0;
+    while (di + 1 < G.count && G.d[di + 1].tile_prefix <= item) ++di;
+    const FwdDesc& D = G.d[di];
+    const T* latent = reinterpret_cast<const T*>(D.latent);
+    const int n = D.n, layers = D.layers, Bm = (1 << n) - 1;
+    const int64_t L = D.L;
+    __syncthreads();  // the previous tile is done with the latent copy, sign table and buffers
+    if (di != cur) {
+      make_frags(f, g, t, n);
+      // power-of-two prescale: tile L2 norm into [2^11, 2^12)
+      float ss = 0.0f;
+      for (int64_t i = tid; i < L; i += kThreads) {
+        float v = Cvt<T>::to_f(latent[i]);
+        ss += v * v;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) red[w] = ss;
+      __syncthreads();
+      if (tid == 0) {
+        float s = 0.0f;
+        for (int i = 0; i < kThreads / 32; ++i) s += red[i];
+        s *= (float)(kB >> n);  // the tile holds 2^(15-n) copies of the latent
+        int e = 0;
+        if (s > 0.0f) {
+          frexpf(sqrtf(s), &e);  // norm = m * 2^e with m in [0.5, 1)
+          e -= 12;
+        }
+        k0_shared = e;
+      }
+      __syncthreads();
+      k0 = k0_shared;
+      const float in_scale = ldexpf(1.0f, -k0);
+      // the first run is pass B for layers 1 and 3, pass A for layers 2
+      const bool first_is_b = (layers != 2);
+      for (int c = tid; c < kB / 8; c += kThreads) {  // 8 consecutive positions per step
+        float v[8];
+        const int p0 = 8 * c, q0 = p0 & Bm;  // q0: position inside its block
+        if (q0 + 8 <= L && (reinterpret_cast<uintptr_t>(latent) & 15) == 0) {
+          uint4 raw = __ldg(reinterpret_cast<const uint4*>(latent + q0));
+          const T* ev = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = Cvt<T>::to_f(ev[e]) * in_scale;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = (q0 + e < L) ? Cvt<T>::to_f(latent[q0 + e]) * in_scale : 0.0f;
+        }
+        uint32_t hv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) hv[e] = pack_h2(v[2 * e], v[2 * e + 1]);
+        if (first_is_b) {
+          *reinterpret_cast<uint4*>(zbuf + lay_ab(p0)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) zbuf[lay_ba(p0 + e)] = (uint16_t)(hv[e >> 1] >> (16 * (e & 1)));
+        }
+      }
+      cur = di;
+    }
+    const float out_scale = ldexpf(1.0f, k0) * D.corr;
+    T* out = reinterpret_cast<T*>(D.out);
+    const bool vec_ok = ((D.start & 7) == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+    const int64_t blk = D.first_tile + (item - D.tile_prefix);
     for (int i = tid; i < (layers + 1) * kWords; i += kThreads) {
       int l = i / kWords, wd = i - l * kWords;
       const int p = 32 * wd;
       sw[l * kWordsPad + spad(wd)] =
-          sign_word(block_layer_key(seed32, (blk << (kLog - n)) + (p >> n), l), (p & Bm) >> 5);
+          sign_word(block_layer_key(D.seed32, (blk << (kLog - n)) + (p >> n), l), (p & Bm) >> 5);
     }
     __syncthreads();
     if (layers == 1) {
       run<1, false, true>(f, zb, xb, sw, nullptr, w, lane, g, t);
       __syncthreads();
-      run_final<T>(f, xb, yb, ybuf, sw + 1 * kWordsPad, out_scale, out, blk, start, stop, vec_ok, w, lane, g, t);
+      run_final<T>(f, xb, yb, ybuf, sw + 1 * kWordsPad, out_scale, out, blk, D.start, D.stop, vec_ok, w, lane, g, t);
     } else if (layers == 2) {
       run<0, false, true>(f, zb, yb, sw, nullptr, w, lane, g, t);
       __syncthreads();
       run<1, true, false>(f, yb, xb, nullptr, sw + 1 * kWordsPad, w, lane, g, t);
       __syncthreads();
-      run_final<T>(f, xb, yb, ybuf, sw + 2 * kWordsPad, out_scale, out, blk, start, stop, vec_ok, w, lane, g, t);
+      run_final<T>(f, xb, yb, ybuf, sw + 2 * kWordsPad, out_scale, out, blk, D.start, D.stop, vec_ok, w, lane, g, t);
     } else {
       run<1, false, true>(f, zb, xb, sw, nullptr, w, lane, g, t);
       __syncthreads();
@@ -477,16 +504,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncthreads();
       run<1, true, false>(f, yb, xb, nullptr, sw + 2 * kWordsPad, w, lane, g, t);
       __syncthreads();
-      run_final<T>(f, xb, yb, ybuf, sw + 3 * kWordsPad, out_scale, out, blk, start, stop, vec_ok, w, lane, g, t);
+      run_final<T>(f, xb, yb, ybuf, sw + 3 * kWordsPad, out_scale, out, blk, D.start, D.stop, vec_ok, w, lane, g, t);
     }
   }
 }
 
 constexpr size_t kSmem = 3 * kB * 2 + 4 * kWordsPad * 4;
 
+inline int sm_count();
+
 template <typename T>
-int launch_forward_t(const void* latent, int64_t L, int layers, int n, uint32_t seed32, int64_t first_block,
-                     int64_t nblocks, int64_t start, int64_t stop, void* out, cudaStream_t st) {
+int launch_forward_t(const FwdGroup& G, cudaStream_t st) {
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(fht15_forward_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem) !=
@@ -494,17 +522,12 @@ int launch_forward_t(const void* latent, int64_t L, int layers, int n, uint32_t 
       return -1;
     attr = true;
   }
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  int grid = (int)(nblocks < sms ? nblocks : sms);
-  const float corr = (float)std::pow(layer_correction(n), layers);
-  fht15_forward_kernel<T><<<grid, kThreads, kSmem, st>>>(reinterpret_cast<const T*>(latent), L, layers, n, seed32,
-                                                         first_block, nblocks, start, stop, corr,
-                                                         reinterpret_cast<T*>(out));
+  if (G.total_tiles <= 0) return 0;
+  int sms = sm_count();
+  int grid = (int)(G.total_tiles < sms ? G.total_tiles : sms);
+  fht15_forward_kernel<T><<<grid, kThreads, kSmem, st>>>(G);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
-
 
 // ---------------------------------------------------------------------------
 // Backward: grad_z = sum_b [S0 Ĥ S1 ... Ĥ S_layers g_b][0:L].  Same runs as the
@@ -1028,15 +1051,55 @@ bool mma_forward_supported(int dtype, int64_t latent_size, unsigned flags) {
   return B >= 32 && B <= fmma::kB;
 }
 
-int mma_forward(int dtype, const void* latent, int64_t L, int layers, uint64_t seed, int64_t start, int64_t stop,
-                void* out, cudaStream_t st) {
+// Fill descriptor d of G for one generator call (tiles counted from G's running total).
+static void add_forward_desc(fmma::FwdGroup& G, const void* latent, int64_t L, int layers, uint64_t seed,
+                             int64_t start, int64_t stop, void* out) {
   const int64_t B = fmma::kB;
   int64_t first = start / B, last = (stop + B - 1) / B;
-  if (last <= first) return 0;
-  uint32_t s32 = fold_seed(seed);
-  if (dtype == LWL_BF16)
-    return fmma::launch_forward_t<__nv_bfloat16>(latent, L, layers, ilog2(next_pow2(L)), s32, first, last - first, start, stop, out, st);
-  return fmma::launch_forward_t<__half>(latent, L, layers, ilog2(next_pow2(L)), s32, first, last - first, start, stop, out, st);
+  fmma::FwdDesc& D = G.d[G.count++];
+  D.latent = latent;
+  D.out = out;
+  D.L = L;
+  D.start = start;
+  D.stop = stop;
+  D.first_tile = first;
+  D.tile_prefix = G.total_tiles;
+  D.seed32 = fold_seed(seed);
+  D.n = ilog2(next_pow2(L));
+  D.layers = layers;
+  D.corr = (float)std::pow(fmma::layer_correction(D.n), layers);
+  G.total_tiles += (last > first ? last - first : 0);
+}
+
+static int launch_group(int dtype, const fmma::FwdGroup& G, cudaStream_t st) {
+  if (dtype == LWL_BF16) return fmma::launch_forward_t<__nv_bfloat16>(G, st);
+  return fmma::launch_forward_t<__half>(G, st);
+}
+
+int mma_forward(int dtype, const void* latent, int64_t L, int layers, uint64_t seed, int64_t start, int64_t stop,
+                void* out, cudaStream_t st) {
+  fmma::FwdGroup G;
+  G.count = 0;
+  G.total_tiles = 0;
+  add_forward_desc(G, latent, L, layers, seed, start, stop, out);
+  return launch_group(dtype, G, st);
+}
+
+int mma_forward_grouped(int dtype, int count, const lwl_fht_forward_desc* descs, cudaStream_t st) {
+  fmma::FwdGroup G;
+  G.count = 0;
+  G.total_tiles = 0;
+  for (int i = 0; i < count; ++i) {
+    const lwl_fht_forward_desc& q = descs[i];
+    if (q.stop <= q.start) continue;
+    add_forward_desc(G, q.latent, q.latent_size, q.layers, q.seed, q.start, q.stop, q.out);
+    if (G.count == fmma::kMaxGroup) {
+      if (launch_group(dtype, G, st) != 0) return -1;
+      G.count = 0;
+      G.total_tiles = 0;
+    }
+  }
+  return G.count ? launch_group(dtype, G, st) : 0;
 }
 
 }  // namespace lwl

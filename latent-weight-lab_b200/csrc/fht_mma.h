@@ -4,6 +4,7 @@
 #include <stdint.h>
 
 #include "fht_tile.cuh"
+#include "lwl_b200.h"
 
 namespace lwl {
 
@@ -12,6 +13,8 @@ bool mma_forward_supported(int dtype, int64_t latent_size, unsigned flags);
 // Tensor-core forward for padded block size 2^15; returns 0 or -1 (launch failure).
 int mma_forward(int dtype, const void* latent, int64_t latent_size, int layers, uint64_t seed, int64_t start,
                 int64_t stop, void* out, cudaStream_t st);
+// Many tensor-core forwards in as few launches as possible (up to 96 generators per launch).
+int mma_forward_grouped(int dtype, int count, const lwl_fht_forward_desc* descs, cudaStream_t st);
 
 // Tensor-core backward for padded block size 2^15 (fp32 partials in TMEM,
 // one [L] row per CTA in the workspace, then a row reduction).

@@ -48,12 +48,22 @@ def _declare(lib: ctypes.CDLL) -> None:
         fn = getattr(lib, name)
         fn.restype = sz
         fn.argtypes = [ci, i64, i64, ci, i64, i64, cu]
+    lib.lwl_fht_forward_grouped.restype = ci
+    lib.lwl_fht_forward_grouped.argtypes = [ci, ci, ctypes.POINTER(ForwardDesc), cu, vp]
     lib.lwl_fht_launch_count.restype = ci
     lib.lwl_fht_launch_count.argtypes = [ci, i64, i64, ci, i64, i64, ci, cu]
     for name in ("lwl_fht_forward", "lwl_fht_backward"):
         fn = getattr(lib, name)
         fn.restype = ci
         fn.argtypes = [ci, vp, i64, i64, ci, u64, i64, i64, vp, vp, sz, cu, vp]
+
+
+class ForwardDesc(ctypes.Structure):
+    """lwl_fht_forward_desc (include/lwl_b200.h)."""
+
+    _fields_ = [("latent", ctypes.c_void_p), ("latent_size", ctypes.c_int64), ("size", ctypes.c_int64),
+                ("layers", ctypes.c_int), ("seed", ctypes.c_uint64), ("start", ctypes.c_int64),
+                ("stop", ctypes.c_int64), ("out", ctypes.c_void_p)]
 
 
 def load() -> ctypes.CDLL:
@@ -173,3 +183,31 @@ def sign_words(seed: int, block: int, layer: int, first_word: int, count: int,
         _check(lib.lwl_sign_words(_seed_u64(seed), int(block), int(layer), int(first_word), int(count),
                                   out.data_ptr() if count else None, _stream_ptr(device)))
     return out.to(torch.int64) & 0xFFFFFFFF
+
+
+def fht_forward_grouped(items, flags: int = 0) -> list[torch.Tensor]:
+    """Several generator slices in as few launches as possible.
+
+    items: sequence of (latent, size, layers, seed, start, stop); all latents
+    share one CUDA device and dtype.  Returns one output tensor per item.
+    """
+    items = list(items)
+    if not items:
+        return []
+    lib = load()
+    dev, dt = items[0][0].device, items[0][0].dtype
+    outs, keep = [], []
+    descs = (ForwardDesc * len(items))()
+    for i, (latent, size, layers, seed, start, stop) in enumerate(items):
+        _require_cuda(latent, "latent")
+        if latent.device != dev or latent.dtype != dt:
+            raise ValueError("grouped generation needs one device and dtype")
+        latent = latent.detach().contiguous()
+        keep.append(latent)
+        out = torch.empty(max(int(stop) - int(start), 0), dtype=dt, device=dev)
+        outs.append(out)
+        descs[i] = ForwardDesc(latent.data_ptr(), latent.numel(), int(size), int(layers), _seed_u64(seed),
+                               int(start), int(stop), out.data_ptr() if out.numel() else None)
+    with torch.cuda.device(dev):
+        _check(lib.lwl_fht_forward_grouped(dtype_code(dt), len(items), descs, int(flags), _stream_ptr(dev)))
+    return outs

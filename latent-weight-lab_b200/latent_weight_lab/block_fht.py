@@ -293,7 +293,11 @@ class BlockFHTLinear(nn.Module):
     @property
     def weight(self) -> torch.Tensor:
         """The effective [out, in] weight, differentiable in every parameter."""
-        weight = self.generator() * self.weight_scale
+        return self._compose_weight(self.generator())
+
+    def _compose_weight(self, generated: torch.Tensor) -> torch.Tensor:
+        """Scale, modulation, residual base, spectral correction and gains around the generated vector."""
+        weight = generated * self.weight_scale
         if self.modulation_alpha != 0.0:
             weight = weight + self.modulation_alpha * self._modulation_offset()
         weight = weight.view(self.out_features, self.in_features)
@@ -399,9 +403,32 @@ class BlockFHTLinear(nn.Module):
 
 
 def prepare_block_fht_weight_cache(model: nn.Module, dtype: torch.dtype | None = None) -> None:
-    for module in model.modules():
-        if isinstance(module, BlockFHTLinear):
-            module.materialize_weight_cache(dtype=dtype)
+    """Materialise every BlockFHTLinear weight of `model` (block_fht.py:560-563).
+
+    The generators are run together: one grouped library call per
+    (device, dtype) instead of one call per module.
+    """
+    modules = [m for m in model.modules() if isinstance(m, BlockFHTLinear)]
+    todo = [m for m in modules
+            if m._cached_weight is None and m.residual_base_weight is None and m.spectral_core is None]
+    groups: dict[tuple, list[BlockFHTLinear]] = {}
+    for m in todo:
+        lat = m.generator.latent
+        # the grouped launch serves 16-bit generators with blocks up to 2^15; the rest go one by one
+        if lat.is_cuda and lat.dtype in (torch.bfloat16, torch.float16) and m.generator.block_size <= 32768:
+            groups.setdefault((lat.device, lat.dtype), []).append(m)
+    with torch.no_grad():
+        for mods in groups.values():
+            raws = _native.fht_forward_grouped(
+                [(m.generator.latent, m.generator.size, m.generator.layers, m.generator.seed, 0, m.generator.size)
+                 for m in mods], flags=_flags())
+            for m, raw in zip(mods, raws):
+                weight = m._compose_weight(raw)
+                if dtype is not None:
+                    weight = weight.to(dtype=dtype)
+                m._cached_weight = weight.detach().requires_grad_(True)
+    for module in modules:
+        module.materialize_weight_cache(dtype=dtype)
 
 
 def flush_block_fht_weight_cache(model: nn.Module) -> None:

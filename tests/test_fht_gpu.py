@@ -191,3 +191,25 @@ def test_large_block_sizes_bf16(nat, logb, layers):
     size = 2 * B + 13
     _check_forward(nat, L, size, layers, 99, 17, size - 3, torch.bfloat16)
     _check_backward(nat, L, size, layers, 99, 17, size - 3, torch.bfloat16)
+
+
+def test_grouped_forward_matches_single_calls(nat):
+    """One grouped launch over generators of different sizes, layers, seeds and slices."""
+    torch.manual_seed(11)
+    specs = [(32768, 3 * 32768 + 5, 3, 1, 0, 3 * 32768 + 5), (5000, 40000, 2, 2, 17, 39999),
+             (100, 7000, 1, 3, 0, 7000), (16384, 2 * 16384, 3, 4, 8, 2 * 16384), (32, 640, 2, 5, 3, 600)]
+    for dt in (torch.bfloat16, torch.float16):
+        items = [(torch.randn(L, device="cuda").to(dt), size, layers, seed, start, stop)
+                 for L, size, layers, seed, start, stop in specs]
+        outs = nat.fht_forward_grouped(items)
+        torch.cuda.synchronize()
+        for (z, size, layers, seed, start, stop), y in zip(items, outs):
+            single = nat.fht_forward(z, size, layers, seed, start, stop)
+            assert torch.equal(y, single)
+
+
+def test_grouped_forward_more_than_one_launch(nat):
+    items = [(torch.randn(2000, device="cuda").bfloat16(), 9000, 3, s, 0, 9000) for s in range(130)]
+    outs = nat.fht_forward_grouped(items)
+    for (z, size, layers, seed, start, stop), y in zip(items, outs):
+        assert torch.equal(y, nat.fht_forward(z, size, layers, seed, start, stop))

@@ -1,0 +1,87 @@
+"""BlockFHTLinear on the GPU against the oracle and the reference's golden outputs."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_l2
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def test_linear_forward_backward_matches_golden(native_lib, golden):
+    from latent_weight_lab import BlockFHTLinear
+
+    layer = BlockFHTLinear(96, 40, bias=False, latent_dim=300, layers=3, seed=5, weight_scale=0.5).cuda()
+    with torch.no_grad():
+        layer.generator.latent.copy_(torch.from_numpy(golden["lin2_latent"]))
+    x = torch.from_numpy(golden["lin2_x"]).cuda().requires_grad_(True)
+    y = layer(x)
+    y.backward(torch.from_numpy(golden["lin2_grad_y"]).cuda())
+    assert rel_l2(y.detach().cpu().numpy(), golden["lin2_out"]) < 1e-5
+    assert rel_l2(x.grad.cpu().numpy(), golden["lin2_grad_x"]) < 1e-5
+    assert rel_l2(layer.generator.latent.grad.cpu().numpy(), golden["lin2_grad_latent"]) < 1e-5
+
+
+def test_small_linear_with_bias_matches_golden(native_lib, golden):
+    from latent_weight_lab import BlockFHTLinear
+
+    layer = BlockFHTLinear(5, 3, bias=True, latent_dim=8, layers=2, seed=11).cuda()
+    with torch.no_grad():
+        layer.generator.latent.copy_(torch.from_numpy(golden["lin_latent"]))
+        layer.bias.copy_(torch.from_numpy(golden["lin_bias"]))
+    out = layer(torch.from_numpy(golden["lin_x"]).cuda())
+    assert np.allclose(out.detach().cpu().numpy(), golden["lin_out"], atol=1e-6)
+    assert np.allclose(layer.weight.detach().cpu().numpy(), golden["lin_weight"], atol=1e-7)
+
+
+@pytest.mark.parametrize("dtype, tol", [(torch.float32, 1e-5), (torch.bfloat16, 1e-2), (torch.float16, 1e-2)])
+def test_gpt_shaped_linear_against_oracle(native_lib, dtype, tol):
+    """768 -> 3072 with a 32768-value latent (blocks straddle weight rows)."""
+    from latent_weight_lab import BlockFHTLinear
+
+    torch.manual_seed(0)
+    layer = BlockFHTLinear(768, 3072, latent_dim=32768, layers=3, seed=7).cuda().to(dtype)
+    x = torch.randn(64, 768, device="cuda", dtype=dtype, requires_grad=True)
+    y = layer(x)
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    z = layer.generator.latent.detach().float().cpu().numpy()
+    ref_y = orc.linear_forward(x.detach().float().cpu().numpy(), z, 3072, 3, 7)
+    assert rel_l2(y.detach().float().cpu().numpy(), ref_y) < tol
+    gx, gz, _ = orc.linear_backward(gy.float().cpu().numpy(), x.detach().float().cpu().numpy(), z, 3072, 3, 7)
+    assert rel_l2(x.grad.float().cpu().numpy(), gx) < tol
+    assert rel_l2(layer.generator.latent.grad.float().cpu().numpy(), gz) < tol
+
+
+def test_forward_fused_and_weight_cache(native_lib):
+    from latent_weight_lab import (BlockFHTLinear, flush_block_fht_weight_cache, prepare_block_fht_weight_cache)
+
+    torch.manual_seed(123)
+    dyn = BlockFHTLinear(8, 6, bias=True, latent_dim=32, layers=2, seed=99, output_gain=True).cuda()
+    cached = BlockFHTLinear(8, 6, bias=True, latent_dim=32, layers=2, seed=99, output_gain=True).cuda()
+    cached.load_state_dict(dyn.state_dict())
+    with torch.no_grad():
+        dyn.output_gain.copy_(torch.linspace(0.5, 1.5, 6))
+        cached.output_gain.copy_(torch.linspace(0.5, 1.5, 6))
+    x = torch.randn(11, 8, device="cuda")
+    assert torch.allclose(dyn.forward_fused(x), dyn(x), atol=2e-5)
+    dyn(x).square().mean().backward()
+    prepare_block_fht_weight_cache(cached)
+    cached(x).square().mean().backward()
+    flush_block_fht_weight_cache(cached)
+    assert torch.allclose(cached.generator.latent.grad, dyn.generator.latent.grad, atol=1e-6)
+    assert torch.allclose(cached.output_gain.grad, dyn.output_gain.grad, atol=1e-6)
+
+
+def test_grouped_weight_cache_bf16(native_lib):
+    from latent_weight_lab import BlockFHTLinear, prepare_block_fht_weight_cache
+
+    torch.manual_seed(1)
+    model = torch.nn.Sequential(*[BlockFHTLinear(768, 768, latent_dim=5898, layers=3, seed=s) for s in range(6)])
+    model = model.cuda().bfloat16()
+    prepare_block_fht_weight_cache(model)
+    for m in model:
+        assert torch.equal(m._cached_weight.detach(), m.weight.detach())

@@ -104,6 +104,30 @@ int lwl_fht_backward(int dtype, const void* grad_out, int64_t latent_size, int64
                      int layers, uint64_t seed, int64_t start, int64_t stop, void* grad_latent,
                      void* workspace, size_t workspace_bytes, unsigned flags, void* stream);
 
+/* Workspace for lwl_linear_forward: 16 bytes; its first int is a device
+ * error word, 0 after a successful call (1 = a bounded pipeline wait gave up). */
+size_t lwl_linear_forward_workspace_bytes(void);
+
+/* y[tokens, out_features] (bf16) = x[tokens, in_features] (bf16) @ (weight_scale * W)^T,
+ * W = the generator's first in*out coordinates viewed as [out, in], generated
+ * on chip: each CTA regenerates its 128-row weight panel with the tensor-core
+ * transform, keeps it in tensor memory as the tcgen05.mma A operand and
+ * streams x tiles by TMA.  Supported: bf16, in_features % 64 == 0 and <= 768,
+ * out_features % 128 == 0, padded block size <= 2^15; otherwise
+ * LWL_ERR_UNSUPPORTED (callers then generate W and use a library GEMM).
+ * Replaces: pybind `linear_forward` (csrc/block_fht_ext.cpp:52-67),
+ * block_fht_linear_forward_cuda (csrc/block_fht_ext_cuda.cu:624-681), whose
+ * kernel requires block % in_features == 0 and block <= 16384. */
+int lwl_linear_forward(int dtype, const void* x, int64_t tokens, int64_t in_features, const void* latent,
+                       int64_t latent_size, int64_t out_features, int layers, uint64_t seed, float weight_scale,
+                       void* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Dense-weight variant of the same tcgen05 pipeline: y = x @ w^T with a given
+ * bf16 w[out_features, in_features] (same shape limits).  No reference
+ * counterpart; it isolates the MMA pipeline from the generator for testing. */
+int lwl_tc_linear_dense(const void* x, int64_t tokens, int64_t in_features, const void* w, int64_t out_features,
+                        void* y, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Number of kernel launches one lwl_fht_forward (backward = 0) or
  * lwl_fht_backward (backward = 1) call with these arguments enqueues; -1 on
  * invalid arguments.  No reference counterpart (the reference launches

@@ -6,6 +6,7 @@
 // widened here down to 2^0 (the reference's CPU path accepts any size).
 #include <cstdarg>
 #include <cstdio>
+#include <cstdint>
 #include <cstring>
 
 #include "fht_engine.h"
@@ -231,6 +232,77 @@ int lwl_fht_forward_grouped(int dtype, int count, const lwl_fht_forward_desc* de
     int rc = lwl_fht_forward(dtype, q.latent, q.latent_size, q.size, q.layers, q.seed, q.start, q.stop, q.out,
                              nullptr, 0, flags, stream);
     if (rc) return rc;
+  }
+  return LWL_OK;
+}
+
+size_t lwl_linear_forward_workspace_bytes(void) { return 16; }
+
+static int linear_common(bool gen, int dtype, const void* x, int64_t T, int64_t K, int64_t N, const void* latent,
+                         int64_t L, int layers, void* y, void* ws, size_t ws_bytes) {
+  if (dtype != LWL_BF16) {
+    lwl::set_error("the tcgen05 linear supports bf16 only");
+    return LWL_ERR_UNSUPPORTED;
+  }
+  if (T <= 0 || K <= 0 || N <= 0 || T > INT32_MAX || K > INT32_MAX || N > INT32_MAX) {
+    lwl::set_error("tokens, in_features and out_features must be positive");
+    return LWL_ERR_INVALID;
+  }
+  if (gen) {
+    int st = lwl::validate_fht(dtype, L, K * N, layers, 0, K * N);
+    if (st) return st;
+  }
+  if (!x || !y || (gen && !latent)) {
+    lwl::set_error("null data pointer");
+    return LWL_ERR_INVALID;
+  }
+  if (!lwl::tc_linear_supported((int)K, (int)N, (int)T) || (gen && lwl::next_pow2(L) > 32768) ||
+      (reinterpret_cast<uintptr_t>(x) & 15)) {
+    lwl::set_error("shape outside the tcgen05 linear (in %% 64 == 0, in <= 768, out %% 128 == 0, block <= 2^15)");
+    return LWL_ERR_UNSUPPORTED;
+  }
+  if (!ws || ws_bytes < 16) {
+    lwl::set_error("workspace of 16 bytes required");
+    return LWL_ERR_WORKSPACE;
+  }
+  return LWL_OK;
+}
+
+int lwl_linear_forward(int dtype, const void* x, int64_t tokens, int64_t in_features, const void* latent,
+                       int64_t latent_size, int64_t out_features, int layers, uint64_t seed, float weight_scale,
+                       void* y, void* workspace, size_t workspace_bytes, void* stream) {
+  lwl::g_err[0] = 0;
+  int st = linear_common(true, dtype, x, tokens, in_features, out_features, latent, latent_size, layers, y, workspace,
+                         workspace_bytes);
+  if (st) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  LWL_CUDA_TRY(cudaMemsetAsync(workspace, 0, 16, s));
+  int rc = lwl::tc_linear_launch(true, x, (int)tokens, (int)in_features, (int)out_features, latent, latent_size,
+                                 layers, seed, weight_scale, nullptr, y, reinterpret_cast<int*>(workspace), s);
+  if (rc) {
+    lwl::set_error("tcgen05 linear launch failed (%d): %s", rc, cudaGetErrorString(cudaGetLastError()));
+    return LWL_ERR_CUDA;
+  }
+  return LWL_OK;
+}
+
+int lwl_tc_linear_dense(const void* x, int64_t tokens, int64_t in_features, const void* w, int64_t out_features,
+                        void* y, void* workspace, size_t workspace_bytes, void* stream) {
+  lwl::g_err[0] = 0;
+  int st = linear_common(false, LWL_BF16, x, tokens, in_features, out_features, nullptr, 1, 1, y, workspace,
+                         workspace_bytes);
+  if (st) return st;
+  if (!w) {
+    lwl::set_error("null weight pointer");
+    return LWL_ERR_INVALID;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  LWL_CUDA_TRY(cudaMemsetAsync(workspace, 0, 16, s));
+  int rc = lwl::tc_linear_launch(false, x, (int)tokens, (int)in_features, (int)out_features, nullptr, 1, 1, 0, 1.0f,
+                                 w, y, reinterpret_cast<int*>(workspace), s);
+  if (rc) {
+    lwl::set_error("tcgen05 linear launch failed (%d): %s", rc, cudaGetErrorString(cudaGetLastError()));
+    return LWL_ERR_CUDA;
   }
   return LWL_OK;
 }

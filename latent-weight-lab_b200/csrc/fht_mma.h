@@ -30,4 +30,9 @@ bool mma_lo_supported(int dtype, int n, unsigned flags);
 int mma_lo_grid(const TileParams& p);
 int mma_lo_launch(int dtype, const TileParams& p, int grid, cudaStream_t st);
 
+// tcgen05 BlockFHTLinear forward (linear_tc.cu).
+bool tc_linear_supported(int K, int N, int T);
+int tc_linear_launch(bool gen, const void* x, int T, int K, int N, const void* latent, int64_t L, int layers,
+                     uint64_t seed, float wscale, const void* wdense, void* y, int* err, cudaStream_t st);
+
 }  // namespace lwl

@@ -1,0 +1,429 @@
+// linear_tc.cu -- BlockFHTLinear forward on tcgen05 with the weight generated on chip.
+//
+// y[T, N] = x[T, K] * (scale * W)^T, W = the BlockFHT generator's first N*K
+// coordinates viewed as [N, K] (latent_weight_lab/block_fht.py:283-287, 306-311).
+//
+// One work item = a panel of 128 weight rows [n0, n0+128) x a range of
+// 128-token tiles.  Per item the CTA
+//   1. generates the 2^15-coordinate generator tiles that cover the panel with
+//      the tensor-core FHT runs (fht_mma_core.cuh), stages each tile's part of
+//      the panel in shared memory with a padded row pitch, and stores it into
+//      tensor memory as the MMA A operand (128 lanes = weight rows, two bf16 per
+//      32-bit column along K);
+//   2. streams x tiles [128 tokens x 64] by TMA (128-byte swizzle, 4-stage
+//      mbarrier ring; no multicast) and issues tcgen05.mma (M=128 weight rows,
+//      N=128 tokens, K=16) from one thread, accumulating y^T in tensor memory;
+//   3. drains the accumulator with four epilogue warps (one per TMEM lane
+//      quadrant) straight to y.
+// The generated weight never leaves the SM.  Tensor memory: A uses K/2
+// columns (K <= 768), the accumulator 128 columns at 384.
+//
+// The dense variant (GEN = false) loads a given bf16 W panel instead of
+// generating it; it runs the same MMA pipeline and is used to validate it.
+#include <cuda.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "fht_mma_core.cuh"
+#include "tc_ptx.cuh"
+
+namespace lwl {
+namespace fmma {
+
+constexpr int kLinThreads = 512;
+constexpr int kStages = 4;
+constexpr int kStageBytes = 128 * 64 * 2;  // 128 tokens x 64 K bf16
+constexpr int kMaxK = 768;
+constexpr int kDCol = 384;                 // accumulator columns [384, 512)
+constexpr int kStageOff = kB * 2;          // TMA stages reuse the first exchange buffer (1024-aligned)
+constexpr int kPanelStageOff = 2 * kB * 2; // padded panel staging (second exchange buffer, extended)
+constexpr int kPanelStageBytes = 82944;    // >= rows-per-tile x (K + 8) x 2 (at most ~74 KB) for every supported K
+constexpr int kSwOff = kPanelStageOff + kPanelStageBytes;
+constexpr size_t kLinSmem = kSwOff + 4 * kWordsPad * 4 + 1024;  // + alignment slack
+
+struct LinParams {
+  const void* latent;
+  const void* wdense;  // dense variant: bf16 [N, K]
+  void* y;             // bf16 [T, N]
+  int* err;
+  int64_t L;
+  int n, layers;
+  uint32_t seed32;
+  float corr, wscale;
+  int K, N, T;
+  int panels, tsplit, tpt;  // items = panels * tsplit; token tiles per item
+};
+
+// Final run (pass A) of one generator tile, written into the padded panel
+// staging: the panel rows this tile touches, starting at panel row
+// `row_base`, at pitch K+8 elements (16-byte row offset so that threads
+// reading different rows hit different bank groups).  A tile touches at most
+// 32768/K + 1 rows, i.e. <= 73,872 bytes for every supported K.
+__device__ __forceinline__ void final_to_panel(const Frags& f, uint32_t in_base, const uint32_t* sw, float scale,
+                                               uint16_t* stage, int64_t tile_coord0, int64_t panel_lo,
+                                               int64_t panel_hi, int row_base, int K, int w, int lane, int g,
+                                               int t) {
+  uint32_t o[8][4];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    float c[8];
+    final_tile(f, in_base, w, k, lane, c);
+    o[k][0] = pack_out<__nv_bfloat16>(c[0] * scale, c[1] * scale);
+    o[k][1] = pack_out<__nv_bfloat16>(c[2] * scale, c[3] * scale);
+    o[k][2] = pack_out<__nv_bfloat16>(c[4] * scale, c[5] * scale);
+    o[k][3] = pack_out<__nv_bfloat16>(c[6] * scale, c[7] * scale);
+    sign_acc<0>(o[k], sw, w, k, g, t);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t sel = h ? 0x7632u : 0x5410u;
+      const int p = dep_a(w, 0, g + 8 * (j & 1), 2 * t + h + 8 * (j >> 1));
+      const int64_t f0 = tile_coord0 + p;  // 8 consecutive coordinates, never straddling a row (K % 8 == 0)
+      if (f0 >= panel_lo && f0 < panel_hi) {
+        const int64_t rel = f0 - panel_lo;
+        const int row = (int)(rel / K), col = (int)(rel - (int64_t)row * K);
+        const int srow = row - row_base;
+        uint32_t v0 = prmt(o[0][j], o[1][j], sel), v1 = prmt(o[2][j], o[3][j], sel);
+        uint32_t v2 = prmt(o[4][j], o[5][j], sel), v3 = prmt(o[6][j], o[7][j], sel);
+        *reinterpret_cast<uint4*>(stage + (size_t)srow * (K + 8) + col) = make_uint4(v0, v1, v2, v3);
+      }
+    }
+  }
+}
+
+template <bool GEN>
+__global__ void __launch_bounds__(kLinThreads, 1)
+    linear_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ LinParams P) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  // 1024-byte aligned base: the swizzled TMA stages and descriptors assume 1024-byte atoms
+  unsigned char* smem = smem_raw + ((1024 - ((uint32_t)__cvta_generic_to_shared(smem_raw) & 1023)) & 1023);
+  uint16_t* zbuf = reinterpret_cast<uint16_t*>(smem);
+  uint16_t* xbuf = reinterpret_cast<uint16_t*>(smem + kStageOff);
+  uint16_t* pstage = reinterpret_cast<uint16_t*>(smem + kPanelStageOff);
+  uint32_t* sw = reinterpret_cast<uint32_t*>(smem + kSwOff);
+  __shared__ __align__(8) uint64_t bars[2 * kStages + 2];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ float red[kLinThreads / 32];
+  __shared__ int k0_sh, abort_sh;
+
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
+  const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(&bars[0]);
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (kStages + s); };
+  const uint32_t dfull = bar0 + 8u * (2 * kStages), dempty = bar0 + 8u * (2 * kStages + 1);
+
+  if (w == 0) tc::tmem_alloc((uint32_t)__cvta_generic_to_shared(&tmem_base_sh), 512);
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      tc::mbar_init(full_bar(s), 1);
+      tc::mbar_init(empty_bar(s), 1);
+    }
+    tc::mbar_init(dfull, 1);
+    tc::mbar_init(dempty, 128);
+    tc::mbar_fence_init();
+    abort_sh = 0;
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  const int K = P.K, KC = K / 64;
+
+  // scaled fp16 latent copy, once per CTA (every panel comes from the same generator)
+  const int n = P.n, layers = P.layers, Bm = (1 << n) - 1;
+  int k0 = 0;
+  if (GEN) {
+    const __nv_bfloat16* latent = reinterpret_cast<const __nv_bfloat16*>(P.latent);
+    float ss = 0.0f;
+    for (int64_t i = tid; i < P.L; i += kLinThreads) {
+      float v = __bfloat162float(latent[i]);
+      ss += v * v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[w] = ss;
+    __syncthreads();
+    if (tid == 0) {
+      float s = 0.0f;
+      for (int i = 0; i < kLinThreads / 32; ++i) s += red[i];
+      s *= (float)(kB >> n);
+      int e = 0;
+      if (s > 0.0f) {
+        frexpf(sqrtf(s), &e);
+        e -= 12;
+      }
+      k0_sh = e;
+    }
+    __syncthreads();
+    k0 = k0_sh;
+    const float in_scale = ldexpf(1.0f, -k0);
+    const bool first_is_b = (layers != 2);
+    for (int c = tid; c < kB / 8; c += kLinThreads) {
+      const int p0 = 8 * c, q0 = p0 & Bm;
+      uint32_t hv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float a = (q0 + 2 * e < P.L) ? __bfloat162float(latent[q0 + 2 * e]) * in_scale : 0.0f;
+        float b = (q0 + 2 * e + 1 < P.L) ? __bfloat162float(latent[q0 + 2 * e + 1]) * in_scale : 0.0f;
+        hv[e] = pack_h2(a, b);
+      }
+      if (first_is_b) {
+        *reinterpret_cast<uint4*>(zbuf + lay_ab(p0)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) zbuf[lay_ba(p0 + e)] = (uint16_t)(hv[e >> 1] >> (16 * (e & 1)));
+      }
+    }
+  }
+  const uint32_t zb = (uint32_t)__cvta_generic_to_shared(zbuf);
+  const uint32_t xb = (uint32_t)__cvta_generic_to_shared(xbuf);
+  const uint32_t yb = (uint32_t)__cvta_generic_to_shared(smem + kPanelStageOff);
+  const float out_scale = ldexpf(1.0f, k0) * P.corr * P.wscale;
+  const int ntok_tiles = (P.T + 127) / 128;
+  const uint32_t idesc = tc::idesc_bf16(128, 128);
+  // per-role pipeline state (each role is always the same thread / warps)
+  uint32_t prod_it = 0, mma_it = 0, tcount = 0;
+
+  for (int item = blockIdx.x; item < P.panels * P.tsplit; item += gridDim.x) {
+    const int panel = item / P.tsplit, split = item - panel * P.tsplit;
+    const int n0 = panel * 128;
+    const int tt0 = split * P.tpt, tt1 = min(ntok_tiles, tt0 + P.tpt);
+    __syncthreads();  // previous item fully drained (accumulator read, stages idle)
+
+    // ---- 1. weight panel -> tensor memory (A operand) ----
+    const int q = w & 3, cgi = w >> 2;  // TMEM lane quadrant and column group of this warp
+    const uint32_t a_lane = tmem + ((uint32_t)(32 * q) << 16);
+    const int m = 32 * q + lane;        // panel row owned by this thread in the copy
+    if (GEN) {
+      const int64_t panel_lo = (int64_t)n0 * K, panel_hi = panel_lo + (int64_t)128 * K;
+      const int64_t ct_first = panel_lo >> kLog, ct_last = (panel_hi - 1) >> kLog;
+      for (int64_t ct = ct_first; ct <= ct_last; ++ct) {
+        __syncthreads();
+        for (int i = tid; i < (layers + 1) * kWords; i += kLinThreads) {
+          int l = i / kWords, wd = i - l * kWords;
+          const int p = 32 * wd;
+          sw[l * kWordsPad + spad(wd)] =
+              sign_word(block_layer_key(P.seed32, (ct << (kLog - n)) + (p >> n), l), (p & Bm) >> 5);
+        }
+        __syncthreads();
+        Frags f;
+        make_frags(f, g, t, n);
+        const uint32_t* fsw = sw + layers * kWordsPad;
+        if (layers == 1) {
+          run<1, false, true>(f, zb, xb, sw, nullptr, w, lane, g, t);
+        } else if (layers == 2) {
+          run<0, false, true>(f, zb, yb, sw, nullptr, w, lane, g, t);
+          __syncthreads();
+          run<1, true, false>(f, yb, xb, nullptr, sw + 1 * kWordsPad, w, lane, g, t);
+        } else {
+          run<1, false, true>(f, zb, xb, sw, nullptr, w, lane, g, t);
+          __syncthreads();
+          run<0, true, false>(f, xb, yb, nullptr, sw + 1 * kWordsPad, w, lane, g, t);
+          __syncthreads();
+          run<1, true, false>(f, yb, xb, nullptr, sw + 2 * kWordsPad, w, lane, g, t);
+        }
+        __syncthreads();
+        const int64_t tile_lo = ct << kLog;
+        const int64_t seg_lo = max(tile_lo, panel_lo), seg_hi = min(tile_lo + kB, panel_hi);
+        const int row_base = (int)((seg_lo - panel_lo) / K);  // first panel row this tile touches
+        final_to_panel(f, xb, fsw, out_scale, pstage, tile_lo, panel_lo, panel_hi, row_base, K, w, lane, g, t);
+        __syncthreads();
+        // rows of this tile: copy their parts into TMEM, keeping what other tiles wrote
+        const int64_t my_lo = panel_lo + (int64_t)m * K;  // this lane's row [my_lo, my_lo + K)
+        for (int c8 = cgi; c8 < K / 8; c8 += 4) {
+          const int64_t f0 = my_lo + 8 * c8;
+          const bool mine = f0 >= seg_lo && f0 + 8 <= seg_hi;
+          uint32_t v[4];
+          asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];\n"
+                       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                       : "r"(a_lane + 4 * c8));
+          asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+          if (mine) {
+            uint4 s4 = *reinterpret_cast<const uint4*>(pstage + (size_t)(m - row_base) * (K + 8) + 8 * c8);
+            v[0] = s4.x;
+            v[1] = s4.y;
+            v[2] = s4.z;
+            v[3] = s4.w;
+          }
+          tc::tmem_st4(a_lane + 4 * c8, v[0], v[1], v[2], v[3]);
+        }
+        tc::tmem_wait_st();
+      }
+    } else {
+      const __nv_bfloat16* W = reinterpret_cast<const __nv_bfloat16*>(P.wdense);
+      for (int c8 = cgi; c8 < K / 8; c8 += 4) {
+        uint4 s4 = make_uint4(0, 0, 0, 0);
+        if (n0 + m < P.N) s4 = *reinterpret_cast<const uint4*>(W + (size_t)(n0 + m) * K + 8 * c8);
+        tc::tmem_st4(a_lane + 4 * c8, s4.x, s4.y, s4.z, s4.w);
+      }
+      tc::tmem_wait_st();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+
+    // ---- 2./3. MMA pipeline over this item's token tiles ----
+    if (tid == 0) {  // TMA producer
+      // the stages reuse a buffer the transform wrote through the generic proxy
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      for (int tt = tt0; tt < tt1 && !abort_sh; ++tt) {
+        for (int c = 0; c < KC; ++c, ++prod_it) {
+          const int s = prod_it % kStages;
+          const uint32_t ph = (prod_it / kStages) & 1;
+          if (!tc::mbar_wait(empty_bar(s), ph ^ 1)) {
+            abort_sh = 1;
+            atomicExch(P.err, 1);
+            break;
+          }
+          tc::mbar_expect_tx(full_bar(s), kStageBytes);
+          tc::tma_load_2d(xb + s * kStageBytes, &tmx, c * 64, tt * 128, full_bar(s));
+        }
+      }
+    } else if (tid == 32) {  // MMA issuer
+      for (int tt = tt0; tt < tt1 && !abort_sh; ++tt, ++tcount) {
+        if (!tc::mbar_wait(dempty, (tcount & 1) ^ 1)) {
+          abort_sh = 1;
+          atomicExch(P.err, 1);
+          break;
+        }
+        tc::tc_fence_after();
+        for (int c = 0; c < KC; ++c, ++mma_it) {
+          const int s = mma_it % kStages;
+          const uint32_t ph = (mma_it / kStages) & 1;
+          if (!tc::mbar_wait(full_bar(s), ph)) {
+            abort_sh = 1;
+            atomicExch(P.err, 1);
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t sbase = xb + s * kStageBytes;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            tc::mma_ts(tmem + kDCol, tmem + (uint32_t)(c * 32 + kk * 8), tc::smem_desc_k128(sbase + 32 * kk), idesc,
+                       (c > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc::mma_commit(empty_bar(s));  // frees the stage when these MMAs finish
+        }
+        tc::mma_commit(dfull);  // accumulator complete
+      }
+    } else if (w >= 4 && w < 8) {  // epilogue: warp w drains TMEM lanes 32*(w-4) ..
+      const int qe = w - 4;
+      const int nrow = n0 + 32 * qe + lane;  // output feature of this thread
+      __nv_bfloat16* Y = reinterpret_cast<__nv_bfloat16*>(P.y);
+      for (int tt = tt0; tt < tt1 && !abort_sh; ++tt, ++tcount) {
+        if (!tc::mbar_wait(dfull, tcount & 1)) {
+          abort_sh = 1;
+          atomicExch(P.err, 1);
+          break;
+        }
+        tc::tc_fence_after();
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t r[32];
+          tc::tmem_ld32(tmem + ((uint32_t)(32 * qe) << 16) + kDCol + 32 * cc, r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int tok = tt * 128 + 32 * cc + i;
+            if (tok < P.T && nrow < P.N) Y[(size_t)tok * P.N + nrow] = __float2bfloat16_rn(__uint_as_float(r[i]));
+          }
+        }
+        tc::tc_fence_before();
+        tc::mbar_arrive(dempty);
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  if (w == 0) tc::tmem_dealloc(tmem, 512);
+}
+
+}  // namespace fmma
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+}  // namespace
+
+bool tc_linear_supported(int K, int N, int T) {
+  return K % 64 == 0 && K >= 64 && K <= fmma::kMaxK && N % 128 == 0 && N > 0 && T > 0;
+}
+
+int tc_linear_launch(bool gen, const void* x, int T, int K, int N, const void* latent, int64_t L, int layers,
+                     uint64_t seed, float wscale, const void* wdense, void* y, int* err, cudaStream_t st) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return -2;
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)T};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return -3;
+  fmma::LinParams P;
+  std::memset(&P, 0, sizeof(P));
+  P.latent = latent;
+  P.wdense = wdense;
+  P.y = y;
+  P.err = err;
+  P.L = L;
+  P.n = gen ? ilog2(next_pow2(L)) : 15;
+  P.layers = layers;
+  P.seed32 = fold_seed(seed);
+  P.corr = gen ? (float)std::pow(fmma::layer_correction(P.n), layers) : 1.0f;
+  P.wscale = wscale;
+  P.K = K;
+  P.N = N;
+  P.T = T;
+  P.panels = N / 128;
+  const int ntok = (T + 127) / 128;
+  int sms = fmma::sm_count();
+  P.tsplit = std::max(1, std::min(ntok, sms / std::max(1, P.panels)));
+  P.tpt = (ntok + P.tsplit - 1) / P.tsplit;
+  P.tsplit = (ntok + P.tpt - 1) / P.tpt;
+  const int items = P.panels * P.tsplit;
+  const int grid = std::min(items, sms);
+  if (gen) {
+    static bool attr = false;
+    if (!attr) {
+      if (cudaFuncSetAttribute(fmma::linear_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)fmma::kLinSmem) != cudaSuccess)
+        return -1;
+      attr = true;
+    }
+    fmma::linear_tc_kernel<true><<<grid, fmma::kLinThreads, fmma::kLinSmem, st>>>(map, P);
+  } else {
+    static bool attr = false;
+    if (!attr) {
+      if (cudaFuncSetAttribute(fmma::linear_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)fmma::kLinSmem) != cudaSuccess)
+        return -1;
+      attr = true;
+    }
+    fmma::linear_tc_kernel<false><<<grid, fmma::kLinThreads, fmma::kLinSmem, st>>>(map, P);
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace lwl

@@ -50,6 +50,12 @@ def _declare(lib: ctypes.CDLL) -> None:
         fn.argtypes = [ci, i64, i64, ci, i64, i64, cu]
     lib.lwl_fht_forward_grouped.restype = ci
     lib.lwl_fht_forward_grouped.argtypes = [ci, ci, ctypes.POINTER(ForwardDesc), cu, vp]
+    lib.lwl_linear_forward_workspace_bytes.restype = sz
+    lib.lwl_linear_forward_workspace_bytes.argtypes = []
+    lib.lwl_linear_forward.restype = ci
+    lib.lwl_linear_forward.argtypes = [ci, vp, i64, i64, vp, i64, i64, ci, u64, ctypes.c_float, vp, vp, sz, vp]
+    lib.lwl_tc_linear_dense.restype = ci
+    lib.lwl_tc_linear_dense.argtypes = [vp, i64, i64, vp, i64, vp, vp, sz, vp]
     lib.lwl_fht_launch_count.restype = ci
     lib.lwl_fht_launch_count.argtypes = [ci, i64, i64, ci, i64, i64, ci, cu]
     for name in ("lwl_fht_forward", "lwl_fht_backward"):
@@ -211,3 +217,42 @@ def fht_forward_grouped(items, flags: int = 0) -> list[torch.Tensor]:
     with torch.cuda.device(dev):
         _check(lib.lwl_fht_forward_grouped(dtype_code(dt), len(items), descs, int(flags), _stream_ptr(dev)))
     return outs
+
+
+def linear_forward(x2d: torch.Tensor, latent: torch.Tensor, out_features: int, layers: int, seed: int,
+                   weight_scale: float = 1.0, return_status: bool = False):
+    """Fused tcgen05 forward y = x @ (scale * W)^T with W generated on chip.
+
+    Returns None when the shape is outside the fused kernel (the caller then
+    generates W and uses a library GEMM).  With return_status the device error
+    word tensor is returned too (0 = every pipeline wait completed).
+    """
+    _require_cuda(x2d, "input")
+    lib = load()
+    x2d = x2d.contiguous()
+    latent = latent.detach().contiguous()
+    T, K = x2d.shape
+    y = torch.empty(T, int(out_features), dtype=x2d.dtype, device=x2d.device)
+    ws = torch.empty(lib.lwl_linear_forward_workspace_bytes(), dtype=torch.uint8, device=x2d.device)
+    with torch.cuda.device(x2d.device):
+        st = lib.lwl_linear_forward(dtype_code(x2d.dtype), x2d.data_ptr(), T, K, latent.data_ptr(), latent.numel(),
+                                    int(out_features), int(layers), _seed_u64(seed), float(weight_scale),
+                                    y.data_ptr(), ws.data_ptr(), ws.numel(), _stream_ptr(x2d.device))
+    if st == 2:
+        return None
+    _check(st)
+    return (y, ws.view(torch.int32)[:1]) if return_status else y
+
+
+def tc_linear_dense(x2d: torch.Tensor, w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """y = x @ w^T on the tcgen05 linear pipeline (bf16); returns (y, device error word)."""
+    lib = load()
+    x2d, w = x2d.contiguous(), w.contiguous()
+    T, K = x2d.shape
+    N = w.shape[0]
+    y = torch.empty(T, N, dtype=x2d.dtype, device=x2d.device)
+    ws = torch.empty(16, dtype=torch.uint8, device=x2d.device)
+    with torch.cuda.device(x2d.device):
+        _check(lib.lwl_tc_linear_dense(x2d.data_ptr(), T, K, w.data_ptr(), N, y.data_ptr(), ws.data_ptr(), 16,
+                                       _stream_ptr(x2d.device)))
+    return y, ws.view(torch.int32)[:1]

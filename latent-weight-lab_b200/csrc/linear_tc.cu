@@ -10,13 +10,15 @@
 //      the panel in shared memory with a padded row pitch, and stores it into
 //      tensor memory as the MMA A operand (128 lanes = weight rows, two bf16 per
 //      32-bit column along K);
-//   2. streams x tiles [128 tokens x 64] by TMA (128-byte swizzle, 4-stage
+//   2. streams x tiles [64 tokens x 64] by TMA (128-byte swizzle, 8-stage
 //      mbarrier ring; no multicast) and issues tcgen05.mma (M=128 weight rows,
-//      N=128 tokens, K=16) from one thread, accumulating y^T in tensor memory;
-//   3. drains the accumulator with four epilogue warps (one per TMEM lane
-//      quadrant) straight to y.
+//      N=64 tokens, K=16) from one thread into one of two tensor-memory
+//      accumulators, so the next tile's MMAs overlap the previous drain;
+//   3. drains an accumulator with four epilogue warps (one per TMEM lane
+//      quadrant) into a shared-memory output tile that one thread writes to
+//      y with a TMA store.
 // The generated weight never leaves the SM.  Tensor memory: A uses K/2
-// columns (K <= 768), the accumulator 128 columns at 384.
+// columns (K <= 768), the accumulators 2 x 64 columns at 384.
 //
 // The dense variant (GEN = false) loads a given bf16 W panel instead of
 // generating it; it runs the same MMA pipeline and is used to validate it.
@@ -32,10 +34,12 @@ namespace lwl {
 namespace fmma {
 
 constexpr int kLinThreads = 512;
-constexpr int kStages = 4;
-constexpr int kStageBytes = 128 * 64 * 2;  // 128 tokens x 64 K bf16
+constexpr int kStages = 8;
+constexpr int kTT = 64;                     // tokens per MMA tile (N of the MMA)
+constexpr int kStageBytes = kTT * 64 * 2;   // 64 tokens x 64 K bf16
+constexpr int kYStageBytes = kTT * 128 * 2; // one output tile [64 tokens x 128 features] bf16
 constexpr int kMaxK = 768;
-constexpr int kDCol = 384;                 // accumulator columns [384, 512)
+constexpr int kDCol = 384;                 // two accumulators: columns [384, 448) and [448, 512)
 constexpr int kStageOff = kB * 2;          // TMA stages reuse the first exchange buffer (1024-aligned)
 constexpr int kPanelStageOff = 2 * kB * 2; // padded panel staging (second exchange buffer, extended)
 constexpr int kPanelStageBytes = 82944;    // >= rows-per-tile x (K + 8) x 2 (at most ~74 KB) for every supported K
@@ -96,7 +100,8 @@ __device__ __forceinline__ void final_to_panel(const Frags& f, uint32_t in_base,
 
 template <bool GEN>
 __global__ void __launch_bounds__(kLinThreads, 1)
-    linear_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ LinParams P) {
+    linear_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmy,
+                     const __grid_constant__ LinParams P) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   // 1024-byte aligned base: the swizzled TMA stages and descriptors assume 1024-byte atoms
   unsigned char* smem = smem_raw + ((1024 - ((uint32_t)__cvta_generic_to_shared(smem_raw) & 1023)) & 1023);
@@ -104,7 +109,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   uint16_t* xbuf = reinterpret_cast<uint16_t*>(smem + kStageOff);
   uint16_t* pstage = reinterpret_cast<uint16_t*>(smem + kPanelStageOff);
   uint32_t* sw = reinterpret_cast<uint32_t*>(smem + kSwOff);
-  __shared__ __align__(8) uint64_t bars[2 * kStages + 2];
+  __shared__ __align__(8) uint64_t bars[2 * kStages + 4];
   __shared__ uint32_t tmem_base_sh;
   __shared__ float red[kLinThreads / 32];
   __shared__ int k0_sh, abort_sh;
@@ -113,7 +118,8 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(&bars[0]);
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
   auto empty_bar = [&](int s) { return bar0 + 8u * (kStages + s); };
-  const uint32_t dfull = bar0 + 8u * (2 * kStages), dempty = bar0 + 8u * (2 * kStages + 1);
+  auto dfull = [&](int b) { return bar0 + 8u * (2 * kStages + b); };
+  auto dempty = [&](int b) { return bar0 + 8u * (2 * kStages + 2 + b); };
 
   if (w == 0) tc::tmem_alloc((uint32_t)__cvta_generic_to_shared(&tmem_base_sh), 512);
   if (tid == 0) {
@@ -121,8 +127,10 @@ __global__ void __launch_bounds__(kLinThreads, 1)
       tc::mbar_init(full_bar(s), 1);
       tc::mbar_init(empty_bar(s), 1);
     }
-    tc::mbar_init(dfull, 1);
-    tc::mbar_init(dempty, 128);
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(dfull(b), 1);
+      tc::mbar_init(dempty(b), 128);
+    }
     tc::mbar_fence_init();
     abort_sh = 0;
   }
@@ -182,8 +190,8 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   const uint32_t xb = (uint32_t)__cvta_generic_to_shared(xbuf);
   const uint32_t yb = (uint32_t)__cvta_generic_to_shared(smem + kPanelStageOff);
   const float out_scale = ldexpf(1.0f, k0) * P.corr * P.wscale;
-  const int ntok_tiles = (P.T + 127) / 128;
-  const uint32_t idesc = tc::idesc_bf16(128, 128);
+  const int ntok_tiles = (P.T + kTT - 1) / kTT;
+  const uint32_t idesc = tc::idesc_bf16(128, kTT);
   // per-role pipeline state (each role is always the same thread / warps)
   uint32_t prod_it = 0, mma_it = 0, tcount = 0;
 
@@ -279,17 +287,20 @@ __global__ void __launch_bounds__(kLinThreads, 1)
             break;
           }
           tc::mbar_expect_tx(full_bar(s), kStageBytes);
-          tc::tma_load_2d(xb + s * kStageBytes, &tmx, c * 64, tt * 128, full_bar(s));
+          tc::tma_load_2d(xb + s * kStageBytes, &tmx, c * 64, tt * kTT, full_bar(s));
         }
       }
     } else if (tid == 32) {  // MMA issuer
       for (int tt = tt0; tt < tt1 && !abort_sh; ++tt, ++tcount) {
-        if (!tc::mbar_wait(dempty, (tcount & 1) ^ 1)) {
+        const int b = tcount & 1;
+        const uint32_t dph = (tcount >> 1) & 1;
+        if (!tc::mbar_wait(dempty(b), dph ^ 1)) {
           abort_sh = 1;
           atomicExch(P.err, 1);
           break;
         }
         tc::tc_fence_after();
+        const uint32_t dcol = tmem + kDCol + 64 * b;
         for (int c = 0; c < KC; ++c, ++mma_it) {
           const int s = mma_it % kStages;
           const uint32_t ph = (mma_it / kStages) & 1;
@@ -302,37 +313,45 @@ __global__ void __launch_bounds__(kLinThreads, 1)
           const uint32_t sbase = xb + s * kStageBytes;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            tc::mma_ts(tmem + kDCol, tmem + (uint32_t)(c * 32 + kk * 8), tc::smem_desc_k128(sbase + 32 * kk), idesc,
+            tc::mma_ts(dcol, tmem + (uint32_t)(c * 32 + kk * 8), tc::smem_desc_k128(sbase + 32 * kk), idesc,
                        (c > 0 || kk > 0) ? 1u : 0u);
           }
           tc::mma_commit(empty_bar(s));  // frees the stage when these MMAs finish
         }
-        tc::mma_commit(dfull);  // accumulator complete
+        tc::mma_commit(dfull(b));  // accumulator b complete
       }
     } else if (w >= 4 && w < 8) {  // epilogue: warp w drains TMEM lanes 32*(w-4) ..
-      const int qe = w - 4;
-      const int nrow = n0 + 32 * qe + lane;  // output feature of this thread
-      __nv_bfloat16* Y = reinterpret_cast<__nv_bfloat16*>(P.y);
+      const int qe = w - 4, et = tid - 128;  // 0..127 within the epilogue
+      const int frow = 32 * qe + lane;      // feature (panel row) of this thread
       for (int tt = tt0; tt < tt1 && !abort_sh; ++tt, ++tcount) {
-        if (!tc::mbar_wait(dfull, tcount & 1)) {
+        const int b = tcount & 1;
+        const uint32_t dph = (tcount >> 1) & 1;
+        if (!tc::mbar_wait(dfull(b), dph)) {
           abort_sh = 1;
           atomicExch(P.err, 1);
           break;
         }
         tc::tc_fence_after();
-#pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t r[32];
-          tc::tmem_ld32(tmem + ((uint32_t)(32 * qe) << 16) + kDCol + 32 * cc, r);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int tok = tt * 128 + 32 * cc + i;
-            if (tok < P.T && nrow < P.N) Y[(size_t)tok * P.N + nrow] = __float2bfloat16_rn(__uint_as_float(r[i]));
-          }
-        }
+        uint32_t r0[32], r1[32];
+        tc::tmem_ld32(tmem + ((uint32_t)(32 * qe) << 16) + kDCol + 64 * b, r0);
+        tc::tmem_ld32(tmem + ((uint32_t)(32 * qe) << 16) + kDCol + 64 * b + 32, r1);
         tc::tc_fence_before();
-        tc::mbar_arrive(dempty);
+        tc::mbar_arrive(dempty(b));  // the accumulator can be overwritten now
+        // output tile b in shared memory: [64 tokens][128 features]; wait until
+        // the TMA store that last read this buffer is done
+        if (et == 0) tc::tma_store_wait_read<1>();
+        tc::named_bar(1, 128);
+        __nv_bfloat16* yst = reinterpret_cast<__nv_bfloat16*>(pstage) + b * (kYStageBytes / 2);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          yst[i * 128 + frow] = __float2bfloat16_rn(__uint_as_float(r0[i]));
+          yst[(i + 32) * 128 + frow] = __float2bfloat16_rn(__uint_as_float(r1[i]));
+        }
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        tc::named_bar(1, 128);
+        if (et == 0) tc::tma_store_2d(&tmy, (uint32_t)__cvta_generic_to_shared(yst), n0, tt * kTT);
       }
+      if (et == 0) tc::tma_store_wait_all();  // the next item's transform reuses these buffers
     }
   }
   tc::tc_fence_before();
@@ -372,14 +391,21 @@ int tc_linear_launch(bool gen, const void* x, int T, int K, int N, const void* l
                      uint64_t seed, float wscale, const void* wdense, void* y, int* err, cudaStream_t st) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return -2;
-  CUtensorMap map;
+  CUtensorMap map, ymap;
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)T};
   cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  cuuint32_t box[2] = {64, 128};
+  cuuint32_t box[2] = {64, (cuuint32_t)fmma::kTT};
   cuuint32_t estr[2] = {1, 1};
   if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return -3;
+  cuuint64_t ydims[2] = {(cuuint64_t)N, (cuuint64_t)T};
+  cuuint64_t ystrides[1] = {(cuuint64_t)N * 2};
+  cuuint32_t ybox[2] = {128, (cuuint32_t)fmma::kTT};
+  if (enc(&ymap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, ydims, ystrides, ybox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+      CUDA_SUCCESS)
     return -3;
   fmma::LinParams P;
   std::memset(&P, 0, sizeof(P));
@@ -397,7 +423,7 @@ int tc_linear_launch(bool gen, const void* x, int T, int K, int N, const void* l
   P.N = N;
   P.T = T;
   P.panels = N / 128;
-  const int ntok = (T + 127) / 128;
+  const int ntok = (T + fmma::kTT - 1) / fmma::kTT;
   int sms = fmma::sm_count();
   P.tsplit = std::max(1, std::min(ntok, sms / std::max(1, P.panels)));
   P.tpt = (ntok + P.tsplit - 1) / P.tsplit;
@@ -412,7 +438,7 @@ int tc_linear_launch(bool gen, const void* x, int T, int K, int N, const void* l
         return -1;
       attr = true;
     }
-    fmma::linear_tc_kernel<true><<<grid, fmma::kLinThreads, fmma::kLinSmem, st>>>(map, P);
+    fmma::linear_tc_kernel<true><<<grid, fmma::kLinThreads, fmma::kLinSmem, st>>>(map, ymap, P);
   } else {
     static bool attr = false;
     if (!attr) {
@@ -421,7 +447,7 @@ int tc_linear_launch(bool gen, const void* x, int T, int K, int N, const void* l
         return -1;
       attr = true;
     }
-    fmma::linear_tc_kernel<false><<<grid, fmma::kLinThreads, fmma::kLinSmem, st>>>(map, P);
+    fmma::linear_tc_kernel<false><<<grid, fmma::kLinThreads, fmma::kLinSmem, st>>>(map, ymap, P);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }

@@ -10,15 +10,17 @@
 //      the panel in shared memory with a padded row pitch, and stores it into
 //      tensor memory as the MMA A operand (128 lanes = weight rows, two bf16 per
 //      32-bit column along K);
-//   2. streams x tiles [64 tokens x 64] by TMA (128-byte swizzle, 8-stage
-//      mbarrier ring; no multicast) and issues tcgen05.mma (M=128 weight rows,
-//      N=64 tokens, K=16) from one thread into one of two tensor-memory
-//      accumulators, so the next tile's MMAs overlap the previous drain;
-//   3. drains an accumulator with four epilogue warps (one per TMEM lane
-//      quadrant) into a shared-memory output tile that one thread writes to
-//      y with a TMA store.
+//   2. streams x tiles [128 tokens x 64] by TMA (128-byte swizzle, 8-stage
+//      mbarrier ring over the latent copy and first exchange buffer, which the
+//      next item rebuilds; no multicast) and issues tcgen05.mma (M=128 weight
+//      rows, N=128 tokens, K=16) from one warp -- one elected lane issues,
+//      the converged warp waits -- into tensor-memory accumulators;
+//   3. drains an accumulator with eight epilogue warps (lane quadrant w % 4,
+//      column half) into registers, releases it, and stages the bf16 output
+//      tile in shared memory for a TMA store.
 // The generated weight never leaves the SM.  Tensor memory: A uses K/2
-// columns (K <= 768), the accumulators 2 x 64 columns at 384.
+// columns (K <= 768); two 128-column accumulators follow when K <= 512 (the
+// next tile's MMAs overlap the previous drain), else one.
 //
 // The dense variant (GEN = false) loads a given bf16 W panel instead of
 // generating it; it runs the same MMA pipeline and is used to validate it.
@@ -35,15 +37,17 @@ namespace fmma {
 
 constexpr int kLinThreads = 512;
 constexpr int kStages = 8;
-constexpr int kTT = 64;                     // tokens per MMA tile (N of the MMA)
-constexpr int kStageBytes = kTT * 64 * 2;   // 64 tokens x 64 K bf16
-constexpr int kYStageBytes = kTT * 128 * 2; // one output tile [64 tokens x 128 features] bf16
+constexpr int kTT = 128;                    // tokens per MMA tile (N of the MMA)
+constexpr int kStageBytes = kTT * 64 * 2;   // 128 tokens x 64 K bf16
+constexpr int kYStageBytes = kTT * 128 * 2; // one output tile [128 tokens x 128 features] bf16
 constexpr int kMaxK = 768;
-constexpr int kDCol = 384;                 // two accumulators: columns [384, 448) and [448, 512)
-constexpr int kStageOff = kB * 2;          // TMA stages reuse the first exchange buffer (1024-aligned)
+constexpr int kEpiWarps = 8;                // warps 4..11: lane quadrant w % 4, column half (w - 4) / 4
+constexpr int kStageOff = 0;                // TMA stages reuse the latent copy and the first exchange buffer
 constexpr int kPanelStageOff = 2 * kB * 2; // padded panel staging (second exchange buffer, extended)
 constexpr int kPanelStageBytes = 82944;    // >= rows-per-tile x (K + 8) x 2 (at most ~74 KB) for every supported K
 constexpr int kSwOff = kPanelStageOff + kPanelStageBytes;
+static_assert(kStages * kStageBytes <= 2 * kB * 2, "x stages must fit the latent copy + first exchange buffer");
+static_assert(2 * kYStageBytes <= kPanelStageBytes, "two output tiles must fit the panel staging");
 constexpr size_t kLinSmem = kSwOff + 4 * kWordsPad * 4 + 1024;  // + alignment slack
 
 struct LinParams {
@@ -129,7 +133,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(dfull(b), 1);
-      tc::mbar_init(dempty(b), 128);
+      tc::mbar_init(dempty(b), 32 * kEpiWarps);
     }
     tc::mbar_fence_init();
     abort_sh = 0;
@@ -140,7 +144,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   const uint32_t tmem = tmem_base_sh;
   const int K = P.K, KC = K / 64;
 
-  // scaled fp16 latent copy, once per CTA (every panel comes from the same generator)
+  // input scale exponent, once per CTA (every panel comes from the same generator)
   const int n = P.n, layers = P.layers, Bm = (1 << n) - 1;
   int k0 = 0;
   if (GEN) {
@@ -167,31 +171,17 @@ __global__ void __launch_bounds__(kLinThreads, 1)
     }
     __syncthreads();
     k0 = k0_sh;
-    const float in_scale = ldexpf(1.0f, -k0);
-    const bool first_is_b = (layers != 2);
-    for (int c = tid; c < kB / 8; c += kLinThreads) {
-      const int p0 = 8 * c, q0 = p0 & Bm;
-      uint32_t hv[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float a = (q0 + 2 * e < P.L) ? __bfloat162float(latent[q0 + 2 * e]) * in_scale : 0.0f;
-        float b = (q0 + 2 * e + 1 < P.L) ? __bfloat162float(latent[q0 + 2 * e + 1]) * in_scale : 0.0f;
-        hv[e] = pack_h2(a, b);
-      }
-      if (first_is_b) {
-        *reinterpret_cast<uint4*>(zbuf + lay_ab(p0)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) zbuf[lay_ba(p0 + e)] = (uint16_t)(hv[e >> 1] >> (16 * (e & 1)));
-      }
-    }
   }
   const uint32_t zb = (uint32_t)__cvta_generic_to_shared(zbuf);
-  const uint32_t xb = (uint32_t)__cvta_generic_to_shared(xbuf);
+  const uint32_t xb = (uint32_t)__cvta_generic_to_shared(xbuf);           // x stages
+  const uint32_t eb = (uint32_t)__cvta_generic_to_shared(smem + kB * 2);  // first exchange buffer
   const uint32_t yb = (uint32_t)__cvta_generic_to_shared(smem + kPanelStageOff);
   const float out_scale = ldexpf(1.0f, k0) * P.corr * P.wscale;
   const int ntok_tiles = (P.T + kTT - 1) / kTT;
   const uint32_t idesc = tc::idesc_bf16(128, kTT);
+  // accumulators after the K/2 columns of A: two when they fit, else one
+  const int nd = (K / 2 <= 512 - 2 * kTT) ? 2 : 1;
+  const uint32_t dbase = 512 - nd * kTT;
   // per-role pipeline state (each role is always the same thread / warps)
   uint32_t prod_it = 0, mma_it = 0, tcount = 0;
 
@@ -201,6 +191,28 @@ __global__ void __launch_bounds__(kLinThreads, 1)
     const int tt0 = split * P.tpt, tt1 = min(ntok_tiles, tt0 + P.tpt);
     __syncthreads();  // previous item fully drained (accumulator read, stages idle)
 
+    if (GEN) {
+      // scaled fp16 latent copy (the x stages of the previous item overwrote it)
+      const __nv_bfloat16* latent = reinterpret_cast<const __nv_bfloat16*>(P.latent);
+      const float in_scale = ldexpf(1.0f, -k0);
+      const bool first_is_b = (layers != 2);
+      for (int c = tid; c < kB / 8; c += kLinThreads) {
+        const int p0 = 8 * c, q0 = p0 & Bm;
+        uint32_t hv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float a = (q0 + 2 * e < P.L) ? __bfloat162float(latent[q0 + 2 * e]) * in_scale : 0.0f;
+          float b = (q0 + 2 * e + 1 < P.L) ? __bfloat162float(latent[q0 + 2 * e + 1]) * in_scale : 0.0f;
+          hv[e] = pack_h2(a, b);
+        }
+        if (first_is_b) {
+          *reinterpret_cast<uint4*>(zbuf + lay_ab(p0)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) zbuf[lay_ba(p0 + e)] = (uint16_t)(hv[e >> 1] >> (16 * (e & 1)));
+        }
+      }
+    }
     // ---- 1. weight panel -> tensor memory (A operand) ----
     const int q = w & 3, cgi = w >> 2;  // TMEM lane quadrant and column group of this warp
     const uint32_t a_lane = tmem + ((uint32_t)(32 * q) << 16);
@@ -221,23 +233,23 @@ __global__ void __launch_bounds__(kLinThreads, 1)
         make_frags(f, g, t, n);
         const uint32_t* fsw = sw + layers * kWordsPad;
         if (layers == 1) {
-          run<1, false, true>(f, zb, xb, sw, nullptr, w, lane, g, t);
+          run<1, false, true>(f, zb, eb, sw, nullptr, w, lane, g, t);
         } else if (layers == 2) {
           run<0, false, true>(f, zb, yb, sw, nullptr, w, lane, g, t);
           __syncthreads();
-          run<1, true, false>(f, yb, xb, nullptr, sw + 1 * kWordsPad, w, lane, g, t);
+          run<1, true, false>(f, yb, eb, nullptr, sw + 1 * kWordsPad, w, lane, g, t);
         } else {
-          run<1, false, true>(f, zb, xb, sw, nullptr, w, lane, g, t);
+          run<1, false, true>(f, zb, eb, sw, nullptr, w, lane, g, t);
           __syncthreads();
-          run<0, true, false>(f, xb, yb, nullptr, sw + 1 * kWordsPad, w, lane, g, t);
+          run<0, true, false>(f, eb, yb, nullptr, sw + 1 * kWordsPad, w, lane, g, t);
           __syncthreads();
-          run<1, true, false>(f, yb, xb, nullptr, sw + 2 * kWordsPad, w, lane, g, t);
+          run<1, true, false>(f, yb, eb, nullptr, sw + 2 * kWordsPad, w, lane, g, t);
         }
         __syncthreads();
         const int64_t tile_lo = ct << kLog;
         const int64_t seg_lo = max(tile_lo, panel_lo), seg_hi = min(tile_lo + kB, panel_hi);
         const int row_base = (int)((seg_lo - panel_lo) / K);  // first panel row this tile touches
-        final_to_panel(f, xb, fsw, out_scale, pstage, tile_lo, panel_lo, panel_hi, row_base, K, w, lane, g, t);
+        final_to_panel(f, eb, fsw, out_scale, pstage, tile_lo, panel_lo, panel_hi, row_base, K, w, lane, g, t);
         __syncthreads();
         // rows of this tile: copy their parts into TMEM, keeping what other tiles wrote
         const int64_t my_lo = panel_lo + (int64_t)m * K;  // this lane's row [my_lo, my_lo + K)
@@ -290,42 +302,47 @@ __global__ void __launch_bounds__(kLinThreads, 1)
           tc::tma_load_2d(xb + s * kStageBytes, &tmx, c * 64, tt * kTT, full_bar(s));
         }
       }
-    } else if (tid == 32) {  // MMA issuer
-      for (int tt = tt0; tt < tt1 && !abort_sh; ++tt, ++tcount) {
-        const int b = tcount & 1;
-        const uint32_t dph = (tcount >> 1) & 1;
-        if (!tc::mbar_wait(dempty(b), dph ^ 1)) {
+    } else if (w == 1) {  // MMA issuer: the whole warp runs the loop, one elected lane issues
+      for (int tt = tt0; tt < tt1 && !__any_sync(0xffffffffu, abort_sh); ++tt, ++tcount) {
+        const int b = nd == 2 ? (int)(tcount & 1) : 0;
+        const uint32_t dph = (nd == 2 ? (tcount >> 1) : tcount) & 1;
+        if (!__all_sync(0xffffffffu, tc::mbar_wait(dempty(b), dph ^ 1))) {
           abort_sh = 1;
           atomicExch(P.err, 1);
           break;
         }
         tc::tc_fence_after();
-        const uint32_t dcol = tmem + kDCol + 64 * b;
+        const uint32_t dcol = tmem + dbase + kTT * b;
         for (int c = 0; c < KC; ++c, ++mma_it) {
           const int s = mma_it % kStages;
           const uint32_t ph = (mma_it / kStages) & 1;
-          if (!tc::mbar_wait(full_bar(s), ph)) {
+          if (!__all_sync(0xffffffffu, tc::mbar_wait(full_bar(s), ph))) {
             abort_sh = 1;
             atomicExch(P.err, 1);
             break;
           }
           tc::tc_fence_after();
           const uint32_t sbase = xb + s * kStageBytes;
+          if (tc::elect_one()) {
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            tc::mma_ts(dcol, tmem + (uint32_t)(c * 32 + kk * 8), tc::smem_desc_k128(sbase + 32 * kk), idesc,
-                       (c > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk) {
+              tc::mma_ts(dcol, tmem + (uint32_t)(c * 32 + kk * 8), tc::smem_desc_k128(sbase + 32 * kk), idesc,
+                         (c > 0 || kk > 0) ? 1u : 0u);
+            }
+            tc::mma_commit(empty_bar(s));  // frees the stage when these MMAs finish
           }
-          tc::mma_commit(empty_bar(s));  // frees the stage when these MMAs finish
+          __syncwarp();
         }
-        tc::mma_commit(dfull(b));  // accumulator b complete
+        if (tc::elect_one()) tc::mma_commit(dfull(b));  // accumulator b complete
+        __syncwarp();
       }
-    } else if (w >= 4 && w < 8) {  // epilogue: warp w drains TMEM lanes 32*(w-4) ..
-      const int qe = w - 4, et = tid - 128;  // 0..127 within the epilogue
-      const int frow = 32 * qe + lane;      // feature (panel row) of this thread
+    } else if (w >= 4 && w < 4 + kEpiWarps) {
+      // epilogue: warp w drains TMEM lanes 32*(w%4).. and accumulator columns 64*h..64*h+63
+      const int qe = w & 3, h = (w - 4) >> 2, et = tid - 128;  // et: 0..255 within the epilogue
+      const int frow = 32 * qe + lane;                           // feature (panel row) of this thread
       for (int tt = tt0; tt < tt1 && !abort_sh; ++tt, ++tcount) {
-        const int b = tcount & 1;
-        const uint32_t dph = (tcount >> 1) & 1;
+        const int b = nd == 2 ? (int)(tcount & 1) : 0;
+        const uint32_t dph = (nd == 2 ? (tcount >> 1) : tcount) & 1;
         if (!tc::mbar_wait(dfull(b), dph)) {
           abort_sh = 1;
           atomicExch(P.err, 1);
@@ -333,23 +350,28 @@ __global__ void __launch_bounds__(kLinThreads, 1)
         }
         tc::tc_fence_after();
         uint32_t r0[32], r1[32];
-        tc::tmem_ld32(tmem + ((uint32_t)(32 * qe) << 16) + kDCol + 64 * b, r0);
-        tc::tmem_ld32(tmem + ((uint32_t)(32 * qe) << 16) + kDCol + 64 * b + 32, r1);
+        const uint32_t dl = tmem + ((uint32_t)(32 * qe) << 16) + dbase + kTT * b + 64 * h;
+        tc::tmem_ld32(dl, r0);
+        tc::tmem_ld32(dl + 32, r1);
         tc::tc_fence_before();
         tc::mbar_arrive(dempty(b));  // the accumulator can be overwritten now
-        // output tile b in shared memory: [64 tokens][128 features]; wait until
-        // the TMA store that last read this buffer is done
+        // output tile in shared memory: [128 tokens][128 features], two buffers;
+        // wait until the TMA store that last read this buffer is done
+        const int yb_i = (int)(tcount & 1);
         if (et == 0) tc::tma_store_wait_read<1>();
-        tc::named_bar(1, 128);
-        __nv_bfloat16* yst = reinterpret_cast<__nv_bfloat16*>(pstage) + b * (kYStageBytes / 2);
+        tc::named_bar(1, 32 * kEpiWarps);
+        __nv_bfloat16* yst = reinterpret_cast<__nv_bfloat16*>(pstage) + yb_i * (kYStageBytes / 2) + 64 * h * 128;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           yst[i * 128 + frow] = __float2bfloat16_rn(__uint_as_float(r0[i]));
           yst[(i + 32) * 128 + frow] = __float2bfloat16_rn(__uint_as_float(r1[i]));
         }
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-        tc::named_bar(1, 128);
-        if (et == 0) tc::tma_store_2d(&tmy, (uint32_t)__cvta_generic_to_shared(yst), n0, tt * kTT);
+        tc::named_bar(1, 32 * kEpiWarps);
+        if (et == 0)
+          tc::tma_store_2d(&tmy, (uint32_t)__cvta_generic_to_shared(reinterpret_cast<__nv_bfloat16*>(pstage) +
+                                                                     yb_i * (kYStageBytes / 2)),
+                           n0, tt * kTT);
       }
       if (et == 0) tc::tma_store_wait_all();  // the next item's transform reuses these buffers
     }

@@ -251,33 +251,38 @@ __global__ void __launch_bounds__(kLinThreads, 1)
         const int row_base = (int)((seg_lo - panel_lo) / K);  // first panel row this tile touches
         final_to_panel(f, eb, fsw, out_scale, pstage, tile_lo, panel_lo, panel_hi, row_base, K, w, lane, g, t);
         __syncthreads();
-        // rows of this tile: copy their parts into TMEM, keeping what other tiles wrote
+        // 64 coordinates (32 tensor-memory columns) of this lane's row per
+        // step: eight independent 16-byte loads, one 32-column store.  A
+        // 64-aligned chunk never straddles a generator tile (K % 64 == 0).
         const int64_t my_lo = panel_lo + (int64_t)m * K;  // this lane's row [my_lo, my_lo + K)
-        for (int c8 = cgi; c8 < K / 8; c8 += 4) {
-          const int64_t f0 = my_lo + 8 * c8;
-          const bool mine = f0 >= seg_lo && f0 + 8 <= seg_hi;
-          uint32_t v[4];
-          asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];\n"
-                       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
-                       : "r"(a_lane + 4 * c8));
-          asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+        for (int c64 = cgi; c64 < K / 64; c64 += 4) {
+          const int64_t f0 = my_lo + 64 * c64;
+          const bool mine = f0 >= seg_lo && f0 + 64 <= seg_hi;
+          uint32_t v[32];
+          if (!__all_sync(0xffffffffu, mine)) tc::tmem_ld32(a_lane + 32 * c64, v);  // keep other tiles' part
           if (mine) {
-            uint4 s4 = *reinterpret_cast<const uint4*>(pstage + (size_t)(m - row_base) * (K + 8) + 8 * c8);
-            v[0] = s4.x;
-            v[1] = s4.y;
-            v[2] = s4.z;
-            v[3] = s4.w;
+            const uint4* src = reinterpret_cast<const uint4*>(pstage + (m - row_base) * (K + 8) + 64 * c64);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const uint4 s4 = src[u];
+              v[4 * u] = s4.x, v[4 * u + 1] = s4.y, v[4 * u + 2] = s4.z, v[4 * u + 3] = s4.w;
+            }
           }
-          tc::tmem_st4(a_lane + 4 * c8, v[0], v[1], v[2], v[3]);
+          tc::tmem_st32(a_lane + 32 * c64, v);
         }
         tc::tmem_wait_st();
       }
     } else {
       const __nv_bfloat16* W = reinterpret_cast<const __nv_bfloat16*>(P.wdense);
-      for (int c8 = cgi; c8 < K / 8; c8 += 4) {
-        uint4 s4 = make_uint4(0, 0, 0, 0);
-        if (n0 + m < P.N) s4 = *reinterpret_cast<const uint4*>(W + (size_t)(n0 + m) * K + 8 * c8);
-        tc::tmem_st4(a_lane + 4 * c8, s4.x, s4.y, s4.z, s4.w);
+      for (int c64 = cgi; c64 < K / 64; c64 += 4) {
+        uint32_t v[32];
+        const uint4* src = reinterpret_cast<const uint4*>(W + (size_t)(n0 + m) * K + 64 * c64);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint4 s4 = n0 + m < P.N ? src[u] : make_uint4(0, 0, 0, 0);
+          v[4 * u] = s4.x, v[4 * u + 1] = s4.y, v[4 * u + 2] = s4.z, v[4 * u + 3] = s4.w;
+        }
+        tc::tmem_st32(a_lane + 32 * c64, v);
       }
       tc::tmem_wait_st();
     }

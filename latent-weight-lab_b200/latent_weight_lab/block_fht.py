@@ -138,12 +138,25 @@ def _generated_weight(latent: torch.Tensor, in_features: int, out_features: int,
 
 def block_fht_linear_forward(input: torch.Tensor, latent: torch.Tensor, out_features: int, layers: int, seed: int,
                              weight_scale: float = 1.0) -> torch.Tensor:
-    """y = input @ (weight_scale * W)^T with W generated from latent, no autograd (block_fht.py:251-288)."""
+    """y = input @ (weight_scale * W)^T with W generated from latent, no autograd (block_fht.py:251-288).
+
+    Like the reference, which takes its fused extension kernel when the shape
+    allows it (block_fht.py:263-281), bf16 inputs with in_features % 64 == 0,
+    in_features <= 768 and out_features % 128 == 0 run the fused tcgen05
+    kernel: each CTA regenerates its weight panel on chip and W never exists in
+    device memory.  Other shapes, dtypes and exact_arithmetic() generate W and
+    use a library GEMM.
+    """
     if input.dim() < 2:
         raise ValueError("input must have at least 2 dimensions")
     in_features = input.shape[-1]
     flat = input.reshape(-1, in_features)
     with torch.no_grad():
+        if (flat.is_cuda and flat.dtype == torch.bfloat16 and latent.dtype == torch.bfloat16 and flat.shape[0] > 0
+                and not _flags()):
+            out = _native.linear_forward(flat, latent, int(out_features), int(layers), int(seed), float(weight_scale))
+            if out is not None:
+                return out.reshape(*input.shape[:-1], int(out_features))
         w = _generated_weight(latent, in_features, out_features, layers, seed, weight_scale)
         out = F.linear(flat, w.to(dtype=flat.dtype))
     return out.reshape(*input.shape[:-1], int(out_features))

@@ -85,3 +85,22 @@ def test_grouped_weight_cache_bf16(native_lib):
     prepare_block_fht_weight_cache(model)
     for m in model:
         assert torch.equal(m._cached_weight.detach(), m.weight.detach())
+
+
+def test_block_fht_linear_forward_takes_fused_kernel_bf16(native_lib):
+    """bf16 768 -> 3072: the drop-in forward runs the fused tcgen05 kernel (bit-identical
+    to a direct call) and matches the oracle within the bf16 tolerance."""
+    from latent_weight_lab import BlockFHTLinear, _native, block_fht_linear_forward
+
+    torch.manual_seed(3)
+    layer = BlockFHTLinear(768, 3072, bias=False, latent_dim=32768, layers=3, seed=21).cuda().bfloat16()
+    x = torch.randn(2, 300, 768, device="cuda", dtype=torch.bfloat16)
+    y = layer.forward_fused(x, weight_scale=0.5)
+    direct = _native.linear_forward(x.reshape(-1, 768), layer.generator.latent, 3072, 3, 21, 0.5)
+    assert direct is not None
+    assert torch.equal(y.reshape(-1, 3072), direct)
+    y2 = block_fht_linear_forward(x, layer.generator.latent, 3072, 3, 21, weight_scale=0.5)
+    assert torch.equal(y, y2)
+    z = layer.generator.latent.detach().float().cpu().numpy()
+    ref = orc.linear_forward(x.reshape(-1, 768).float().cpu().numpy(), z, 3072, 3, 21) * 0.5
+    assert rel_l2(y.reshape(-1, 3072).float().cpu().numpy(), ref) < 1e-2

@@ -423,6 +423,88 @@ def run_sweep(args) -> None:
                 del ws
 
 
+def run_linear(args) -> None:
+    """Fused BlockFHTLinear forward (inference): y = x @ (scale * W)^T with W
+    regenerated on chip by the tcgen05 kernel (lwl_linear_forward), GPT-2
+    fc shape 768 -> 3072, latent 32768 (block size 32768), layers=3, bf16.
+    The same public call is timed against the unfused path of the same
+    function (grouped-capable generation into HBM + cuBLAS), and against the
+    kernel's dense-weight variant (same MMA pipeline, W read from HBM)."""
+    import torch
+    import torch.nn.functional as F
+
+    from latent_weight_lab import BlockFHTLinear, _native, block_fht_linear_forward
+
+    _native.load()
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    T, K, N = args.tokens, 768, 3072
+    layer = BlockFHTLinear(K, N, bias=False, latent_dim=32768, layers=3, seed=7).to(dev, torch.bfloat16)
+    lat = layer.generator.latent.detach()
+    x = torch.randn(T, K, device=dev, dtype=torch.bfloat16)
+
+    def fused():
+        return block_fht_linear_forward(x, lat, N, 3, 7)
+
+    def unfused():
+        w = _native.fht_forward(lat, K * N, 3, 7, 0, K * N).view(N, K)
+        return F.linear(x, w)
+
+    w_dense = _native.fht_forward(lat, K * N, 3, 7, 0, K * N).view(N, K)
+
+    def dense():
+        return _native.tc_linear_dense(x, w_dense)[0]
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / steps
+
+    with torch.no_grad():
+        with ClockSampler(0) as clk:
+            ms = timed(fused, args.steps)
+        ms_unfused = timed(unfused, args.steps)
+        ms_dense = timed(dense, args.steps)
+        # end to end: x from pinned host memory in, y back to pinned host memory, every step
+        x_host = x.cpu().pin_memory()
+        y_host = torch.empty(T, N, dtype=torch.bfloat16).pin_memory()
+
+        def e2e():
+            x.copy_(x_host, non_blocking=True)
+            y_host.copy_(fused(), non_blocking=True)
+
+        ms_e2e = timed(e2e, max(3, args.steps // 4))
+    flops = 2.0 * T * K * N
+    peaks = _peaks()
+    achieved = flops / (ms * 1e-3) / 1e12
+    line = {
+        "metric": "fused BlockFHTLinear forward TFLOP/s (768->3072, latent 32768, layers 3)",
+        "value": achieved, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (x ~N(0,1), latent ~N(0,0.02) reference init)",
+        "config": {"workload": f"fused BlockFHTLinear forward, {T} tokens x 768 -> 3072", "tokens": T,
+                   "generated_weight_bytes_in_hbm": 0,
+                   "l2": "y (T x 3072 bf16) exceeds L2 for T >= 32768; x is re-read from L2 by every panel"},
+        "tokens_per_s": T / (ms * 1e-3),
+        "unfused_ms": ms_unfused, "unfused_tflops": flops / (ms_unfused * 1e-3) / 1e12,
+        "dense_weight_variant_ms": ms_dense,
+        "e2e": {"value": flops / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": T * K * 2, "d2h_bytes_per_step": T * N * 2},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / peaks["bf16_tflops"], "traffic": None, "peak_source": peaks["source"]},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_gpt2(args) -> None:
     """C4: GPT-2-small-shaped decoder inference (12 layers, d=768, 12 heads, seq 1024,
     batch 8, vocab 50257 padded to 50304) with every qkv / attn-proj / fc / fc-proj
@@ -536,11 +618,12 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["fht", "mlp", "sweep", "gpt2"], default="fht")
+    ap.add_argument("--workload", choices=["fht", "mlp", "sweep", "gpt2", "linear"], default="fht")
     ap.add_argument("--latent-mode", choices=["ratio", "literal"], default="ratio")
     ap.add_argument("--min-log", type=int, default=5)
     ap.add_argument("--max-log", type=int, default=23)
     ap.add_argument("--latent", type=int, default=32768, help="latent size for --workload mlp")
+    ap.add_argument("--tokens", type=int, default=32768, help="tokens for --workload linear")
     args = ap.parse_args()
     if args.workload == "mlp":
         run_mlp(args)
@@ -548,6 +631,8 @@ def main() -> None:
         run_sweep(args)
     elif args.workload == "gpt2":
         run_gpt2(args)
+    elif args.workload == "linear":
+        run_linear(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -1,7 +1,7 @@
 """The ctypes shim shown in INTEGRATION.md (reference-side binding) works against the library."""
 from __future__ import annotations
 
-import ctypes
+from pathlib import Path
 
 import pytest
 import torch
@@ -12,55 +12,21 @@ from oracle import oracle as orc
 pytestmark = pytest.mark.gpu
 
 
-class _LwlB200Ext:
-    """Drop-in for the reference's pybind module, backed by liblwl_b200.so."""
-    _codes = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
-
-    def __init__(self, path):
-        lib = ctypes.CDLL(path)
-        i64, u64, vp, sz, ci, cu = (ctypes.c_int64, ctypes.c_uint64, ctypes.c_void_p,
-                                    ctypes.c_size_t, ctypes.c_int, ctypes.c_uint)
-        for n in ("lwl_fht_forward", "lwl_fht_backward"):
-            getattr(lib, n).argtypes = [ci, vp, i64, i64, ci, u64, i64, i64, vp, vp, sz, cu, vp]
-        for n in ("lwl_fht_forward_workspace_bytes", "lwl_fht_backward_workspace_bytes"):
-            getattr(lib, n).restype = sz
-            getattr(lib, n).argtypes = [ci, i64, i64, ci, i64, i64, cu]
-        lib.lwl_last_error.restype = ctypes.c_char_p
-        self.lib = lib
-
-    def _call(self, fn, wsfn, x, L, size, layers, seed, start, stop, out):
-        code = self._codes[x.dtype]
-        nbytes = wsfn(code, L, size, layers, start, stop, 0)
-        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
-        st = fn(code, x.data_ptr(), L, size, layers, seed & (2**64 - 1), start, stop, out.data_ptr(),
-                ws.data_ptr(), nbytes, 0, torch.cuda.current_stream(x.device).cuda_stream)
-        if st:
-            raise RuntimeError(self.lib.lwl_last_error().decode())
-        return out
-
-    # block_fht_ext.cpp:28-38 -> returns [y]
-    def forward(self, latent, output_size, layers, seed, start, stop):
-        out = torch.empty(stop - start, dtype=latent.dtype, device=latent.device)
-        return [self._call(self.lib.lwl_fht_forward, self.lib.lwl_fht_forward_workspace_bytes,
-                           latent.contiguous(), latent.numel(), output_size, layers, seed, start, stop, out)]
-
-    # block_fht_ext.cpp:40-50 -> grad_latent
-    def backward(self, grad_out, latent_size, output_size, layers, seed, start, stop):
-        out = torch.empty(latent_size, dtype=grad_out.dtype, device=grad_out.device)
-        return self._call(self.lib.lwl_fht_backward, self.lib.lwl_fht_backward_workspace_bytes,
-                          grad_out.contiguous(), latent_size, output_size, layers, seed, start, stop, out)
-
-    # block_fht_ext.cpp:52-67 -> y = x @ (scale * W)^T; W generated by the library, GEMM by cuBLAS
-    def linear_forward(self, x2d, latent, out_features, layers, seed, weight_scale):
-        size = x2d.shape[1] * out_features
-        w = self.forward(latent, size, layers, seed, 0, size)[0].view(out_features, x2d.shape[1])
-        return torch.nn.functional.linear(x2d, w * weight_scale)
+def _shim_class():
+    """Execute the ctypes shim exactly as INTEGRATION.md prints it."""
+    text = (Path(__file__).resolve().parents[1] / "INTEGRATION.md").read_text()
+    sec = text[text.index("## Reference-side binding"):]
+    code = sec[sec.index("```python") + len("```python"):]
+    code = code[:code.index("```")]
+    ns: dict = {}
+    exec(compile(code, "INTEGRATION.md", "exec"), ns)
+    return ns["_LwlB200Ext"]
 
 
 def test_shim_matches_oracle(native_lib):
     from latent_weight_lab import _native
 
-    ext = _LwlB200Ext(str(_native.library_path()))
+    ext = _shim_class()(str(_native.library_path()))
     torch.manual_seed(0)
     z = torch.randn(1024, device="cuda")
     y = ext.forward(z, 108618, 3, 123, 0, 108618)[0]
@@ -72,3 +38,18 @@ def test_shim_matches_oracle(native_lib):
     x = torch.randn(5, 8, device="cuda")
     out = ext.linear_forward(x, torch.randn(32, device="cuda"), 6, 2, 9, 0.5)
     assert out.shape == (5, 6)
+
+
+def test_shim_fused_linear_bf16(native_lib):
+    """bf16 768 -> 3072 goes through lwl_linear_forward and matches the oracle."""
+    from latent_weight_lab import _native
+
+    ext = _shim_class()(str(_native.library_path()))
+    torch.manual_seed(1)
+    x = torch.randn(200, 768, device="cuda").bfloat16()
+    z = (torch.randn(32768) * 0.02).bfloat16()
+    y = ext.linear_forward(x, z.cuda(), 3072, 3, 4, 0.5)
+    direct = _native.linear_forward(x, z.cuda(), 3072, 3, 4, 0.5)
+    assert torch.equal(y, direct)
+    ref = orc.linear_forward(x.float().cpu().numpy(), z.float().numpy(), 3072, 3, 4, 0.5)
+    assert rel_l2(y.float().cpu().numpy(), ref) < 1e-2

@@ -122,6 +122,25 @@ int lwl_linear_forward(int dtype, const void* x, int64_t tokens, int64_t in_feat
                        int64_t latent_size, int64_t out_features, int layers, uint64_t seed, float weight_scale,
                        void* y, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Workspace for lwl_linear_backward: the generated W, grad_W (both [out, in]
+ * in dtype), the transform workspace and 4 MiB for cuBLAS. */
+size_t lwl_linear_backward_workspace_bytes(int dtype, int64_t tokens, int64_t in_features, int64_t out_features,
+                                           int64_t latent_size, int layers, unsigned flags);
+
+/* Backward of y = x @ (weight_scale * W)^T (fp32 / bf16 / fp16, all tensors of
+ * one dtype, row-major, contiguous):
+ *   grad_x[tokens, in]  = weight_scale * grad_y @ W          (skipped if grad_x is NULL)
+ *   grad_latent[latent] = weight_scale * J^T (grad_y^T @ x)   (skipped if grad_latent is NULL)
+ * W is regenerated into the workspace; the two products are plain cuBLAS
+ * GEMMs (fp32 accumulation); J^T is lwl_fht_backward over all in*out
+ * coordinates.  The bias gradient and the modulation terms stay with the
+ * caller.  Replaces: _BlockFHTLinearFn.backward (latent_weight_lab/block_fht.py:322-356);
+ * the reference's pybind module has no linear backward. */
+int lwl_linear_backward(int dtype, const void* x, const void* grad_y, int64_t tokens, int64_t in_features,
+                        int64_t out_features, const void* latent, int64_t latent_size, int layers, uint64_t seed,
+                        float weight_scale, void* grad_x, void* grad_latent, void* workspace, size_t workspace_bytes,
+                        unsigned flags, void* stream);
+
 /* Dense-weight variant of the same tcgen05 pipeline: y = x @ w^T with a given
  * bf16 w[out_features, in_features] (same shape limits).  No reference
  * counterpart; it isolates the MMA pipeline from the generator for testing. */

@@ -59,7 +59,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if changed or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
         cuda = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
         cmd = [nvcc, *ARCH, "-shared", "-cudart", "shared", "-o", str(LIB), *map(str, objs),
-               "-Xlinker", f"-rpath,{cuda / 'lib64'}"]
+               "-lcublas", "-Xlinker", f"-rpath,{cuda / 'lib64'}"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

@@ -4,10 +4,12 @@
 // failures: slice bounds and layer range (latent_weight_lab/block_fht.py:92-93,
 // :609-610; csrc/block_fht_ext_cuda.cu:523-529), block-size range 2^5..2^23 is
 // widened here down to 2^0 (the reference's CPU path accepts any size).
+#include <cublas_v2.h>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdint>
 #include <cstring>
+#include <algorithm>
 
 #include "fht_engine.h"
 #include "fht_mma.h"
@@ -132,6 +134,56 @@ static size_t fht_ws(bool backward, int dtype, int64_t L, int64_t size, int laye
 
 }  // namespace lwl
 
+namespace {
+
+// Linear backward workspace: [W (grad_x) | grad_W (grad_latent) | transform
+// workspace | cuBLAS workspace], each 256-byte aligned.
+constexpr size_t kCublasWs = size_t(4) << 20;
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+struct LinBwdPlan {
+  size_t w_off, gw_off, fht_off, cub_off, total;
+};
+
+LinBwdPlan plan_linear_backward(int dtype, int64_t K, int64_t N, int64_t L, int layers, unsigned flags) {
+  const size_t es = dtype == LWL_F32 ? 4 : 2, wbytes = align256((size_t)(K * N) * es);
+  const int64_t size = K * N;
+  const size_t fws = std::max(lwl::fht_ws(false, dtype, L, size, layers, 0, size, flags),
+                              lwl::fht_ws(true, dtype, L, size, layers, 0, size, flags));
+  LinBwdPlan p;
+  p.w_off = 0;
+  p.gw_off = wbytes;
+  p.fht_off = 2 * wbytes;
+  p.cub_off = p.fht_off + align256(fws);
+  p.total = p.cub_off + kCublasWs;
+  return p;
+}
+
+cublasHandle_t cublas_handle() {
+  static thread_local cublasHandle_t h[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!h[dev] && cublasCreate(&h[dev]) != CUBLAS_STATUS_SUCCESS) h[dev] = nullptr;
+  return h[dev];
+}
+
+__global__ void scale_kernel(void* p, int dtype, int64_t n, float s) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    if (dtype == LWL_F32) {
+      reinterpret_cast<float*>(p)[i] *= s;
+    } else if (dtype == LWL_BF16) {
+      __nv_bfloat16* q = reinterpret_cast<__nv_bfloat16*>(p) + i;
+      *q = __float2bfloat16_rn(__bfloat162float(*q) * s);
+    } else {
+      __half* q = reinterpret_cast<__half*>(p) + i;
+      *q = __float2half_rn(__half2float(*q) * s);
+    }
+  }
+}
+
+}  // namespace
+
 extern "C" {
 
 int lwl_version(void) { return 100; }
@@ -232,6 +284,91 @@ int lwl_fht_forward_grouped(int dtype, int count, const lwl_fht_forward_desc* de
     int rc = lwl_fht_forward(dtype, q.latent, q.latent_size, q.size, q.layers, q.seed, q.start, q.stop, q.out,
                              nullptr, 0, flags, stream);
     if (rc) return rc;
+  }
+  return LWL_OK;
+}
+
+size_t lwl_linear_backward_workspace_bytes(int dtype, int64_t tokens, int64_t in_features, int64_t out_features,
+                                           int64_t latent_size, int layers, unsigned flags) {
+  (void)tokens;
+  if (in_features <= 0 || out_features <= 0 || latent_size <= 0) return 0;
+  return plan_linear_backward(dtype, in_features, out_features, latent_size, layers, flags).total;
+}
+
+int lwl_linear_backward(int dtype, const void* x, const void* grad_y, int64_t tokens, int64_t in_features,
+                        int64_t out_features, const void* latent, int64_t latent_size, int layers, uint64_t seed,
+                        float weight_scale, void* grad_x, void* grad_latent, void* workspace, size_t workspace_bytes,
+                        unsigned flags, void* stream) {
+  lwl::g_err[0] = 0;
+  const int64_t T = tokens, K = in_features, N = out_features, size = K * N;
+  if (T < 0 || K <= 0 || N <= 0) {
+    lwl::set_error("tokens must be >= 0, in_features and out_features > 0");
+    return LWL_ERR_INVALID;
+  }
+  int st = lwl::validate_fht(dtype, latent_size, size, layers, 0, size);
+  if (st) return st;
+  if (!grad_x && !grad_latent) return LWL_OK;
+  if (!latent || (T > 0 && (!grad_y || (grad_latent && !x)))) {
+    lwl::set_error("null data pointer");
+    return LWL_ERR_INVALID;
+  }
+  const LinBwdPlan pl = plan_linear_backward(dtype, K, N, latent_size, layers, flags);
+  if (!workspace || workspace_bytes < pl.total) {
+    lwl::set_error("workspace of %zu bytes needed, %zu given", pl.total, workspace_bytes);
+    return LWL_ERR_WORKSPACE;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = reinterpret_cast<char*>(workspace);
+  const size_t fht_bytes = pl.cub_off - pl.fht_off;
+  cublasHandle_t h = cublas_handle();
+  if (!h) {
+    lwl::set_error("cublasCreate failed");
+    return LWL_ERR_CUDA;
+  }
+  if (cublasSetStream(h, s) != CUBLAS_STATUS_SUCCESS ||
+      cublasSetWorkspace(h, ws + pl.cub_off, kCublasWs) != CUBLAS_STATUS_SUCCESS) {
+    lwl::set_error("cuBLAS stream / workspace setup failed");
+    return LWL_ERR_CUDA;
+  }
+  const cudaDataType_t dt = dtype == LWL_F32 ? CUDA_R_32F : dtype == LWL_BF16 ? CUDA_R_16BF : CUDA_R_16F;
+  const float one = 1.0f, zero = 0.0f;
+  // row-major [r, c] is column-major [c x r]
+  if (grad_x) {
+    if (T > 0) {
+      // W = generator's first N*K coordinates, [N, K]
+      st = lwl::fht_call(false, dtype, latent, ws + pl.w_off, latent_size, size, layers, seed, 0, size,
+                         ws + pl.fht_off, fht_bytes, flags, stream);
+      if (st) return st;
+      // grad_x[T, K] = scale * grad_y[T, N] @ W[N, K]  (block_fht.py:330-337)
+      if (cublasGemmEx(h, CUBLAS_OP_N, CUBLAS_OP_N, (int)K, (int)T, (int)N, &weight_scale, ws + pl.w_off, dt,
+                       (int)K, grad_y, dt, (int)N, &zero, grad_x, dt, (int)K, CUBLAS_COMPUTE_32F,
+                       CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS) {
+        lwl::set_error("cublasGemmEx (grad_x) failed");
+        return LWL_ERR_CUDA;
+      }
+    }
+  }
+  if (grad_latent) {
+    if (T == 0) {
+      LWL_CUDA_TRY(cudaMemsetAsync(grad_latent, 0, (size_t)latent_size * (dtype == LWL_F32 ? 4 : 2), s));
+      return LWL_OK;
+    }
+    // grad_W[N, K] = grad_y^T[N, T] @ x[T, K]  (block_fht.py:339-341)
+    if (cublasGemmEx(h, CUBLAS_OP_N, CUBLAS_OP_T, (int)K, (int)N, (int)T, &one, x, dt, (int)K, grad_y, dt, (int)N,
+                     &zero, ws + pl.gw_off, dt, (int)K, CUBLAS_COMPUTE_32F,
+                     CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS) {
+      lwl::set_error("cublasGemmEx (grad_W) failed");
+      return LWL_ERR_CUDA;
+    }
+    // grad_latent = scale * J^T grad_W  (block_fht.py:342-348)
+    st = lwl::fht_call(true, dtype, ws + pl.gw_off, grad_latent, latent_size, size, layers, seed, 0, size,
+                       ws + pl.fht_off, fht_bytes, flags, stream);
+    if (st) return st;
+    if (weight_scale != 1.0f) {
+      scale_kernel<<<(int)std::min<int64_t>((latent_size + 255) / 256, 1024), 256, 0, s>>>(grad_latent, dtype,
+                                                                                         latent_size, weight_scale);
+      LWL_CUDA_TRY(cudaGetLastError());
+    }
   }
   return LWL_OK;
 }

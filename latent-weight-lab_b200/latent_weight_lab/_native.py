@@ -54,6 +54,11 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.lwl_linear_forward_workspace_bytes.argtypes = []
     lib.lwl_linear_forward.restype = ci
     lib.lwl_linear_forward.argtypes = [ci, vp, i64, i64, vp, i64, i64, ci, u64, ctypes.c_float, vp, vp, sz, vp]
+    lib.lwl_linear_backward_workspace_bytes.restype = sz
+    lib.lwl_linear_backward_workspace_bytes.argtypes = [ci, i64, i64, i64, i64, ci, cu]
+    lib.lwl_linear_backward.restype = ci
+    lib.lwl_linear_backward.argtypes = [ci, vp, vp, i64, i64, i64, vp, i64, ci, u64, ctypes.c_float, vp, vp, vp, sz,
+                                        cu, vp]
     lib.lwl_tc_linear_dense.restype = ci
     lib.lwl_tc_linear_dense.argtypes = [vp, i64, i64, vp, i64, vp, vp, sz, vp]
     lib.lwl_fht_launch_count.restype = ci
@@ -242,6 +247,33 @@ def linear_forward(x2d: torch.Tensor, latent: torch.Tensor, out_features: int, l
         return None
     _check(st)
     return (y, ws.view(torch.int32)[:1]) if return_status else y
+
+
+def linear_backward(x2d: torch.Tensor, grad_y2d: torch.Tensor, latent: torch.Tensor, out_features: int,
+                    layers: int, seed: int, weight_scale: float = 1.0, need_input: bool = True,
+                    need_latent: bool = True, flags: int = 0):
+    """Backward of y = x @ (scale * W)^T through lwl_linear_backward: returns
+    (grad_x or None, grad_latent or None), both in the input dtype."""
+    _require_cuda(x2d, "input")
+    lib = load()
+    x2d, grad_y2d, latent = x2d.contiguous(), grad_y2d.contiguous(), latent.detach().contiguous()
+    if not (x2d.dtype == grad_y2d.dtype == latent.dtype):
+        raise ValueError("input, grad_output and latent must have one dtype")
+    T, K = x2d.shape
+    code = dtype_code(x2d.dtype)
+    gx = torch.empty_like(x2d) if need_input else None
+    gz = torch.empty_like(latent) if need_latent else None
+    nbytes = lib.lwl_linear_backward_workspace_bytes(code, T, K, int(out_features), latent.numel(), int(layers),
+                                                     flags)
+    ws, _ = _workspace(nbytes, x2d.device)
+    with torch.cuda.device(x2d.device):
+        _check(lib.lwl_linear_backward(code, x2d.data_ptr(), grad_y2d.data_ptr(), T, K, int(out_features),
+                                       latent.data_ptr(), latent.numel(), int(layers), _seed_u64(seed),
+                                       float(weight_scale), gx.data_ptr() if gx is not None else None,
+                                       gz.data_ptr() if gz is not None else None,
+                                       ws.data_ptr() if ws is not None else None, nbytes, flags,
+                                       _stream_ptr(x2d.device)))
+    return gx, gz
 
 
 def tc_linear_dense(x2d: torch.Tensor, w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:

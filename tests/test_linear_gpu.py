@@ -104,3 +104,38 @@ def test_block_fht_linear_forward_takes_fused_kernel_bf16(native_lib):
     z = layer.generator.latent.detach().float().cpu().numpy()
     ref = orc.linear_forward(x.reshape(-1, 768).float().cpu().numpy(), z, 3072, 3, 21) * 0.5
     assert rel_l2(y.reshape(-1, 3072).float().cpu().numpy(), ref) < 1e-2
+
+
+@pytest.mark.parametrize("dtype, tol, K, N, L, scale", [(torch.float32, 1e-5, 96, 40, 300, 0.5),
+                                                       (torch.float32, 1e-5, 768, 384, 40000, 1.0),
+                                                       (torch.bfloat16, 1e-2, 768, 3072, 32768, 0.25),
+                                                       (torch.float16, 1e-2, 256, 512, 5000, 1.0)])
+def test_linear_backward_capi_matches_oracle(native_lib, dtype, tol, K, N, L, scale):
+    """lwl_linear_backward (regenerated W, cuBLAS products, transform backward) against the
+    oracle's _BlockFHTLinearFn.backward restatement."""
+    from latent_weight_lab import _native
+
+    torch.manual_seed(K + N)
+    T = 129
+    x = torch.randn(T, K, device="cuda").to(dtype)
+    gy = torch.randn(T, N, device="cuda").to(dtype)
+    z = (torch.randn(L, device="cuda") * 0.05).to(dtype)
+    gx, gz = _native.linear_backward(x, gy, z, N, 3, 17, weight_scale=scale)
+    rx, rz, _ = orc.linear_backward(gy.float().cpu().numpy(), x.float().cpu().numpy(), z.float().cpu().numpy(),
+                                    N, 3, 17, scale)
+    assert rel_l2(gx.float().cpu().numpy(), rx) < tol
+    assert rel_l2(gz.float().cpu().numpy(), rz) < tol
+    only_x, none_z = _native.linear_backward(x, gy, z, N, 3, 17, weight_scale=scale, need_latent=False)
+    assert none_z is None and torch.equal(only_x, gx)
+    none_x, only_z = _native.linear_backward(x, gy, z, N, 3, 17, weight_scale=scale, need_input=False)
+    assert none_x is None and torch.equal(only_z, gz)
+
+
+def test_linear_backward_capi_zero_tokens(native_lib):
+    from latent_weight_lab import _native
+
+    x = torch.zeros(0, 64, device="cuda")
+    gy = torch.zeros(0, 32, device="cuda")
+    z = torch.randn(100, device="cuda")
+    gx, gz = _native.linear_backward(x, gy, z, 32, 2, 1)
+    assert gx.shape == (0, 64) and torch.count_nonzero(gz) == 0

@@ -505,6 +505,55 @@ def run_linear(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_mix(args) -> None:
+    """FixedFHTMix (reference examples/nanogpt/model.py:200-218) on activations:
+    rows x features bf16 through lwl_fixed_fht_mix; HBM-bound (one read and
+    one write per element).  Default: GPT-2-small c_fc output mix, 65536
+    tokens x 3072 features (P = 4096)."""
+    import torch
+
+    from latent_weight_lab import _native
+    from latent_weight_lab.fht_mix import FixedFHTMix
+
+    _native.load()
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    T, Fe = args.tokens * 2, args.features
+    mix = FixedFHTMix(Fe, 98).to(dev)
+    x = torch.randn(T, Fe, device=dev, dtype=torch.bfloat16)
+    for _ in range(args.warmup):
+        _native.fixed_fht_mix(x, mix.signs)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        a.record()
+        for _ in range(args.steps):
+            _native.fixed_fht_mix(x, mix.signs)
+        b.record()
+        torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    nbytes = 2 * T * Fe * 2
+    peaks = _peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    line = {
+        "metric": "FixedFHTMix GB/s (bf16 activations, read + write)", "value": gbs, "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic x ~N(0,1)",
+        "config": {"workload": f"FixedFHTMix {T} rows x {Fe} features (P = {_native_pow2(Fe)})",
+                   "l2": "input and output each exceed L2"},
+        "rows_per_s": T / (ms * 1e-3),
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"], "traffic": None, "peak_source": peaks["source"]},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _native_pow2(v: int) -> int:
+    return 1 << (int(v) - 1).bit_length()
+
+
 def run_gpt2(args) -> None:
     """C4: GPT-2-small-shaped decoder inference (12 layers, d=768, 12 heads, seq 1024,
     batch 8, vocab 50257 padded to 50304) with every qkv / attn-proj / fc / fc-proj
@@ -618,12 +667,13 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["fht", "mlp", "sweep", "gpt2", "linear"], default="fht")
+    ap.add_argument("--workload", choices=["fht", "mlp", "sweep", "gpt2", "linear", "mix"], default="fht")
     ap.add_argument("--latent-mode", choices=["ratio", "literal"], default="ratio")
     ap.add_argument("--min-log", type=int, default=5)
     ap.add_argument("--max-log", type=int, default=23)
     ap.add_argument("--latent", type=int, default=32768, help="latent size for --workload mlp")
-    ap.add_argument("--tokens", type=int, default=32768, help="tokens for --workload linear")
+    ap.add_argument("--tokens", type=int, default=32768, help="tokens for --workload linear (mix: rows / 2)")
+    ap.add_argument("--features", type=int, default=3072, help="features for --workload mix")
     args = ap.parse_args()
     if args.workload == "mlp":
         run_mlp(args)
@@ -633,6 +683,8 @@ def main() -> None:
         run_gpt2(args)
     elif args.workload == "linear":
         run_linear(args)
+    elif args.workload == "mix":
+        run_mix(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -141,6 +141,16 @@ int lwl_linear_backward(int dtype, const void* x, const void* grad_y, int64_t to
                         float weight_scale, void* grad_x, void* grad_latent, void* workspace, size_t workspace_bytes,
                         unsigned flags, void* stream);
 
+/* FixedFHTMix over the last dimension: for every row r,
+ *   y[r, :features] = (S * H_P / sqrt(P) * S * pad(x[r, :]))[:features],
+ * P = next_pow2(features) <= 8192, S = diag(signs), signs[P] fp32 (+-1) on the
+ * device; x and y [rows, features] row-major in dtype, fp32 arithmetic.  The
+ * map is its own adjoint, so the same call computes the input gradient.
+ * Replaces: FixedFHTMix.forward / normalized_fht_last_dim
+ * (examples/nanogpt/model.py:182-218), a pure-torch op in the reference. */
+int lwl_fixed_fht_mix(int dtype, const void* x, int64_t rows, int64_t features, const float* signs, void* y,
+                      void* stream);
+
 /* Dense-weight variant of the same tcgen05 pipeline: y = x @ w^T with a given
  * bf16 w[out_features, in_features] (same shape limits).  No reference
  * counterpart; it isolates the MMA pipeline from the generator for testing. */

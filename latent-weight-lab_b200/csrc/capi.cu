@@ -17,6 +17,8 @@
 #include "lwl_common.cuh"
 
 namespace lwl {
+int fht_mix_launch(int dtype, const void* x, void* y, const float* signs, int64_t rows, int F, int logP,
+                   cudaStream_t st);
 
 static thread_local char g_err[512];
 
@@ -284,6 +286,34 @@ int lwl_fht_forward_grouped(int dtype, int count, const lwl_fht_forward_desc* de
     int rc = lwl_fht_forward(dtype, q.latent, q.latent_size, q.size, q.layers, q.seed, q.start, q.stop, q.out,
                              nullptr, 0, flags, stream);
     if (rc) return rc;
+  }
+  return LWL_OK;
+}
+
+int lwl_fixed_fht_mix(int dtype, const void* x, int64_t rows, int64_t features, const float* signs, void* y,
+                      void* stream) {
+  lwl::g_err[0] = 0;
+  if (dtype != LWL_F32 && dtype != LWL_BF16 && dtype != LWL_F16) {
+    lwl::set_error("dtype must be fp32, bf16 or fp16");
+    return LWL_ERR_INVALID;
+  }
+  if (rows < 0 || features <= 0) {
+    lwl::set_error("rows must be >= 0 and features > 0");
+    return LWL_ERR_INVALID;
+  }
+  const int logP = lwl::ilog2(features);
+  if (logP > 13) {
+    lwl::set_error("padded feature count %lld exceeds 8192", (long long)(int64_t(1) << logP));
+    return LWL_ERR_UNSUPPORTED;
+  }
+  if (rows == 0) return LWL_OK;
+  if (!x || !y || !signs) {
+    lwl::set_error("null data pointer");
+    return LWL_ERR_INVALID;
+  }
+  if (lwl::fht_mix_launch(dtype, x, y, signs, rows, (int)features, logP, reinterpret_cast<cudaStream_t>(stream))) {
+    lwl::set_error("fixed FHT mix launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    return LWL_ERR_CUDA;
   }
   return LWL_OK;
 }

@@ -59,6 +59,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.lwl_linear_backward.restype = ci
     lib.lwl_linear_backward.argtypes = [ci, vp, vp, i64, i64, i64, vp, i64, ci, u64, ctypes.c_float, vp, vp, vp, sz,
                                         cu, vp]
+    lib.lwl_fixed_fht_mix.restype = ci
+    lib.lwl_fixed_fht_mix.argtypes = [ci, vp, i64, i64, vp, vp, vp]
     lib.lwl_tc_linear_dense.restype = ci
     lib.lwl_tc_linear_dense.argtypes = [vp, i64, i64, vp, i64, vp, vp, sz, vp]
     lib.lwl_fht_launch_count.restype = ci
@@ -274,6 +276,22 @@ def linear_backward(x2d: torch.Tensor, grad_y2d: torch.Tensor, latent: torch.Ten
                                        ws.data_ptr() if ws is not None else None, nbytes, flags,
                                        _stream_ptr(x2d.device)))
     return gx, gz
+
+
+def fixed_fht_mix(x: torch.Tensor, signs: torch.Tensor) -> torch.Tensor:
+    """(S * H_P/sqrt(P) * S * pad(x))[..., :F] over the last dimension through
+    lwl_fixed_fht_mix; signs: fp32 [P] on x's device, P = next_pow2(F)."""
+    _require_cuda(x, "input")
+    lib = load()
+    x = x.contiguous()
+    F = x.shape[-1]
+    sg = signs.to(device=x.device, dtype=torch.float32).contiguous()
+    y = torch.empty_like(x)
+    rows = x.numel() // F if F > 0 else 0
+    with torch.cuda.device(x.device):
+        _check(lib.lwl_fixed_fht_mix(dtype_code(x.dtype), x.data_ptr(), rows, F, sg.data_ptr(), y.data_ptr(),
+                                     _stream_ptr(x.device)))
+    return y
 
 
 def tc_linear_dense(x2d: torch.Tensor, w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:

@@ -13,6 +13,8 @@ Reference behaviour restated here (file:line within verithia/latent-weight-lab):
 * ``linear_forward``      latent_weight_lab/block_fht.py:291-311 (_BlockFHTLinearFn.forward:
                           W = slice(0, in*out) * scale, viewed [out, in], then x @ W^T)
 * ``linear_backward``     latent_weight_lab/block_fht.py:323-356
+* ``fixed_fht_mix``       examples/nanogpt/model.py:182-218 (normalized_fht_last_dim,
+                          FixedFHTMix.forward); its own adjoint, so also the gradient
 """
 from __future__ import annotations
 
@@ -141,3 +143,32 @@ def linear_backward(grad_y, x, latent, out_features: int, layers: int, seed: int
     grad_z = np.float64(weight_scale) * fht_backward(grad_w.reshape(-1).astype(np.float32), z.size,
                                                      size, layers, seed, 0, size)
     return grad_x, grad_z, g2.sum(axis=0)
+
+
+def normalized_wht_last_dim(values) -> np.ndarray:
+    """Natural-order Walsh-Hadamard over the last axis times 1/sqrt(n), fp64
+    (examples/nanogpt/model.py:182-197: radix-2 butterflies a+b, a-b with the
+    stride doubling from 1)."""
+    out = np.array(values, dtype=np.float64)
+    n = out.shape[-1]
+    if n & (n - 1):
+        raise ValueError("FHT size must be a power of two")
+    h = 1
+    while h < n:
+        v = out.reshape(*out.shape[:-1], n // (2 * h), 2, h)
+        a, b = v[..., 0, :].copy(), v[..., 1, :].copy()
+        v[..., 0, :], v[..., 1, :] = a + b, a - b
+        out = v.reshape(*out.shape[:-1], n)
+        h *= 2
+    return out / np.sqrt(n)
+
+
+def fixed_fht_mix(x, signs) -> np.ndarray:
+    """(S * H_P/sqrt(P) * S * pad(x))[..., :F] over the last axis, P = len(signs)
+    (examples/nanogpt/model.py:211-218)."""
+    x = np.asarray(x, dtype=np.float64)
+    s = np.asarray(signs, dtype=np.float64)
+    F = x.shape[-1]
+    pad = np.zeros(x.shape[:-1] + (s.size,), dtype=np.float64)
+    pad[..., :F] = x
+    return (normalized_wht_last_dim(pad * s) * s)[..., :F]

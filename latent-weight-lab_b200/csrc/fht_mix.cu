@@ -3,12 +3,13 @@
 // Reference: examples/nanogpt/model.py:182-218 (normalized_fht_last_dim + FixedFHTMix.forward).
 // The map is symmetric, so the same kernel computes the gradient.
 //
-// HBM-bound: one read and one write per element.  Layout of a row in the
-// threads that own it: position p = wr * 1024 + lane * E + e, with E = P / 32
-// values per lane (E <= 32, fp32 registers), lane = 0..31, wr = warp of the
-// row (P / 1024 warps when P > 1024).  Butterflies over the e bits run in
-// registers, over the lane bits with shfl_xor, over the warp bits through a
-// shared-memory exchange.  For P < 32 one warp holds 32 / P rows.
+// HBM-bound: one read and one write per element.  E = P / 32 values per lane
+// (E <= 32, fp32 registers) in chunks of up to 16 bytes: lane l owns chunks
+// l, l + 32, ... of the row's 1024-element slice of its warp, so every warp
+// access is contiguous (P / 1024 warps per row when P > 1024).  Butterflies
+// over the register bits run in registers, over the lane bits with shfl_xor,
+// over the warp bits through a shared-memory exchange.  Signs are applied as
+// sign-bit flips from a per-CTA bit table.  For P < 32 one warp holds 32 / P rows.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -60,8 +61,15 @@ __global__ void __launch_bounds__(kThreads) fht_mix_kernel(const T* __restrict__
                                                            const float* __restrict__ signs, int64_t rows, int F,
                                                            int logP, bool vec_ok) {
   __shared__ float buf[1 << kMaxLog];
+  __shared__ uint32_t sbits[(1 << kMaxLog) / 32];  // bit p set: signs[p] < 0
   const int P = 1 << logP;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int wd = w; wd < (P + 31) / 32; wd += kThreads / 32) {
+    const int i = 32 * wd + lane;
+    const uint32_t b = __ballot_sync(0xffffffffu, i < P && signs[i] < 0.0f);
+    if (lane == 0) sbits[wd] = b;
+  }
+  __syncthreads();
   const int nw = P > 1024 ? P >> 10 : 1;       // warps per row
   const int rpw = P < 32 ? 32 / P : 1;         // rows per warp
   const int lanes = P < 32 ? P : 32;           // lanes per row
@@ -69,27 +77,58 @@ __global__ void __launch_bounds__(kThreads) fht_mix_kernel(const T* __restrict__
   const int wr = w % nw, rg = w / nw;          // warp within its row, row group of the warp
   const int sub = lane / lanes, ln = lane % lanes;
   const float scale = rsqrtf((float)P);
-  for (int64_t rb = (int64_t)blockIdx.x * rows_per_cta; rb < rows; rb += (int64_t)gridDim.x * rows_per_cta) {
+  // Element e = c * CH + u of a lane sits at row position
+  //   p(e) = wr * 1024 + CH * (ln + lanes * c) + u,
+  // i.e. a lane owns chunks ln, ln + 32, ... of CH consecutive elements, so a
+  // warp's 16-byte accesses are contiguous.  Register bits (u, c) and lane
+  // bits each map to distinct position bits, so the butterflies below are the
+  // natural-order transform whatever the assignment.
+  constexpr int VEC = 16 / (int)sizeof(T);  // elements per 16-byte access
+  constexpr int CH = E >= VEC ? VEC : E, NC = E / CH;
+  auto pos = [&](int e) { return wr * 1024 + CH * (ln + lanes * (e / CH)) + e % CH; };
+  uint32_t sbc[NC];  // sign bits of each chunk (CH <= 8 consecutive bits of one word)
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int b0 = pos(c * CH);
+    sbc[c] = sbits[b0 >> 5] >> (b0 & 31);
+  }
+  auto sgn = [&](float val, int e) {
+    return __uint_as_float(__float_as_uint(val) ^ (((sbc[e / CH] >> (e % CH)) & 1u) << 31));
+  };
+  // the next row's full 16-byte chunks are loaded before the current row is
+  // transformed, so each warp keeps one row of loads in flight
+  const int64_t stride = (int64_t)gridDim.x * rows_per_cta;
+  auto full = [&](int c, bool act) { return CH == VEC && vec_ok && act && pos(c * CH) + VEC <= F; };
+  uint4 raw[NC];
+  {
+    const int64_t row0 = (int64_t)blockIdx.x * rows_per_cta + (int64_t)rg * rpw + sub;
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+      if (full(c, row0 < rows)) raw[c] = __ldg(reinterpret_cast<const uint4*>(x + row0 * F + pos(c * CH)));
+  }
+  for (int64_t rb = (int64_t)blockIdx.x * rows_per_cta; rb < rows; rb += stride) {
     const int64_t row = rb + (int64_t)rg * rpw + sub;
     const bool active = row < rows;
+    const T* xr = x + row * F;
     float v[E];
-    const int p0 = wr * 1024 + ln * E;
-    constexpr int VEC = 16 / (int)sizeof(T);  // elements per 16-byte access
-    const bool vec = (E % VEC == 0) && vec_ok && active && p0 + E <= F;
-    if (vec) {
 #pragma unroll
-      for (int c = 0; c < E / VEC; ++c) {
-        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + row * F + p0) + c);
-        const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+    for (int c = 0; c < NC; ++c) {
+      const int b0 = pos(c * CH);
+      if (full(c, active)) {
+        const uint32_t wv[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
 #pragma unroll
-        for (int u = 0; u < VEC; ++u) v[c * VEC + u] = unpack<T>(wv, u) * signs[p0 + c * VEC + u];
+        for (int u = 0; u < CH; ++u) v[c * CH + u] = sgn(unpack<T>(wv, u), c * CH + u);
+      } else {
+#pragma unroll
+        for (int u = 0; u < CH; ++u) v[c * CH + u] = (active && b0 + u < F) ? sgn(ld(xr + b0 + u), c * CH + u) : 0.0f;
       }
-    } else {
+    }
+    {
+      const int64_t nrow = row + stride;
+      const bool nact = nrow < rows;
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const int p = p0 + e;
-        v[e] = (active && p < F) ? ld(x + row * F + p) * signs[p] : 0.0f;
-      }
+      for (int c = 0; c < NC; ++c)
+        if (full(c, nact)) raw[c] = __ldg(reinterpret_cast<const uint4*>(x + nrow * F + pos(c * CH)));
     }
     // bits of e
 #pragma unroll
@@ -116,7 +155,7 @@ __global__ void __launch_bounds__(kThreads) fht_mix_kernel(const T* __restrict__
       // conflict-free for the lane-strided writes and the consecutive gathers
       float* rbuf = buf + rg * P;
 #pragma unroll
-      for (int e = 0; e < E; ++e) rbuf[swz(p0 + e)] = v[e];
+      for (int e = 0; e < E; ++e) rbuf[swz(pos(e))] = v[e];
       __syncthreads();
       for (int q = wr * 32 + lane; q < 1024; q += nw * 32) {
         float u[8];
@@ -137,24 +176,24 @@ __global__ void __launch_bounds__(kThreads) fht_mix_kernel(const T* __restrict__
       }
       __syncthreads();
 #pragma unroll
-      for (int e = 0; e < E; ++e) v[e] = rbuf[swz(p0 + e)];
+      for (int e = 0; e < E; ++e) v[e] = rbuf[swz(pos(e))];
       __syncthreads();  // the next rows' exchange reuses the buffer
     }
-    if (vec) {
+    T* yr = y + row * F;
 #pragma unroll
-      for (int c = 0; c < E / VEC; ++c) {
+    for (int c = 0; c < NC; ++c) {
+      const int b0 = pos(c * CH);
+      if (CH == VEC && vec_ok && active && b0 + VEC <= F) {
         float f8[VEC];
 #pragma unroll
-        for (int u = 0; u < VEC; ++u) f8[u] = v[c * VEC + u] * scale * signs[p0 + c * VEC + u];
+        for (int u = 0; u < VEC; ++u) f8[u] = sgn(v[c * CH + u] * scale, c * CH + u);
         uint32_t wv[4];
         pack<T>(wv, f8);
-        reinterpret_cast<uint4*>(y + row * F + p0)[c] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-      }
-    } else {
+        *reinterpret_cast<uint4*>(yr + b0) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+      } else {
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const int p = p0 + e;
-        if (active && p < F) y[row * F + p] = Cvt<T>::from_f(v[e] * scale * signs[p]);
+        for (int u = 0; u < CH; ++u)
+          if (active && b0 + u < F) yr[b0 + u] = Cvt<T>::from_f(sgn(v[c * CH + u] * scale, c * CH + u));
       }
     }
   }

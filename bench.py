@@ -554,6 +554,143 @@ def _native_pow2(v: int) -> int:
     return 1 << (int(v) - 1).bit_length()
 
 
+def run_gpt2xl(args) -> None:
+    """C5: GPT-2-XL-shaped training step (48 layers, d=1600, 25 heads, MLP 6400,
+    seq 1024, batch 32 = 32768 tokens per GPU, vocab 50257 padded to 50304)
+    with every qkv / attn-proj / fc / fc-proj weight generated by BlockFHT
+    (bf16, layers=3, per-matrix seeds): forward, cross-entropy on random
+    targets, backward to the latents, LayerNorms and embeddings, and a fused
+    AdamW step.  N GPUs: data parallel (25 heads admit no 2/4/8-way tensor
+    split); the trainable state is the latents, so the only exchange is one
+    NCCL all-reduce of all gradients (~80 MB at ratio latents) per step.
+
+    --latent-mode ratio: latent = 1% of each weight (block sizes
+    131072 / 32768 / 131072 / 131072); literal: 1/16 (524288 / 262144 /
+    1048576 / 1048576)."""
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    from latent_weight_lab import BlockFHTLinear, _native
+
+    world, rank, local = _dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    _native.load()
+    torch.manual_seed(0)
+    n_layer, d, n_head, T, Bsz, vocab = args.xl_layers, 1600, 25, 1024, 32, 50304
+
+    def lin(i, o, seed):
+        lat = max(1, round(i * o * (0.01 if args.latent_mode == "ratio" else 1 / 16)))
+        return BlockFHTLinear(i, o, bias=True, latent_dim=lat, layers=3, seed=seed)
+
+    class Block(torch.nn.Module):
+        def __init__(self, k):
+            super().__init__()
+            self.ln1, self.ln2 = torch.nn.LayerNorm(d), torch.nn.LayerNorm(d)
+            self.qkv, self.proj = lin(d, 3 * d, 4 * k), lin(d, d, 4 * k + 1)
+            self.fc, self.fcp = lin(d, 4 * d, 4 * k + 2), lin(4 * d, d, 4 * k + 3)
+
+        def forward(self, x):
+            b, t, _ = x.shape
+            q, k_, v = self.qkv(self.ln1(x)).split(d, dim=2)
+            q, k_, v = (u.view(b, t, n_head, d // n_head).transpose(1, 2) for u in (q, k_, v))
+            a = F.scaled_dot_product_attention(q, k_, v, is_causal=True).transpose(1, 2).reshape(b, t, d)
+            x = x + self.proj(a)
+            return x + self.fcp(F.gelu(self.fc(self.ln2(x))))
+
+    class GPT(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.wte = torch.nn.Parameter(torch.randn(vocab, d) * 0.02)
+            self.wpe = torch.nn.Parameter(torch.randn(T, d) * 0.01)
+            self.blocks = torch.nn.ModuleList([Block(k) for k in range(n_layer)])
+            self.lnf = torch.nn.LayerNorm(d)
+
+        def forward(self, idx, tgt):
+            x = self.wte[idx] + self.wpe
+            for blk in self.blocks:
+                x = blk(x)
+            logits = F.linear(self.lnf(x), self.wte)
+            return F.cross_entropy(logits.view(-1, vocab).float(), tgt.view(-1))
+
+    model = GPT().to(dev, torch.bfloat16)
+    params = [q for q in model.parameters() if q.requires_grad]
+    opt = torch.optim.AdamW(params, lr=1e-4, fused=True)
+    g = torch.Generator(device="cpu").manual_seed(1234 + rank)
+    idx_host = torch.randint(0, 50257, (Bsz, T), generator=g).pin_memory()
+    tgt_host = torch.randint(0, 50257, (Bsz, T), generator=g).pin_memory()
+    idx = torch.empty(Bsz, T, dtype=torch.long, device=dev)
+    tgt = torch.empty_like(idx)
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+    n_grad = sum(q.numel() for q in params)
+
+    def step():
+        idx.copy_(idx_host, non_blocking=True)
+        tgt.copy_(tgt_host, non_blocking=True)
+        opt.zero_grad(set_to_none=False)
+        loss = model(idx, tgt)
+        loss.backward()
+        if world > 1:
+            flat = torch.cat([q.grad.reshape(-1) for q in params])
+            dist.all_reduce(flat)
+            flat /= world
+            off = 0
+            for q in params:
+                q.grad.copy_(flat[off:off + q.numel()].view_as(q.grad))
+                off += q.numel()
+        opt.step()
+        loss_host.copy_(loss.detach(), non_blocking=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        a.record()
+        for _ in range(args.steps):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    lin_flops_tok = 6 * n_layer * (d * 3 * d + d * d + 2 * d * 4 * d)
+    tokens = Bsz * T * world
+    if rank == 0:
+        peaks = _peaks()
+        achieved = tokens / world * lin_flops_tok / (ms * 1e-3) / 1e12
+        line = {
+            "metric": "GPT-2-XL training tokens/s, BlockFHT-generated linears (C5)",
+            "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic token ids and targets (uniform, seed 1234 + rank), random-init weights",
+            "config": {"workload": f"C5 GPT-2-XL training step, latent mode {args.latent_mode}", "batch": Bsz,
+                       "seq_len": T, "layers": n_layer, "d_model": d, "heads": n_head, "vocab_padded": vocab,
+                       "parallelism": f"dp{world} (latent-gradient all-reduce, NCCL)",
+                       "step": "forward + cross-entropy + backward + gradient all-reduce + fused AdamW",
+                       "trainable_params_per_rank": n_grad},
+            "e2e": {"value": tokens / (ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": 2 * Bsz * T * 8,
+                    "d2h_bytes_per_step": 4},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": achieved / peaks["bf16_tflops"], "traffic": None, "peak_source": peaks["source"],
+                         "counted": "6 * linear FLOPs per token (fwd + grad_x + grad_W); generation, attention "
+                                    "and the LM head not counted"},
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def run_gpt2(args) -> None:
     """C4: GPT-2-small-shaped decoder inference (12 layers, d=768, 12 heads, seq 1024,
     batch 8, vocab 50257 padded to 50304) with every qkv / attn-proj / fc / fc-proj
@@ -667,13 +804,14 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["fht", "mlp", "sweep", "gpt2", "linear", "mix"], default="fht")
+    ap.add_argument("--workload", choices=["fht", "mlp", "sweep", "gpt2", "gpt2xl", "linear", "mix"], default="fht")
     ap.add_argument("--latent-mode", choices=["ratio", "literal"], default="ratio")
     ap.add_argument("--min-log", type=int, default=5)
     ap.add_argument("--max-log", type=int, default=23)
     ap.add_argument("--latent", type=int, default=32768, help="latent size for --workload mlp")
     ap.add_argument("--tokens", type=int, default=32768, help="tokens for --workload linear (mix: rows / 2)")
     ap.add_argument("--features", type=int, default=3072, help="features for --workload mix")
+    ap.add_argument("--xl-layers", type=int, default=48, help="layers for --workload gpt2xl")
     args = ap.parse_args()
     if args.workload == "mlp":
         run_mlp(args)
@@ -681,6 +819,8 @@ def main() -> None:
         run_sweep(args)
     elif args.workload == "gpt2":
         run_gpt2(args)
+    elif args.workload == "gpt2xl":
+        run_gpt2xl(args)
     elif args.workload == "linear":
         run_linear(args)
     elif args.workload == "mix":

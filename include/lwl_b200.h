@@ -104,6 +104,32 @@ int lwl_fht_backward(int dtype, const void* grad_out, int64_t latent_size, int64
                      int layers, uint64_t seed, int64_t start, int64_t stop, void* grad_latent,
                      void* workspace, size_t workspace_bytes, unsigned flags, void* stream);
 
+/* One generator of a grouped backward: grad_latent[latent_size] (dtype) =
+ * the latent gradient of grad_out[stop - start] (dtype), as lwl_fht_backward. */
+typedef struct lwl_fht_backward_desc {
+  const void* grad_out;
+  int64_t latent_size;
+  int64_t size;
+  int layers;
+  uint64_t seed;
+  int64_t start, stop;
+  void* grad_latent;
+} lwl_fht_backward_desc;
+
+/* Workspace for lwl_fht_backward_grouped with these descriptors. */
+size_t lwl_fht_backward_grouped_workspace_bytes(int dtype, int count, const lwl_fht_backward_desc* descs,
+                                                unsigned flags);
+
+/* count lwl_fht_backward calls as one kernel + one reduce launch per 96
+ * generators (16-bit dtypes, padded block size <= 2^15; other generators run
+ * one by one inside the call): each CTA takes a contiguous range of all
+ * generators' 2^15-coordinate tiles and writes one partial row per generator
+ * it touches.  Deterministic.  Replaces: the per-module
+ * block_fht_grad_latent calls of flush_block_fht_weight_cache
+ * (latent_weight_lab/block_fht.py:514-557, 566-569). */
+int lwl_fht_backward_grouped(int dtype, int count, const lwl_fht_backward_desc* descs, void* workspace,
+                             size_t workspace_bytes, unsigned flags, void* stream);
+
 /* Workspace for lwl_linear_forward: 16 bytes; its first int is a device
  * error word, 0 after a successful call (1 = a bounded pipeline wait gave up). */
 size_t lwl_linear_forward_workspace_bytes(void);

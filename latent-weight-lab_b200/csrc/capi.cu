@@ -10,6 +10,7 @@
 #include <cstdint>
 #include <cstring>
 #include <algorithm>
+#include <vector>
 
 #include "fht_engine.h"
 #include "fht_mma.h"
@@ -399,6 +400,64 @@ int lwl_linear_backward(int dtype, const void* x, const void* grad_y, int64_t to
                                                                                          latent_size, weight_scale);
       LWL_CUDA_TRY(cudaGetLastError());
     }
+  }
+  return LWL_OK;
+}
+
+static bool grouped_bwd_fast(int dtype, const lwl_fht_backward_desc& q, unsigned flags) {
+  return lwl::mma_backward_supported(dtype, q.latent_size, flags);
+}
+
+size_t lwl_fht_backward_grouped_workspace_bytes(int dtype, int count, const lwl_fht_backward_desc* descs,
+                                                unsigned flags) {
+  if (count <= 0 || !descs) return 0;
+  std::vector<lwl_fht_backward_desc> fast;
+  size_t need = 0;
+  for (int i = 0; i < count; ++i) {
+    const lwl_fht_backward_desc& q = descs[i];
+    if (grouped_bwd_fast(dtype, q, flags))
+      fast.push_back(q);
+    else
+      need = std::max(need, lwl::fht_ws(true, dtype, q.latent_size, q.size, q.layers, q.start, q.stop, flags));
+  }
+  if (!fast.empty()) need = std::max(need, lwl::mma_backward_grouped_workspace_bytes((int)fast.size(), fast.data()));
+  return need;
+}
+
+int lwl_fht_backward_grouped(int dtype, int count, const lwl_fht_backward_desc* descs, void* workspace,
+                             size_t workspace_bytes, unsigned flags, void* stream) {
+  lwl::g_err[0] = 0;
+  if (count < 0 || (count > 0 && !descs)) {
+    lwl::set_error("invalid descriptor array");
+    return LWL_ERR_INVALID;
+  }
+  std::vector<lwl_fht_backward_desc> fast;
+  for (int i = 0; i < count; ++i) {
+    const lwl_fht_backward_desc& q = descs[i];
+    int st = lwl::validate_fht(dtype, q.latent_size, q.size, q.layers, q.start, q.stop);
+    if (st) return st;
+    if (!q.grad_latent || (q.stop > q.start && !q.grad_out)) {
+      lwl::set_error("descriptor %d: null data pointer", i);
+      return LWL_ERR_INVALID;
+    }
+    if (grouped_bwd_fast(dtype, q, flags)) fast.push_back(q);
+  }
+  const size_t need = lwl_fht_backward_grouped_workspace_bytes(dtype, count, descs, flags);
+  if (need > 0 && (!workspace || workspace_bytes < need)) {
+    lwl::set_error("workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+    return LWL_ERR_WORKSPACE;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (!fast.empty() && lwl::mma_backward_grouped(dtype, (int)fast.size(), fast.data(), workspace, s) != 0) {
+    lwl::set_error("grouped backward launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    return LWL_ERR_CUDA;
+  }
+  for (int i = 0; i < count; ++i) {  // the rest, one by one, reusing the workspace in stream order
+    const lwl_fht_backward_desc& q = descs[i];
+    if (grouped_bwd_fast(dtype, q, flags)) continue;
+    int rc = lwl_fht_backward(dtype, q.grad_out, q.latent_size, q.size, q.layers, q.seed, q.start, q.stop,
+                              q.grad_latent, workspace, workspace_bytes, flags, stream);
+    if (rc) return rc;
   }
   return LWL_OK;
 }

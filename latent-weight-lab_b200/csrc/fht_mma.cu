@@ -484,6 +484,369 @@ int launch_backward_t(const void* grad, int64_t L, int layers, int n, uint32_t s
 
 
 // ---------------------------------------------------------------------------
+// Grouped backward: the latent gradients of many generators in one launch
+// (the projection side of a model's weight cache).  The 2^15-coordinate
+// tiles of all descriptors form one list; CTA c takes the contiguous range
+// [c*T/G, (c+1)*T/G), so it meets few descriptors.  Per descriptor it
+// accumulates in tensor memory exactly as the single-generator kernel does;
+// when the descriptor changes it flushes the accumulator into its partial
+// row of that descriptor (rows of descriptor d: the CTAs c_lo(d) ..) and
+// starts from zero.  fht15_reduce_grouped_kernel sums each descriptor's rows.
+
+struct BwdDesc {
+  const void* grad;
+  void* out;
+  int64_t L, start, stop;
+  int64_t first_block, nblocks, tile_prefix;  // tiles of this descriptor and their place in the list
+  int64_t row_off;                            // float offset of its first partial row
+  int c_lo, rows;                             // first CTA touching it, number of such CTAs
+  uint32_t seed32;
+  int n, layers;
+  float corr;
+};
+struct BwdGroup {
+  int count, grid;
+  int64_t total_tiles;
+  BwdDesc d[kMaxGroup];
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    fht15_backward_grouped_kernel(const __grid_constant__ BwdGroup G, float* __restrict__ partial,
+                                  int* __restrict__ err) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint16_t* xbuf = reinterpret_cast<uint16_t*>(smem);
+  uint16_t* ybuf = xbuf + kB;
+  uint16_t* stage = ybuf + kB;  // raw gradient of the next tile (bulk copy target)
+  uint32_t* sw = reinterpret_cast<uint32_t*>(stage + kB);
+  __shared__ float red[kThreads / 32];
+  __shared__ __align__(8) uint64_t mbar;
+  __shared__ int abort_flag;
+  __shared__ int k0_shared;
+  __shared__ uint32_t tmem_base_shared;
+  if (threadIdx.x == 0) abort_flag = 0;
+
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
+  if (w == 0) {
+    uint32_t dst = (uint32_t)__cvta_generic_to_shared(&tmem_base_shared);
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;\n" ::"r"(dst));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;\n");
+  const uint32_t tbase = tmem_base_shared + ((uint32_t)(32 * (w & 3)) << 16) + (uint32_t)(64 * (w >> 2));
+  auto zero_acc = [&]() {
+    float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tmem_st8(tbase + 8 * k, z);
+    tmem_wait_st();
+  };
+  zero_acc();
+
+  const uint32_t xb = (uint32_t)__cvta_generic_to_shared(xbuf);
+  const uint32_t yb = (uint32_t)__cvta_generic_to_shared(ybuf);
+  const uint32_t stage_s = (uint32_t)__cvta_generic_to_shared(stage);
+  const uint32_t mbar_s = (uint32_t)__cvta_generic_to_shared(&mbar);
+  const int64_t i0 = (int64_t)blockIdx.x * G.total_tiles / G.grid;
+  const int64_t i1 = (int64_t)(blockIdx.x + 1) * G.total_tiles / G.grid;
+  auto desc_of = [&](int64_t i, int from) {
+    int d = from;
+    while (d + 1 < G.count && G.d[d + 1].tile_prefix <= i) ++d;
+    return d;
+  };
+  auto bulk_ok = [&](const BwdDesc& D, int64_t blk) {
+    return ((D.start & 7) == 0) && ((reinterpret_cast<uintptr_t>(D.grad) & 15) == 0) && blk * kB >= D.start &&
+           (blk + 1) * kB <= D.stop;
+  };
+  auto issue = [&](const BwdDesc& D, int64_t blk) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(mbar_s), "r"((uint32_t)(kB * 2)));
+    const T* src = reinterpret_cast<const T*>(D.grad) + (blk * kB - D.start);
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(stage_s),
+        "l"(src), "r"((uint32_t)(kB * 2)), "r"(mbar_s)
+        : "memory");
+  };
+  // partial row of descriptor D for this CTA, staged in natural order through
+  // the exchange buffers; the accumulator restarts from zero
+  auto flush = [&](const BwdDesc& D) {
+    __syncthreads();
+    float* prow = reinterpret_cast<float*>(smem);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float acc[8];
+      tmem_ld8(tbase + 8 * k, acc);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        int R = g + 8 * ((i >> 1) & 1), C = 2 * t + (i & 1) + 8 * (i >> 2);
+        prow[dep_a(w, k, R, C)] = acc[i];
+      }
+    }
+    __syncthreads();
+    float* dst = partial + D.row_off + (int64_t)(blockIdx.x - D.c_lo) * D.L;
+    for (int64_t p = tid; p < D.L; p += kThreads) {
+      float v = 0.0f;
+      for (int j = 0; j < (kB >> D.n); ++j) v += prow[(j << D.n) + p];
+      dst[p] = v;
+    }
+    zero_acc();
+    __syncthreads();
+  };
+
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(mbar_s));
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncthreads();
+  uint32_t phase = 0;
+  if (tid == 0 && i0 < i1) {
+    const BwdDesc& D = G.d[desc_of(i0, 0)];
+    const int64_t blk = D.first_block + (i0 - D.tile_prefix);
+    if (bulk_ok(D, blk)) issue(D, blk);
+  }
+  Frags f;
+  int cur = -1;
+  for (int64_t i = i0; i < i1; ++i) {
+    const int d = desc_of(i, cur < 0 ? 0 : cur);
+    const BwdDesc& D = G.d[d];
+    if (d != cur) {
+      if (cur >= 0) flush(G.d[cur]);
+      make_frags(f, g, t, D.n);
+      cur = d;
+    }
+    const int n = D.n, layers = D.layers, Bm = (1 << n) - 1;
+    const T* grad = reinterpret_cast<const T*>(D.grad);
+    const int64_t blk = D.first_block + (i - D.tile_prefix);
+    const int64_t bbase = blk * kB;
+    const bool first_is_b = (layers != 2);
+    uint16_t* land = first_is_b ? ybuf : xbuf;
+    __syncthreads();
+    for (int q = tid; q < (layers + 1) * kWords; q += kThreads) {
+      int l = q / kWords, wd = q - l * kWords;
+      const int p = 32 * wd;
+      sw[l * kWordsPad + spad(wd)] =
+          sign_word(block_layer_key(D.seed32, (blk << (kLog - n)) + (p >> n), l), (p & Bm) >> 5);
+    }
+    uint4 raw[8];
+    float ss = 0.0f;
+    const bool bulk = bulk_ok(D, blk);
+    if (bulk) {
+      uint32_t done = 0;
+      for (int it = 0; it < (1 << 22) && !done; ++it) {
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(mbar_s), "r"(phase)
+            : "memory");
+      }
+      if (!done) {
+        abort_flag = 1;
+        atomicExch(err, 1);
+      }
+      phase ^= 1u;
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      int c = tid + kThreads * q;
+      int64_t gi = bbase + 8 * c;
+      if (bulk) {
+        raw[q] = reinterpret_cast<const uint4*>(stage)[c];
+      } else {
+        uint32_t vv[4] = {0, 0, 0, 0};
+        for (int e = 0; e < 8; ++e) {
+          int64_t gg = gi + e;
+          if (gg >= D.start && gg < D.stop)
+            vv[e >> 1] |= (uint32_t)reinterpret_cast<const uint16_t*>(grad)[gg - D.start] << (16 * (e & 1));
+        }
+        raw[q] = make_uint4(vv[0], vv[1], vv[2], vv[3]);
+      }
+      const T* ev = reinterpret_cast<const T*>(&raw[q]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float v = Cvt<T>::to_f(ev[e]);
+        ss += v * v;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[w] = ss;
+    __syncthreads();
+    if (abort_flag) break;  // uniform: set before the barrier above
+    if (tid == 0) {
+      // the stage buffer is free again: fetch the next tile while this one runs
+      if (i + 1 < i1) {
+        const BwdDesc& N = G.d[desc_of(i + 1, d)];
+        const int64_t nblk = N.first_block + (i + 1 - N.tile_prefix);
+        if (bulk_ok(N, nblk)) {
+          asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+          issue(N, nblk);
+        }
+      }
+      float s2 = 0.0f;
+      for (int q = 0; q < kThreads / 32; ++q) s2 += red[q];
+      int e = 0;
+      if (s2 > 0.0f) {
+        frexpf(sqrtf(s2), &e);
+        e -= 12;
+      }
+      k0_shared = e;
+    }
+    __syncthreads();
+    const int k0 = k0_shared;
+    const float in_scale = ldexpf(1.0f, -k0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      int c = tid + kThreads * q;
+      const T* ev = reinterpret_cast<const T*>(&raw[q]);
+      uint32_t hv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        hv[e] = pack_h2(Cvt<T>::to_f(ev[2 * e]) * in_scale, Cvt<T>::to_f(ev[2 * e + 1]) * in_scale);
+      if (first_is_b) {
+        *reinterpret_cast<uint4*>(land + lay_ab(8 * c)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) land[lay_ba(8 * c + e)] = (uint16_t)(hv[e >> 1] >> (16 * (e & 1)));
+      }
+    }
+    __syncthreads();
+    const float scale = ldexpf(1.0f, k0) * D.corr;
+    if (layers == 1) {
+      run<1, false, true>(f, yb, xb, sw + 1 * kWordsPad, nullptr, w, lane, g, t);
+      __syncthreads();
+      run_final_acc(f, xb, sw, scale, tbase, w, lane, g, t);
+    } else if (layers == 2) {
+      run<0, false, true>(f, xb, yb, sw + 2 * kWordsPad, nullptr, w, lane, g, t);
+      __syncthreads();
+      run<1, true, false>(f, yb, xb, nullptr, sw + 1 * kWordsPad, w, lane, g, t);
+      __syncthreads();
+      run_final_acc(f, xb, sw, scale, tbase, w, lane, g, t);
+    } else {
+      run<1, false, true>(f, yb, xb, sw + 3 * kWordsPad, nullptr, w, lane, g, t);
+      __syncthreads();
+      run<0, true, false>(f, xb, yb, nullptr, sw + 2 * kWordsPad, w, lane, g, t);
+      __syncthreads();
+      run<1, true, false>(f, yb, xb, nullptr, sw + 1 * kWordsPad, w, lane, g, t);
+      __syncthreads();
+      run_final_acc(f, xb, sw, scale, tbase, w, lane, g, t);
+    }
+  }
+  if (abort_flag) {
+    if (tid == 0) {
+      // let an outstanding copy land before the CTA exits (bounded)
+      uint32_t done = 0;
+      for (int it = 0; it < (1 << 22) && !done; ++it) {
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(mbar_s), "r"(phase ^ 1u)
+            : "memory");
+      }
+    }
+  } else if (cur >= 0) {
+    flush(G.d[cur]);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;\n");
+  if (w == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;\n" ::"r"(tmem_base_shared));
+}
+
+// Sum of each descriptor's partial rows (blockIdx.y = descriptor); a failed
+// bulk-copy wait poisons every gradient of the group with NaN.
+template <typename T>
+__global__ void fht15_reduce_grouped_kernel(const __grid_constant__ BwdGroup G, const float* __restrict__ partial,
+                                            const int* __restrict__ err) {
+  const BwdDesc& D = G.d[blockIdx.y];
+  const bool bad = *err != 0;
+  const float* rows = partial + D.row_off;
+  T* out = reinterpret_cast<T*>(D.out);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < D.L; i += (int64_t)gridDim.x * blockDim.x) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int r = 0;
+    for (; r + 8 <= D.rows; r += 8) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc[u] += rows[(int64_t)(r + u) * D.L + i];
+    }
+    for (; r < D.rows; ++r) acc[0] += rows[(int64_t)r * D.L + i];
+    float s = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+    out[i] = Cvt<T>::from_f(bad ? __int_as_float(0x7fc00000) : s);
+  }
+}
+
+// Host plan of one group: tiles, CTA ranges, partial-row layout.
+inline int64_t cta_of_tile(int64_t i, int64_t total, int grid) {
+  int64_t c = i * grid / total;
+  while (c + 1 < grid && (c + 1) * total / grid <= i) ++c;
+  while (c > 0 && c * total / grid > i) --c;
+  return c;
+}
+
+inline size_t plan_backward_group(int count, const lwl_fht_backward_desc* q, BwdGroup& G) {
+  G.count = count;
+  int64_t prefix = 0;
+  for (int i = 0; i < count; ++i) {
+    BwdDesc& D = G.d[i];
+    const int64_t first = q[i].start / kB, last = (q[i].stop + kB - 1) / kB;
+    D.grad = q[i].grad_out;
+    D.out = q[i].grad_latent;
+    D.L = q[i].latent_size;
+    D.start = q[i].start;
+    D.stop = q[i].stop;
+    D.first_block = first;
+    D.nblocks = last > first ? last - first : 0;
+    D.tile_prefix = prefix;
+    prefix += D.nblocks;
+    D.seed32 = fold_seed(q[i].seed);
+    D.n = ilog2(next_pow2(q[i].latent_size));
+    D.layers = q[i].layers;
+    D.corr = (float)std::pow(layer_correction(D.n), D.layers);
+  }
+  G.total_tiles = prefix;
+  const int sms = sm_count();
+  G.grid = (int)(prefix < sms ? (prefix > 0 ? prefix : 1) : sms);
+  int64_t off = 0;
+  for (int i = 0; i < count; ++i) {
+    BwdDesc& D = G.d[i];
+    if (D.nblocks == 0) {
+      D.c_lo = 0;
+      D.rows = 0;
+    } else {
+      const int64_t lo = cta_of_tile(D.tile_prefix, prefix, G.grid);
+      const int64_t hi = cta_of_tile(D.tile_prefix + D.nblocks - 1, prefix, G.grid);
+      D.c_lo = (int)lo;
+      D.rows = (int)(hi - lo + 1);
+    }
+    D.row_off = off;
+    off += (int64_t)D.rows * D.L;
+  }
+  return kBwdHeader + size_t(off) * 4;
+}
+
+template <typename T>
+int launch_backward_grouped_t(const BwdGroup& G, void* workspace, cudaStream_t st) {
+  int* err = reinterpret_cast<int*>(workspace);
+  float* partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kBwdHeader);
+  if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess) return -1;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(fht15_backward_grouped_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSmemBwd) != cudaSuccess)
+      return -1;
+    attr = true;
+  }
+  if (G.total_tiles > 0) {
+    fht15_backward_grouped_kernel<T><<<G.grid, kThreads, kSmemBwd, st>>>(G, partial, err);
+    if (cudaGetLastError() != cudaSuccess) return -1;
+  }
+  int64_t maxL = 1;
+  for (int i = 0; i < G.count; ++i) maxL = G.d[i].L > maxL ? G.d[i].L : maxL;
+  dim3 rgrid((unsigned)std::min<int64_t>((maxL + 255) / 256, 256), (unsigned)G.count);
+  fht15_reduce_grouped_kernel<T><<<rgrid, 256, 0, st>>>(G, partial, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// ---------------------------------------------------------------------------
 // Low pass of large blocks: one work item = one 2^15 tile (positions
 // [j*2^15, (j+1)*2^15) of block b).  The planner's two-pass launch describes
 // input (latent / gradient slice / fp32 workspace), signs and output (dtype
@@ -759,6 +1122,30 @@ int mma_backward(int dtype, const void* grad, int64_t L, int layers, uint64_t se
                                                   workspace, st);
   return fmma::launch_backward_t<__half>(grad, L, layers, ilog2(next_pow2(L)), s32, first, last - first, start, stop, grad_latent,
                                          workspace, st);
+}
+
+size_t mma_backward_grouped_workspace_bytes(int count, const lwl_fht_backward_desc* descs) {
+  size_t need = 0;
+  for (int g0 = 0; g0 < count; g0 += fmma::kMaxGroup) {
+    fmma::BwdGroup G;
+    const int c = count - g0 < fmma::kMaxGroup ? count - g0 : fmma::kMaxGroup;
+    size_t b = fmma::plan_backward_group(c, descs + g0, G);
+    need = b > need ? b : need;  // the groups run one after another on one stream
+  }
+  return need;
+}
+
+int mma_backward_grouped(int dtype, int count, const lwl_fht_backward_desc* descs, void* workspace,
+                         cudaStream_t st) {
+  for (int g0 = 0; g0 < count; g0 += fmma::kMaxGroup) {
+    fmma::BwdGroup G;
+    const int c = count - g0 < fmma::kMaxGroup ? count - g0 : fmma::kMaxGroup;
+    fmma::plan_backward_group(c, descs + g0, G);
+    int rc = dtype == LWL_BF16 ? fmma::launch_backward_grouped_t<__nv_bfloat16>(G, workspace, st)
+                               : fmma::launch_backward_grouped_t<__half>(G, workspace, st);
+    if (rc) return rc;
+  }
+  return 0;
 }
 
 }  // namespace lwl

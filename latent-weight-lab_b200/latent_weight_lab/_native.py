@@ -59,6 +59,10 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.lwl_linear_backward.restype = ci
     lib.lwl_linear_backward.argtypes = [ci, vp, vp, i64, i64, i64, vp, i64, ci, u64, ctypes.c_float, vp, vp, vp, sz,
                                         cu, vp]
+    lib.lwl_fht_backward_grouped_workspace_bytes.restype = sz
+    lib.lwl_fht_backward_grouped_workspace_bytes.argtypes = [ci, ci, ctypes.POINTER(BackwardDesc), cu]
+    lib.lwl_fht_backward_grouped.restype = ci
+    lib.lwl_fht_backward_grouped.argtypes = [ci, ci, ctypes.POINTER(BackwardDesc), vp, sz, cu, vp]
     lib.lwl_fixed_fht_mix.restype = ci
     lib.lwl_fixed_fht_mix.argtypes = [ci, vp, i64, i64, vp, vp, vp]
     lib.lwl_tc_linear_dense.restype = ci
@@ -77,6 +81,14 @@ class ForwardDesc(ctypes.Structure):
     _fields_ = [("latent", ctypes.c_void_p), ("latent_size", ctypes.c_int64), ("size", ctypes.c_int64),
                 ("layers", ctypes.c_int), ("seed", ctypes.c_uint64), ("start", ctypes.c_int64),
                 ("stop", ctypes.c_int64), ("out", ctypes.c_void_p)]
+
+
+class BackwardDesc(ctypes.Structure):
+    """lwl_fht_backward_desc (include/lwl_b200.h)."""
+
+    _fields_ = [("grad_out", ctypes.c_void_p), ("latent_size", ctypes.c_int64), ("size", ctypes.c_int64),
+                ("layers", ctypes.c_int), ("seed", ctypes.c_uint64), ("start", ctypes.c_int64),
+                ("stop", ctypes.c_int64), ("grad_latent", ctypes.c_void_p)]
 
 
 def load() -> ctypes.CDLL:
@@ -223,6 +235,41 @@ def fht_forward_grouped(items, flags: int = 0) -> list[torch.Tensor]:
                                int(start), int(stop), out.data_ptr() if out.numel() else None)
     with torch.cuda.device(dev):
         _check(lib.lwl_fht_forward_grouped(dtype_code(dt), len(items), descs, int(flags), _stream_ptr(dev)))
+    return outs
+
+
+def fht_backward_grouped(items, flags: int = 0) -> list[torch.Tensor]:
+    """Several latent gradients in as few launches as possible.
+
+    items: sequence of (grad_out, latent_size, size, layers, seed, start, stop);
+    all gradients share one CUDA device and dtype.  Returns one [latent_size]
+    gradient per item, in that dtype.
+    """
+    items = list(items)
+    if not items:
+        return []
+    lib = load()
+    dev, dt = items[0][0].device, items[0][0].dtype
+    outs, keep = [], []
+    descs = (BackwardDesc * len(items))()
+    for i, (grad_out, latent_size, size, layers, seed, start, stop) in enumerate(items):
+        _require_cuda(grad_out, "grad_out")
+        if grad_out.device != dev or grad_out.dtype != dt:
+            raise ValueError("grouped backward needs one device and dtype")
+        grad_out = grad_out.contiguous()
+        if grad_out.numel() != int(stop) - int(start):
+            raise ValueError("grad_out must have stop - start elements")
+        keep.append(grad_out)
+        out = torch.empty(int(latent_size), dtype=dt, device=dev)
+        outs.append(out)
+        descs[i] = BackwardDesc(grad_out.data_ptr() if grad_out.numel() else None, int(latent_size), int(size),
+                                int(layers), _seed_u64(seed), int(start), int(stop), out.data_ptr())
+    code = dtype_code(dt)
+    with torch.cuda.device(dev):
+        nbytes = lib.lwl_fht_backward_grouped_workspace_bytes(code, len(items), descs, int(flags))
+        ws, _ = _workspace(nbytes, dev)
+        _check(lib.lwl_fht_backward_grouped(code, len(items), descs, ws.data_ptr() if ws is not None else None,
+                                            nbytes, int(flags), _stream_ptr(dev)))
     return outs
 
 

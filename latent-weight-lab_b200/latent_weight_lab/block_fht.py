@@ -370,48 +370,64 @@ class BlockFHTLinear(nn.Module):
                 weight = weight.to(dtype=dtype)
         self._cached_weight = weight.detach().requires_grad_(True)
 
+    def _flush_prepare(self) -> torch.Tensor | None:
+        """First half of the cache flush: the gain gradients, and the gradient
+        of the generated weight as a flat tensor in the latent dtype (None when
+        there is nothing to project)."""
+        if self._cached_weight is None or self._cached_weight.grad is None:
+            return None
+        ldt = self.generator.latent.dtype
+        grad_weight = self._cached_weight.grad.to(dtype=ldt)
+        cached_weight = self._cached_weight.detach().to(dtype=ldt)
+        generated_grad_weight = grad_weight
+        if self.output_gain is not None:
+            output_gain = self.output_gain.detach().to(dtype=ldt)
+            if torch.any(output_gain == 0):
+                raise RuntimeError("cannot flush a cached BlockFHT weight with a zero output gain")
+            g = (grad_weight * (cached_weight / output_gain.view(-1, 1))).sum(dim=1)
+            if self.output_gain.grad is None:
+                self.output_gain.grad = g.to(dtype=self.output_gain.dtype)
+            else:
+                self.output_gain.grad.add_(g.to(dtype=self.output_gain.dtype))
+            generated_grad_weight = generated_grad_weight * output_gain.view(-1, 1)
+        if self.input_gain is not None:
+            input_gain = self.input_gain.detach().to(dtype=ldt)
+            if torch.any(input_gain == 0):
+                raise RuntimeError("cannot flush a cached BlockFHT weight with a zero input gain")
+            g = (grad_weight * (cached_weight / input_gain.view(1, -1))).sum(dim=0)
+            if self.input_gain.grad is None:
+                self.input_gain.grad = g.to(dtype=self.input_gain.dtype)
+            else:
+                self.input_gain.grad.add_(g.to(dtype=self.input_gain.dtype))
+            generated_grad_weight = generated_grad_weight * input_gain.view(1, -1)
+        generated_grad_weight = generated_grad_weight.reshape(-1)
+        if self.residual_base_weight is not None:
+            generated_grad_weight = generated_grad_weight * self.residual_base_scale
+        return generated_grad_weight.contiguous()
+
+    def _flush_finish(self, generated_grad_weight: torch.Tensor, projected: torch.Tensor) -> None:
+        """Second half: scale the projected gradient, add the modulation term,
+        accumulate into the latent's gradient and drop the cache."""
+        grad_latent = self.weight_scale * projected
+        if self.modulation_alpha != 0.0:
+            # same value as block_fht.py:551-552; the latent is detached so the
+            # stored gradient carries no autograd graph
+            grad_latent = grad_latent + 2.0 * self.modulation_alpha * self.generator.latent.detach() * \
+                generated_grad_weight.sum()
+        if self.generator.latent.grad is None:
+            self.generator.latent.grad = grad_latent
+        else:
+            self.generator.latent.grad.add_(grad_latent)
+        self._cached_weight = None
+
     def flush_weight_cache_to_latent_grad(self) -> None:
         """Project the cached weight's gradient onto the latent and gains (block_fht.py:514-557)."""
         if self._cached_weight is None:
             return
-        if self._cached_weight.grad is not None:
-            ldt = self.generator.latent.dtype
-            grad_weight = self._cached_weight.grad.to(dtype=ldt)
-            cached_weight = self._cached_weight.detach().to(dtype=ldt)
-            generated_grad_weight = grad_weight
-            if self.output_gain is not None:
-                output_gain = self.output_gain.detach().to(dtype=ldt)
-                if torch.any(output_gain == 0):
-                    raise RuntimeError("cannot flush a cached BlockFHT weight with a zero output gain")
-                g = (grad_weight * (cached_weight / output_gain.view(-1, 1))).sum(dim=1)
-                if self.output_gain.grad is None:
-                    self.output_gain.grad = g.to(dtype=self.output_gain.dtype)
-                else:
-                    self.output_gain.grad.add_(g.to(dtype=self.output_gain.dtype))
-                generated_grad_weight = generated_grad_weight * output_gain.view(-1, 1)
-            if self.input_gain is not None:
-                input_gain = self.input_gain.detach().to(dtype=ldt)
-                if torch.any(input_gain == 0):
-                    raise RuntimeError("cannot flush a cached BlockFHT weight with a zero input gain")
-                g = (grad_weight * (cached_weight / input_gain.view(1, -1))).sum(dim=0)
-                if self.input_gain.grad is None:
-                    self.input_gain.grad = g.to(dtype=self.input_gain.dtype)
-                else:
-                    self.input_gain.grad.add_(g.to(dtype=self.input_gain.dtype))
-                generated_grad_weight = generated_grad_weight * input_gain.view(1, -1)
-            generated_grad_weight = generated_grad_weight.reshape(-1)
-            if self.residual_base_weight is not None:
-                generated_grad_weight = generated_grad_weight * self.residual_base_scale
-            grad_latent = self.weight_scale * block_fht_grad_latent(
-                self.generator.latent, generated_grad_weight, self.generator.size, self.generator.layers,
-                self.generator.seed)
-            if self.modulation_alpha != 0.0:
-                grad_latent = grad_latent + 2.0 * self.modulation_alpha * self.generator.latent * \
-                    generated_grad_weight.sum()
-            if self.generator.latent.grad is None:
-                self.generator.latent.grad = grad_latent
-            else:
-                self.generator.latent.grad.add_(grad_latent)
+        g = self._flush_prepare()
+        if g is not None:
+            self._flush_finish(g, block_fht_grad_latent(self.generator.latent, g, self.generator.size,
+                                                        self.generator.layers, self.generator.seed))
         self._cached_weight = None
 
 
@@ -445,9 +461,30 @@ def prepare_block_fht_weight_cache(model: nn.Module, dtype: torch.dtype | None =
 
 
 def flush_block_fht_weight_cache(model: nn.Module) -> None:
+    """Project every cached weight gradient of `model` onto its latent (block_fht.py:566-569).
+
+    The latent projections of CUDA generators run together: one grouped
+    library call (lwl_fht_backward_grouped) per (device, dtype).
+    """
+    pending: dict[tuple, list[tuple[BlockFHTLinear, torch.Tensor]]] = {}
     for module in model.modules():
-        if isinstance(module, BlockFHTLinear):
+        if not isinstance(module, BlockFHTLinear) or module._cached_weight is None:
+            continue
+        lat = module.generator.latent
+        if not lat.is_cuda:
             module.flush_weight_cache_to_latent_grad()
+            continue
+        g = module._flush_prepare()
+        if g is None:
+            module._cached_weight = None
+            continue
+        pending.setdefault((lat.device, lat.dtype), []).append((module, g))
+    for mods in pending.values():
+        projected = _native.fht_backward_grouped(
+            [(g, m.generator.latent.numel(), m.generator.size, m.generator.layers, m.generator.seed, 0,
+              m.generator.size) for m, g in mods], flags=_flags())
+        for (m, g), pz in zip(mods, projected):
+            m._flush_finish(g, pz)
 
 
 def suspend_block_fht_weight_cache(model: nn.Module) -> list[tuple[BlockFHTLinear, torch.Tensor]]:

@@ -213,3 +213,61 @@ def test_grouped_forward_more_than_one_launch(nat):
     outs = nat.fht_forward_grouped(items)
     for (z, size, layers, seed, start, stop), y in zip(items, outs):
         assert torch.equal(y, nat.fht_forward(z, size, layers, seed, start, stop))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_grouped_backward_matches_single_calls(native_lib, dtype):
+    """lwl_fht_backward_grouped: mixed block sizes and layer counts, ragged and
+    empty slices, a large-block generator (per-item fallback inside the call)
+    and more than one 96-descriptor group."""
+    from latent_weight_lab import _native
+
+    torch.manual_seed(5)
+    specs = [(32768, 3 * 32768, 3, 1, 0, 3 * 32768), (5898, 589824, 3, 2, 0, 589824),
+             (20000, 100000, 2, 3, 777, 65000), (1000, 9000, 1, 4, 5, 5), (40000, 200000, 3, 5, 0, 200000)]
+    specs += [(300 + 7 * i, 4000 + 13 * i, 1 + i % 3, 100 + i, i, 4000 + 13 * i - i) for i in range(100)]
+    items = []
+    for L, size, layers, seed, start, stop in specs:
+        g = torch.randn(stop - start, device="cuda").to(dtype)
+        items.append((g, L, size, layers, seed, start, stop))
+    outs = _native.fht_backward_grouped(items)
+    assert len(outs) == len(items)
+    for (g, L, size, layers, seed, start, stop), got in zip(items, outs):
+        ref = _native.fht_backward(g, L, size, layers, seed, start, stop)
+        assert got.shape == (L,) and got.dtype == dtype
+        if stop == start:
+            assert torch.count_nonzero(got) == 0
+            continue
+        assert rel_l2(got.float().cpu().numpy(), ref.float().cpu().numpy()) < 2e-3, (L, size, layers)
+    # absolute check of a few against the oracle
+    for k in (0, 2, 7):
+        g, L, size, layers, seed, start, stop = items[k]
+        ref = orc.fht_backward(g.float().cpu().numpy(), L, size, layers, seed, start, stop)
+        assert rel_l2(outs[k].float().cpu().numpy(), ref) < 1e-2
+
+
+@pytest.mark.gpu
+def test_weight_cache_flush_grouped_matches_per_module(native_lib):
+    from latent_weight_lab import BlockFHTLinear, flush_block_fht_weight_cache, prepare_block_fht_weight_cache
+
+    torch.manual_seed(2)
+    def model():
+        return torch.nn.Sequential(BlockFHTLinear(768, 768, latent_dim=5898, layers=3, seed=1),
+                                   BlockFHTLinear(768, 3072, latent_dim=32768, layers=3, seed=2, weight_scale=0.5,
+                                                  modulation_alpha=0.01),
+                                   BlockFHTLinear(3072, 768, latent_dim=65536, layers=2, seed=3)).cuda().bfloat16()
+    a, b = model(), model()
+    b.load_state_dict(a.state_dict())
+    x = torch.randn(64, 768, device="cuda", dtype=torch.bfloat16)
+    prepare_block_fht_weight_cache(a)
+    a(x).float().square().mean().backward()
+    flush_block_fht_weight_cache(a)  # grouped
+    prepare_block_fht_weight_cache(b)
+    b(x).float().square().mean().backward()
+    for m in b:
+        m.flush_weight_cache_to_latent_grad()  # one by one
+    for ma, mb in zip(a, b):
+        ga, gb = ma.generator.latent.grad.detach().float(), mb.generator.latent.grad.detach().float()
+        assert rel_l2(ga.cpu().numpy(), gb.cpu().numpy()) < 2e-3
+        assert ma._cached_weight is None

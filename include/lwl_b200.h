@@ -177,6 +177,19 @@ int lwl_linear_backward(int dtype, const void* x, const void* grad_y, int64_t to
 int lwl_fixed_fht_mix(int dtype, const void* x, int64_t rows, int64_t features, const float* signs, void* y,
                       void* stream);
 
+/* lwl_linear_forward with the module's per-feature terms folded in (each a
+ * bf16 device vector or NULL):
+ *   y[:, n] = out_gain[n] * (x @ (weight_scale * W * in_gain[None, :])^T)[:, n] + bias[n].
+ * The input gain scales the generated panel's columns on chip, the output
+ * gain and bias are applied in the epilogue.  Same shape limits as
+ * lwl_linear_forward; in_gain 4-byte aligned.  Replaces: the materialised
+ * weight that BlockFHTLinear.forward_fused falls back to when output_gain /
+ * input_gain are set (latent_weight_lab/block_fht.py:444-462, 482-501). */
+int lwl_linear_forward_ex(int dtype, const void* x, int64_t tokens, int64_t in_features, const void* latent,
+                          int64_t latent_size, int64_t out_features, int layers, uint64_t seed, float weight_scale,
+                          const void* bias, const void* out_gain, const void* in_gain, void* y, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
 /* Dense-weight variant of the same tcgen05 pipeline: y = x @ w^T with a given
  * bf16 w[out_features, in_features] (same shape limits).  No reference
  * counterpart; it isolates the MMA pipeline from the generator for testing. */

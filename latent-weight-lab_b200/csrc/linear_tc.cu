@@ -55,6 +55,9 @@ struct LinParams {
   const void* wdense;  // dense variant: bf16 [N, K]
   void* y;             // bf16 [T, N]
   int* err;
+  const __nv_bfloat16* bias;      // [N] or null
+  const __nv_bfloat16* out_gain;  // [N] or null
+  const __nv_bfloat16* in_gain;   // [K] or null
   int64_t L;
   int n, layers;
   uint32_t seed32;
@@ -267,6 +270,17 @@ __global__ void __launch_bounds__(kLinThreads, 1)
               const uint4 s4 = src[u];
               v[4 * u] = s4.x, v[4 * u + 1] = s4.y, v[4 * u + 2] = s4.z, v[4 * u + 3] = s4.w;
             }
+            if (P.in_gain) {  // W[:, k] * in_gain[k]: columns 64*c64 .. +63 of this row
+              const uint32_t* ig = reinterpret_cast<const uint32_t*>(P.in_gain + 64 * c64);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const uint32_t gb = __ldg(ig + j);
+                const __nv_bfloat162 r =
+                    __floats2bfloat162_rn(__uint_as_float(v[j] << 16) * __uint_as_float(gb << 16),
+                                          __uint_as_float(v[j] & 0xffff0000u) * __uint_as_float(gb & 0xffff0000u));
+                v[j] = (uint32_t)__bfloat16_as_ushort(r.x) | ((uint32_t)__bfloat16_as_ushort(r.y) << 16);
+              }
+            }
           }
           tc::tmem_st32(a_lane + 32 * c64, v);
         }
@@ -366,10 +380,13 @@ __global__ void __launch_bounds__(kLinThreads, 1)
         if (et == 0) tc::tma_store_wait_read<1>();
         tc::named_bar(1, 32 * kEpiWarps);
         __nv_bfloat16* yst = reinterpret_cast<__nv_bfloat16*>(pstage) + yb_i * (kYStageBytes / 2) + 64 * h * 128;
+        // per-feature output gain and bias (identity when absent)
+        const float og = P.out_gain ? __bfloat162float(P.out_gain[n0 + frow]) : 1.0f;
+        const float bs = P.bias ? __bfloat162float(P.bias[n0 + frow]) : 0.0f;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          yst[i * 128 + frow] = __float2bfloat16_rn(__uint_as_float(r0[i]));
-          yst[(i + 32) * 128 + frow] = __float2bfloat16_rn(__uint_as_float(r1[i]));
+          yst[i * 128 + frow] = __float2bfloat16_rn(fmaf(__uint_as_float(r0[i]), og, bs));
+          yst[(i + 32) * 128 + frow] = __float2bfloat16_rn(fmaf(__uint_as_float(r1[i]), og, bs));
         }
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
         tc::named_bar(1, 32 * kEpiWarps);
@@ -415,7 +432,8 @@ bool tc_linear_supported(int K, int N, int T) {
 }
 
 int tc_linear_launch(bool gen, const void* x, int T, int K, int N, const void* latent, int64_t L, int layers,
-                     uint64_t seed, float wscale, const void* wdense, void* y, int* err, cudaStream_t st) {
+                     uint64_t seed, float wscale, const void* wdense, void* y, int* err, cudaStream_t st,
+                     const LinExtras* extras) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return -2;
   CUtensorMap map, ymap;
@@ -440,6 +458,11 @@ int tc_linear_launch(bool gen, const void* x, int T, int K, int N, const void* l
   P.wdense = wdense;
   P.y = y;
   P.err = err;
+  if (extras) {
+    P.bias = reinterpret_cast<const __nv_bfloat16*>(extras->bias);
+    P.out_gain = reinterpret_cast<const __nv_bfloat16*>(extras->out_gain);
+    P.in_gain = reinterpret_cast<const __nv_bfloat16*>(extras->in_gain);
+  }
   P.L = L;
   P.n = gen ? ilog2(next_pow2(L)) : 15;
   P.layers = layers;

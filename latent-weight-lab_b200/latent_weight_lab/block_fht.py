@@ -342,8 +342,44 @@ class BlockFHTLinear(nn.Module):
                                        self.generator.size, self.generator.layers, self.generator.seed,
                                        self.weight_scale, self.modulation_alpha)
 
+    def _forward_fused_gains(self, input: torch.Tensor, weight_scale: float) -> torch.Tensor | None:
+        # like the reference's materialised path (F.linear with self.weight),
+        # the call's weight_scale argument does not enter when gains are set
+        del weight_scale
+        lat = self.generator.latent
+        if not (input.is_cuda and input.dtype == torch.bfloat16 and lat.dtype == torch.bfloat16) or _flags():
+            return None
+        flat = input.reshape(-1, self.in_features)
+        if flat.shape[0] == 0:
+            return None
+        with torch.no_grad():
+            out = _native.linear_forward(flat, lat, self.out_features, self.generator.layers, self.generator.seed,
+                                         self.weight_scale, bias=self.bias,
+                                         output_gain=self.output_gain, input_gain=self.input_gain)
+            if out is None:
+                return None
+            if self.modulation_alpha != 0.0:
+                xg = flat if self.input_gain is None else flat * self.input_gain.to(dtype=flat.dtype)
+                mod = (self.modulation_alpha * self._modulation_offset()).to(dtype=out.dtype) * \
+                    xg.sum(dim=-1, keepdim=True)
+                if self.output_gain is not None:
+                    mod = mod * self.output_gain.to(dtype=out.dtype)
+                out = out + mod
+        return out.reshape(*input.shape[:-1], self.out_features)
+
     def forward_fused(self, input: torch.Tensor, weight_scale: float = 1.0) -> torch.Tensor:
-        """Inference forward without autograd (block_fht.py:482-501)."""
+        """Inference forward without autograd (block_fht.py:482-501).
+
+        With output/input gains the reference multiplies a materialised
+        weight; here, for bf16 layers the fused kernel takes, the gains and
+        the bias are folded into the on-chip panel and the epilogue instead
+        (the modulation term is added afterwards, scaled by the same gains).
+        """
+        if (self.output_gain is not None or self.input_gain is not None) and self.spectral_core is None \
+                and self.residual_base_weight is None:
+            out = self._forward_fused_gains(input, weight_scale)
+            if out is not None:
+                return out
         if self.output_gain is not None or self.input_gain is not None or self.spectral_core is not None:
             return F.linear(input, self.weight.to(dtype=input.dtype), self.bias)
         out = block_fht_linear_forward(input, self.generator.latent, self.out_features, self.generator.layers,

@@ -139,3 +139,33 @@ def test_linear_backward_capi_zero_tokens(native_lib):
     z = torch.randn(100, device="cuda")
     gx, gz = _native.linear_backward(x, gy, z, 32, 2, 1)
     assert gx.shape == (0, 64) and torch.count_nonzero(gz) == 0
+
+
+@pytest.mark.parametrize("gains, alpha", [("out", 0.0), ("in", 0.0), ("both", 0.02), ("both", 0.0)])
+def test_forward_fused_with_gains_matches_materialised(native_lib, gains, alpha):
+    """Gains and bias folded into the fused kernel equal the reference's
+    materialised forward (F.linear with the module's weight) within bf16 tolerance."""
+    from latent_weight_lab import BlockFHTLinear, _native
+
+    torch.manual_seed(11)
+    layer = BlockFHTLinear(768, 3072, bias=True, latent_dim=32768, layers=3, seed=4, weight_scale=0.7,
+                           modulation_alpha=alpha, output_gain=gains in ("out", "both"),
+                           input_gain=gains in ("in", "both")).cuda().bfloat16()
+    with torch.no_grad():
+        if layer.output_gain is not None:
+            layer.output_gain.copy_(torch.rand(3072) + 0.5)
+        if layer.input_gain is not None:
+            layer.input_gain.copy_(torch.rand(768) + 0.5)
+        layer.bias.copy_(torch.randn(3072) * 0.1)
+    x = torch.randn(3, 111, 768, device="cuda", dtype=torch.bfloat16)
+    calls = []
+    orig = _native.linear_forward
+    _native.linear_forward = lambda *a, **k: calls.append(1) or orig(*a, **k)
+    try:
+        y = layer.forward_fused(x, weight_scale=3.0)  # ignored with gains, as in the reference
+    finally:
+        _native.linear_forward = orig
+    assert calls, "the fused kernel was not used"
+    with torch.no_grad():
+        ref = torch.nn.functional.linear(x.float(), layer.weight.float(), layer.bias.float())
+    assert rel_l2(y.float().cpu().numpy(), ref.cpu().numpy()) < 1e-2

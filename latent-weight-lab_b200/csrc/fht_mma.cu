@@ -149,13 +149,7 @@ constexpr size_t kSmem = 3 * kB * 2 + 4 * kWordsPad * 4;
 
 template <typename T>
 int launch_forward_t(const FwdGroup& G, cudaStream_t st) {
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(fht15_forward_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem) !=
-        cudaSuccess)
-      return -1;
-    attr = true;
-  }
+  if (!set_max_smem((const void*)fht15_forward_kernel<T>, (int)kSmem)) return -1;
   if (G.total_tiles <= 0) return 0;
   int sms = sm_count();
   int grid = (int)(G.total_tiles < sms ? G.total_tiles : sms);
@@ -463,13 +457,7 @@ int launch_backward_t(const void* grad, int64_t L, int layers, int n, uint32_t s
   int* err = reinterpret_cast<int*>(workspace);
   float* partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kBwdHeader);
   if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess) return -1;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(fht15_backward_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kSmemBwd) != cudaSuccess)
-      return -1;
-    attr = true;
-  }
+  if (!set_max_smem((const void*)fht15_backward_kernel<T>, (int)kSmemBwd)) return -1;
   int sms = sm_count();
   int grid = (int)(nblocks < sms ? nblocks : sms);
   const float corr = (float)std::pow(layer_correction(n), layers);
@@ -828,13 +816,7 @@ int launch_backward_grouped_t(const BwdGroup& G, void* workspace, cudaStream_t s
   int* err = reinterpret_cast<int*>(workspace);
   float* partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kBwdHeader);
   if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess) return -1;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(fht15_backward_grouped_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kSmemBwd) != cudaSuccess)
-      return -1;
-    attr = true;
-  }
+  if (!set_max_smem((const void*)fht15_backward_grouped_kernel<T>, (int)kSmemBwd)) return -1;
   if (G.total_tiles > 0) {
     fht15_backward_grouped_kernel<T><<<G.grid, kThreads, kSmemBwd, st>>>(G, partial, err);
     if (cudaGetLastError() != cudaSuccess) return -1;
@@ -1167,22 +1149,10 @@ int mma_lo_grid(const TileParams& p) {
 int mma_lo_launch(int dtype, const TileParams& p, int grid, cudaStream_t st) {
   const float corr1 = (float)fmma::layer_correction(fmma::kLog);
   if (dtype == LWL_BF16) {
-    static bool attr = false;
-    if (!attr) {
-      if (cudaFuncSetAttribute(fmma::fht_lo_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)fmma::kSmemLo) != cudaSuccess)
-        return -1;
-      attr = true;
-    }
+    if (!set_max_smem((const void*)fmma::fht_lo_kernel<__nv_bfloat16>, (int)fmma::kSmemLo)) return -1;
     fmma::fht_lo_kernel<__nv_bfloat16><<<grid, fmma::kThreads, fmma::kSmemLo, st>>>(p, corr1);
   } else {
-    static bool attr = false;
-    if (!attr) {
-      if (cudaFuncSetAttribute(fmma::fht_lo_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)fmma::kSmemLo) != cudaSuccess)
-        return -1;
-      attr = true;
-    }
+    if (!set_max_smem((const void*)fmma::fht_lo_kernel<__half>, (int)fmma::kSmemLo)) return -1;
     fmma::fht_lo_kernel<__half><<<grid, fmma::kThreads, fmma::kSmemLo, st>>>(p, corr1);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : -1;

@@ -481,22 +481,10 @@ int tc_linear_launch(bool gen, const void* x, int T, int K, int N, const void* l
   const int items = P.panels * P.tsplit;
   const int grid = std::min(items, sms);
   if (gen) {
-    static bool attr = false;
-    if (!attr) {
-      if (cudaFuncSetAttribute(fmma::linear_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)fmma::kLinSmem) != cudaSuccess)
-        return -1;
-      attr = true;
-    }
+    if (!set_max_smem((const void*)fmma::linear_tc_kernel<true>, (int)fmma::kLinSmem)) return -1;
     fmma::linear_tc_kernel<true><<<grid, fmma::kLinThreads, fmma::kLinSmem, st>>>(map, ymap, P);
   } else {
-    static bool attr = false;
-    if (!attr) {
-      if (cudaFuncSetAttribute(fmma::linear_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)fmma::kLinSmem) != cudaSuccess)
-        return -1;
-      attr = true;
-    }
+    if (!set_max_smem((const void*)fmma::linear_tc_kernel<false>, (int)fmma::kLinSmem)) return -1;
     fmma::linear_tc_kernel<false><<<grid, fmma::kLinThreads, fmma::kLinSmem, st>>>(map, ymap, P);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : -1;

@@ -10,6 +10,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <set>
+#include <utility>
+
 #include "lwl_b200.h"
 
 namespace lwl {
@@ -68,6 +72,21 @@ inline size_t dtype_bytes(int dtype) { return dtype == LWL_F32 ? 4 : 2; }
 
 // Thread-local error text for lwl_last_error().
 void set_error(const char* fmt, ...);
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device):
+// the attribute belongs to the device, so a process that drives several GPUs
+// sets it on each of them.
+inline bool set_max_smem(const void* func, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({func, dev})) return true;
+  if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+  done.insert({func, dev});
+  return true;
+}
 
 }  // namespace lwl
 

@@ -271,3 +271,21 @@ def test_weight_cache_flush_grouped_matches_per_module(native_lib):
         ga, gb = ma.generator.latent.grad.detach().float(), mb.generator.latent.grad.detach().float()
         assert rel_l2(ga.cpu().numpy(), gb.cpu().numpy()) < 2e-3
         assert ma._cached_weight is None
+
+
+@pytest.mark.gpu
+def test_two_devices_in_one_process(native_lib):
+    """Kernel attributes are per device: a process that drives two GPUs gets
+    correct results on both (skipped with one GPU)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from latent_weight_lab import _native
+
+    z = torch.randn(32768)
+    outs = []
+    for dev in ("cuda:0", "cuda:1"):
+        zd = z.to(dev).bfloat16()
+        outs.append(_native.fht_forward(zd, 1 << 20, 3, 9, 0, 1 << 20).cpu())
+        x = torch.randn(256, 768, device=dev).bfloat16()
+        assert _native.linear_forward(x, zd, 3072, 3, 9) is not None
+    assert torch.equal(outs[0], outs[1])

@@ -345,11 +345,30 @@ def run_mlp(args) -> None:
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    run = step
+    if not args.eager:
+        # the whole fwd+bwd step (generation, GEMMs, GELU, latent projections)
+        # replays as one CUDA graph; gradients are unset at capture, so every
+        # replay assigns fresh ones
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        up.generator.latent.grad = down.generator.latent.grad = x.grad = None
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            y = down(torch.nn.functional.gelu(up(x)))
+            y.backward(gy)
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        run = graph.replay
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(0) as clk:
         a.record()
         for _ in range(args.steps):
-            step()
+            run()
         b.record()
         torch.cuda.synchronize()
     ms = a.elapsed_time(b) / args.steps
@@ -362,7 +381,8 @@ def run_mlp(args) -> None:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (x ~N(0,1), latents ~N(0,0.02))",
         "config": {"workload": f"C3 MLP pair 768->3072->768, 8192 tokens, latent {args.latent}, layers=3",
-                   "path": "weights generated by liblwl_b200, GEMMs by cuBLAS (F.linear)"},
+                   "path": "weights generated by liblwl_b200, GEMMs by cuBLAS (F.linear)",
+                   "execution": "eager" if args.eager else "one CUDA graph per fwd+bwd step"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": achieved / peaks["bf16_tflops"], "traffic": None, "peak_source": peaks["source"]},
         "clocks": clk.summary(),
@@ -815,6 +835,7 @@ def main() -> None:
     ap.add_argument("--tokens", type=int, default=32768, help="tokens for --workload linear (mix: rows / 2)")
     ap.add_argument("--features", type=int, default=3072, help="features for --workload mix")
     ap.add_argument("--xl-layers", type=int, default=48, help="layers for --workload gpt2xl")
+    ap.add_argument("--eager", action="store_true", help="--workload mlp without CUDA-graph capture")
     args = ap.parse_args()
     if args.workload == "mlp":
         run_mlp(args)

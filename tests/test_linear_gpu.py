@@ -169,3 +169,39 @@ def test_forward_fused_with_gains_matches_materialised(native_lib, gains, alpha)
     with torch.no_grad():
         ref = torch.nn.functional.linear(x.float(), layer.weight.float(), layer.bias.float())
     assert rel_l2(y.float().cpu().numpy(), ref.cpu().numpy()) < 1e-2
+
+
+def test_mlp_step_replays_as_cuda_graph(native_lib):
+    """Forward + backward through BlockFHTLinear (generation, GEMMs, latent
+    projections) captured in one CUDA graph gives the eager gradients."""
+    from latent_weight_lab import BlockFHTLinear
+
+    torch.manual_seed(7)
+    up = BlockFHTLinear(768, 3072, latent_dim=32768, layers=3, seed=11).cuda().bfloat16()
+    down = BlockFHTLinear(3072, 768, latent_dim=65536, layers=3, seed=12).cuda().bfloat16()  # large-block path
+    x = torch.randn(512, 768, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    gy = torch.randn(512, 768, device="cuda", dtype=torch.bfloat16)
+
+    def step():
+        y = down(torch.nn.functional.gelu(up(x)))
+        y.backward(gy)
+
+    step()
+    eager = [t.grad.clone() for t in (up.generator.latent, down.generator.latent, x)]
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        up.generator.latent.grad = down.generator.latent.grad = x.grad = None
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    up.generator.latent.grad = down.generator.latent.grad = x.grad = None
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    with torch.no_grad():
+        x.mul_(1.0)  # inputs stay in place; the replay reads them
+    graph.replay()
+    graph.replay()
+    torch.cuda.synchronize()
+    for ref, t in zip(eager, (up.generator.latent, down.generator.latent, x)):
+        assert torch.equal(t.grad, ref)

@@ -222,7 +222,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t mbar;
   __shared__ int abort_flag;
   if (threadIdx.x == 0) abort_flag = 0;
-  __shared__ int k0_shared;
   __shared__ uint32_t tmem_base_shared;
 
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
@@ -340,17 +339,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
         issue(first_block + nb);
       }
+    }
+    // every thread forms the prescale exponent from the warp sums (same
+    // summation order everywhere, so all threads agree; no second barrier)
+    int k0 = 0;
+    {
       float s = 0.0f;
       for (int i = 0; i < kThreads / 32; ++i) s += red[i];
-      int e = 0;
       if (s > 0.0f) {
-        frexpf(sqrtf(s), &e);
-        e -= 12;
+        frexpf(sqrtf(s), &k0);
+        k0 -= 12;
       }
-      k0_shared = e;
     }
-    __syncthreads();
-    const int k0 = k0_shared;
     const float in_scale = ldexpf(1.0f, -k0);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -510,7 +510,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ float red[kThreads / 32];
   __shared__ __align__(8) uint64_t mbar;
   __shared__ int abort_flag;
-  __shared__ int k0_shared;
   __shared__ uint32_t tmem_base_shared;
   if (threadIdx.x == 0) abort_flag = 0;
 
@@ -670,17 +669,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           issue(N, nblk);
         }
       }
+    }
+    // every thread forms the prescale exponent from the warp sums (no second barrier)
+    int k0 = 0;
+    {
       float s2 = 0.0f;
       for (int q = 0; q < kThreads / 32; ++q) s2 += red[q];
-      int e = 0;
       if (s2 > 0.0f) {
-        frexpf(sqrtf(s2), &e);
-        e -= 12;
+        frexpf(sqrtf(s2), &k0);
+        k0 -= 12;
       }
-      k0_shared = e;
     }
-    __syncthreads();
-    const int k0 = k0_shared;
     const float in_scale = ldexpf(1.0f, -k0);
 #pragma unroll
     for (int q = 0; q < 8; ++q) {

@@ -59,7 +59,12 @@ __global__ void __launch_bounds__(kThreads, 1) fht15_forward_kernel(const __grid
     const T* latent = reinterpret_cast<const T*>(D.latent);
     const int n = D.n, layers = D.layers, Bm = (1 << n) - 1;
     const int64_t L = D.L;
-    __syncthreads();  // the previous tile is done with the latent copy, sign table and buffers
+    // After the previous tile's staging barrier no warp reads the sign table,
+    // the latent copy or red[] again; slower warps may still copy out of the
+    // staging buffer (ybuf).  For 1 and 3 layers that buffer is next written
+    // two barriers later, so no barrier is needed here; the first run of a
+    // 2-layer tile writes ybuf, so it waits.
+    if (layers == 2) __syncthreads();
     if (di != cur) {
       make_frags(f, g, t, n);
       // power-of-two prescale: tile L2 norm into [2^11, 2^12)

@@ -46,6 +46,17 @@ __global__ void __launch_bounds__(kThreads, 1) fht15_forward_kernel(const __grid
   __shared__ int k0_shared;
 
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
+  __shared__ uint32_t tmem_base_shared;
+  if (w == 0) {
+    uint32_t dst = (uint32_t)__cvta_generic_to_shared(&tmem_base_shared);
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 128;\n" ::"r"(dst));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;\n");
+  // this warp's 32 columns in its lane quadrant: the first run's input fragments
+  const uint32_t tz = tmem_base_shared + ((uint32_t)(32 * (w & 3)) << 16) + (uint32_t)(32 * (w >> 2));
   const uint32_t zb = (uint32_t)__cvta_generic_to_shared(zbuf);
   const uint32_t xb = (uint32_t)__cvta_generic_to_shared(xbuf);
   const uint32_t yb = (uint32_t)__cvta_generic_to_shared(ybuf);
@@ -116,6 +127,11 @@ __global__ void __launch_bounds__(kThreads, 1) fht15_forward_kernel(const __grid
         }
       }
       cur = di;
+      __syncthreads();  // the latent copy is complete
+      if (first_is_b)
+        park_first_input<1>(zb, tz, w, lane);
+      else
+        park_first_input<0>(zb, tz, w, lane);
     }
     const float out_scale = ldexpf(1.0f, k0) * D.corr;
     T* out = reinterpret_cast<T*>(D.out);
@@ -129,17 +145,17 @@ __global__ void __launch_bounds__(kThreads, 1) fht15_forward_kernel(const __grid
     }
     __syncthreads();
     if (layers == 1) {
-      run<1, false, true>(f, zb, xb, sw, nullptr, w, lane, g, t);
+      run_first_tmem<1>(f, tz, xb, sw, w, lane, g, t);
       __syncthreads();
       run_final<T>(f, xb, yb, ybuf, sw + 1 * kWordsPad, out_scale, out, blk, D.start, D.stop, vec_ok, w, lane, g, t);
     } else if (layers == 2) {
-      run<0, false, true>(f, zb, yb, sw, nullptr, w, lane, g, t);
+      run_first_tmem<0>(f, tz, yb, sw, w, lane, g, t);
       __syncthreads();
       run<1, true, false>(f, yb, xb, nullptr, sw + 1 * kWordsPad, w, lane, g, t);
       __syncthreads();
       run_final<T>(f, xb, yb, ybuf, sw + 2 * kWordsPad, out_scale, out, blk, D.start, D.stop, vec_ok, w, lane, g, t);
     } else {
-      run<1, false, true>(f, zb, xb, sw, nullptr, w, lane, g, t);
+      run_first_tmem<1>(f, tz, xb, sw, w, lane, g, t);
       __syncthreads();
       run<0, true, false>(f, xb, yb, nullptr, sw + 1 * kWordsPad, w, lane, g, t);
       __syncthreads();
@@ -148,6 +164,10 @@ __global__ void __launch_bounds__(kThreads, 1) fht15_forward_kernel(const __grid
       run_final<T>(f, xb, yb, ybuf, sw + 3 * kWordsPad, out_scale, out, blk, D.start, D.stop, vec_ok, w, lane, g, t);
     }
   }
+  asm volatile("tcgen05.fence::before_thread_sync;\n");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;\n");
+  if (w == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;\n" ::"r"(tmem_base_shared));
 }
 
 constexpr size_t kSmem = 3 * kB * 2 + 4 * kWordsPad * 4;

@@ -307,6 +307,53 @@ __device__ __forceinline__ void run(const Frags& f, uint32_t in_base, uint32_t o
   write_exchange<PASS>(d, out_base, w, g, t);
 }
 
+// ---- the first run's input fragments kept in tensor memory --------------------
+// Every tile of a forward descriptor starts from the same scaled latent copy,
+// so each warp loads its 8 first-run B-operand fragments (32 registers) once
+// per descriptor into its tensor-memory lanes (quadrant w % 4, 32 columns at
+// 32 * (w / 4)) and each tile's first run reads them with one tcgen05.ld
+// instead of eight ldmatrix from shared memory.
+template <int PASS>
+__device__ __forceinline__ void park_first_input(uint32_t in_base, uint32_t taddr, int w, int lane) {
+  uint32_t x[8][4];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) load_tile<PASS>(in_base, w, k, lane, x[k]);
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(taddr),
+      "r"(x[0][0]), "r"(x[0][1]), "r"(x[0][2]), "r"(x[0][3]), "r"(x[1][0]), "r"(x[1][1]), "r"(x[1][2]), "r"(x[1][3]),
+      "r"(x[2][0]), "r"(x[2][1]), "r"(x[2][2]), "r"(x[2][3]), "r"(x[3][0]), "r"(x[3][1]), "r"(x[3][2]), "r"(x[3][3]),
+      "r"(x[4][0]), "r"(x[4][1]), "r"(x[4][2]), "r"(x[4][3]), "r"(x[5][0]), "r"(x[5][1]), "r"(x[5][2]), "r"(x[5][3]),
+      "r"(x[6][0]), "r"(x[6][1]), "r"(x[6][2]), "r"(x[6][3]), "r"(x[7][0]), "r"(x[7][1]), "r"(x[7][2]), "r"(x[7][3])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+}
+
+// First run (single pass, signs before the transform) with its input from tensor memory.
+template <int PASS>
+__device__ __forceinline__ void run_first_tmem(const Frags& f, uint32_t taddr, uint32_t out_base,
+                                               const uint32_t* pre_sw, int w, int lane, int g, int t) {
+  uint32_t d[8][4];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(d[0][0]), "=r"(d[0][1]), "=r"(d[0][2]), "=r"(d[0][3]), "=r"(d[1][0]), "=r"(d[1][1]), "=r"(d[1][2]),
+        "=r"(d[1][3]), "=r"(d[2][0]), "=r"(d[2][1]), "=r"(d[2][2]), "=r"(d[2][3]), "=r"(d[3][0]), "=r"(d[3][1]),
+        "=r"(d[3][2]), "=r"(d[3][3]), "=r"(d[4][0]), "=r"(d[4][1]), "=r"(d[4][2]), "=r"(d[4][3]), "=r"(d[5][0]),
+        "=r"(d[5][1]), "=r"(d[5][2]), "=r"(d[5][3]), "=r"(d[6][0]), "=r"(d[6][1]), "=r"(d[6][2]), "=r"(d[6][3]),
+        "=r"(d[7][0]), "=r"(d[7][1]), "=r"(d[7][2]), "=r"(d[7][3])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    uint32_t x[4] = {d[k][0], d[k][1], d[k][2], d[k][3]};
+    sign_bop<PASS>(x, pre_sw, w, k, g, t);
+    row_tf<PASS>(f, x, d[k]);
+    col_tf<PASS>(f, d[k]);
+  }
+  write_exchange<PASS>(d, out_base, w, g, t);
+}
+
 // Natural-order staging layout for the output: chunk c = p >> 3 of 8
 // consecutive positions, XOR-swizzled so both the gathering writer (varies
 // chunk bits 2,6,7 within a phase) and the linear copy-out reader (bits 0-2)

@@ -94,6 +94,13 @@ static int fht_call(bool backward, int dtype, const void* in, void* out, int64_t
     }
     return LWL_OK;
   }
+  if (!backward && mma16_forward_supported(dtype, L, flags)) {
+    if (mma16_forward(dtype, in, L, layers, seed, start, stop, out, reinterpret_cast<cudaStream_t>(stream)) != 0) {
+      set_error("2^16 forward launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+      return LWL_ERR_CUDA;
+    }
+    return LWL_OK;
+  }
   if (backward && mma_backward_supported(dtype, L, flags)) {
     size_t need = mma_backward_workspace_bytes(L, start, stop);
     if (need > 0 && (ws == nullptr || ws_bytes < need)) {
@@ -119,6 +126,7 @@ static size_t fht_ws(bool backward, int dtype, int64_t L, int64_t size, int laye
                      int64_t stop, unsigned flags) {
   if (validate_fht(dtype, L, size, layers, start, stop) != LWL_OK) return 0;
   if (!backward && mma_forward_supported(dtype, L, flags)) return 0;
+  if (!backward && mma16_forward_supported(dtype, L, flags)) return 0;
   if (backward && mma_backward_supported(dtype, L, flags)) return mma_backward_workspace_bytes(L, start, stop);
   FhtArgs a;
   std::memset(&a, 0, sizeof(a));
@@ -563,6 +571,7 @@ int lwl_fht_launch_count(int dtype, int64_t latent_size, int64_t size, int layer
   if (lwl::validate_fht(dtype, latent_size, size, layers, start, stop) != LWL_OK) return -1;
   if (stop == start) return 0;
   if (!backward && lwl::mma_forward_supported(dtype, latent_size, flags)) return 1;
+  if (!backward && lwl::mma16_forward_supported(dtype, latent_size, flags)) return 1;
   if (backward && lwl::mma_backward_supported(dtype, latent_size, flags)) return 2;
   lwl::FhtArgs a;
   std::memset(&a, 0, sizeof(a));

@@ -183,6 +183,163 @@ int launch_forward_t(const FwdGroup& G, cudaStream_t st) {
 }
 
 // ---------------------------------------------------------------------------
+// Block size 2^16 forward (16-bit dtypes): one CTA per block holds both 2^15
+// tiles in shared memory.  H_65536 = H_2 (position bit 15) (x) H_32768 (bits
+// 0-14) and the factors commute, so each layer does the one-bit "hi"
+// butterfly between the tiles first -- one pass over both tiles' fp16 buffers
+// that also applies the layer's signs -- and then the tensor-core 2^15
+// transform (pass B, pass A) of each tile.  The hi butterflies are
+// unnormalised (the block norm grows by sqrt(2) per layer; the power-of-two
+// prescale keeps every element inside fp16) and their 2^(-1/2) per layer is
+// folded into the output scale.  Layer 0's hi pass reads the latent from
+// global memory; the last layer ends with the staged copy-out of each tile.
+// No HBM workspace and one launch, where the general large-block path needs
+// an fp32 workspace pass per layer and per high-bit group.
+constexpr size_t kSmem16 = 3 * kB * 2 + 2 * 4 * kWordsPad * 4;
+
+__device__ __forceinline__ void unpack_h8(const uint4 v, float* f) {
+  const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 h = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
+    f[2 * i] = h.x;
+    f[2 * i + 1] = h.y;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    fht16_forward_kernel(const T* __restrict__ latent, int64_t L, int layers, uint32_t seed32, float scale_base,
+                         int64_t first_block, int64_t nblocks, int64_t start, int64_t stop, T* __restrict__ out) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint16_t* z0 = reinterpret_cast<uint16_t*>(smem);  // tile 0 (positions 0..32767 of the block)
+  uint16_t* z1 = z0 + kB;                           // tile 1 (positions 32768..65535)
+  uint16_t* xs = z1 + kB;                           // exchange buffer
+  uint32_t* sw = reinterpret_cast<uint32_t*>(xs + kB);  // [tile][layer][kWordsPad]
+  __shared__ float red[kThreads / 32];
+  __shared__ int k0_shared;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
+  const uint32_t zb[2] = {(uint32_t)__cvta_generic_to_shared(z0), (uint32_t)__cvta_generic_to_shared(z1)};
+  const uint32_t xb = (uint32_t)__cvta_generic_to_shared(xs);
+  Frags f;
+  make_frags(f, g, t, kLog);
+  // power-of-two prescale: the block norm (the padded latent) into [2^11, 2^12)
+  float ss = 0.0f;
+  for (int64_t i = tid; i < L; i += kThreads) {
+    const float v = Cvt<T>::to_f(latent[i]);
+    ss += v * v;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) red[w] = ss;
+  __syncthreads();
+  if (tid == 0) {
+    float s2 = 0.0f;
+    for (int i = 0; i < kThreads / 32; ++i) s2 += red[i];
+    int e = 0;
+    if (s2 > 0.0f) {
+      frexpf(sqrtf(s2), &e);
+      e -= 12;
+    }
+    k0_shared = e;
+  }
+  __syncthreads();
+  const int k0 = k0_shared;
+  const float in_scale = ldexpf(1.0f, -k0), out_scale = ldexpf(1.0f, k0) * scale_base;
+  const bool vec_ok = ((start & 7) == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+  const bool lat_vec = (reinterpret_cast<uintptr_t>(latent) & 15) == 0;
+
+  for (int64_t bi = blockIdx.x; bi < nblocks; bi += gridDim.x) {
+    const int64_t b = first_block + bi;
+    __syncthreads();  // the previous block's copy-out is done with the buffers and sign tables
+    // sign words of both tiles and all layers: tile j has words 1024 j .. of the block
+    for (int i = tid; i < 2 * (layers + 1) * kWords; i += kThreads) {
+      const int per = (layers + 1) * kWords, j = i / per, r = i - j * per, l = r / kWords, wd = r - l * kWords;
+      sw[(4 * j + l) * kWordsPad + spad(wd)] = sign_word(block_layer_key(seed32, b, l), 1024 * j + wd);
+    }
+    __syncthreads();
+    for (int l = 0; l < layers; ++l) {
+      // hi butterfly of layer l (signs S_l first), written in the pass-B input layout
+      const uint32_t* s0 = sw + (4 * 0 + l) * kWordsPad;
+      const uint32_t* s1 = sw + (4 * 1 + l) * kWordsPad;
+      for (int c = tid; c < kB / 8; c += kThreads) {
+        const int p0 = 8 * c;
+        float a[8], bv[8];
+        if (l == 0) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            float* v = j ? bv : a;
+            const int64_t q0 = (int64_t)kB * j + p0;
+            if (q0 + 8 <= L && lat_vec) {
+              const uint4 raw = __ldg(reinterpret_cast<const uint4*>(latent + q0));
+              const T* ev = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[e] = Cvt<T>::to_f(ev[e]) * in_scale;
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[e] = (q0 + e < L) ? Cvt<T>::to_f(latent[q0 + e]) * in_scale : 0.0f;
+            }
+          }
+        } else {
+          unpack_h8(*reinterpret_cast<const uint4*>(z0 + lay_ab(p0)), a);
+          unpack_h8(*reinterpret_cast<const uint4*>(z1 + lay_ab(p0)), bv);
+        }
+        // sign bit set -> +1, clear -> -1 (block_fht.py:55-81)
+        const uint32_t m0 = s0[spad(p0 >> 5)] >> (p0 & 31), m1 = s1[spad(p0 >> 5)] >> (p0 & 31);
+        uint32_t o0[4], o1[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          float u[2], v[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const float x0 = ((m0 >> (e + h)) & 1u) ? a[e + h] : -a[e + h];
+            const float x1 = ((m1 >> (e + h)) & 1u) ? bv[e + h] : -bv[e + h];
+            u[h] = x0 + x1;
+            v[h] = x0 - x1;
+          }
+          o0[e >> 1] = pack_h2(u[0], u[1]);
+          o1[e >> 1] = pack_h2(v[0], v[1]);
+        }
+        *reinterpret_cast<uint4*>(z0 + lay_ab(p0)) = make_uint4(o0[0], o0[1], o0[2], o0[3]);
+        *reinterpret_cast<uint4*>(z1 + lay_ab(p0)) = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+      }
+      __syncthreads();
+      // 2^15 transform of each tile: pass B (z_j -> x), pass A (x -> z_j), or
+      // in the last layer pass A with the last signs, staged through z_j
+      // (consumed by pass B) and copied out
+#pragma unroll 1
+      for (int j = 0; j < 2; ++j) {
+        run<1, false, false>(f, zb[j], xb, nullptr, nullptr, w, lane, g, t);
+        __syncthreads();
+        if (l + 1 < layers) {
+          run<0, false, false>(f, xb, zb[j], nullptr, nullptr, w, lane, g, t);
+        } else {
+          run_final<T>(f, xb, zb[j], j ? z1 : z0, sw + (4 * j + layers) * kWordsPad, out_scale, out, 2 * b + j,
+                       start, stop, vec_ok, w, lane, g, t);
+        }
+        __syncthreads();
+      }
+    }
+  }
+}
+
+template <typename T>
+int launch_forward16_t(const void* latent, int64_t L, int layers, uint64_t seed, int64_t start, int64_t stop,
+                       void* out, cudaStream_t st) {
+  const int64_t B = 2 * kB;
+  const int64_t first = start / B, last = (stop + B - 1) / B;
+  if (last <= first) return 0;
+  if (!set_max_smem((const void*)fht16_forward_kernel<T>, (int)kSmem16)) return -1;
+  const int64_t nb = last - first, sms = sm_count();
+  const int grid = (int)(nb < sms ? nb : sms);
+  const float scale_base = (float)(std::pow(layer_correction(kLog), layers) * std::pow(2.0, -0.5 * layers));
+  fht16_forward_kernel<T><<<grid, kThreads, kSmem16, st>>>(reinterpret_cast<const T*>(latent), L, layers,
+                                                           fold_seed(seed), scale_base, first, nb, start, stop,
+                                                           reinterpret_cast<T*>(out));
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// ---------------------------------------------------------------------------
 // Backward: grad_z = sum_b [S0 Ĥ S1 ... Ĥ S_layers g_b][0:L].  Same runs as the
 // forward with the sign layers reversed; the per-block result (fp32, from the
 // last column transform) is accumulated across the blocks a CTA processes in
@@ -1102,6 +1259,19 @@ int mma_forward_grouped(int dtype, int count, const lwl_fht_forward_desc* descs,
 }  // namespace lwl
 
 namespace lwl {
+
+bool mma16_forward_supported(int dtype, int64_t latent_size, unsigned flags) {
+  if (flags & LWL_FLAG_EXACT) return false;
+  if (dtype != LWL_BF16 && dtype != LWL_F16) return false;
+  return next_pow2(latent_size) == 2 * fmma::kB;
+}
+
+int mma16_forward(int dtype, const void* latent, int64_t L, int layers, uint64_t seed, int64_t start, int64_t stop,
+                  void* out, cudaStream_t st) {
+  if (dtype == LWL_BF16)
+    return fmma::launch_forward16_t<__nv_bfloat16>(latent, L, layers, seed, start, stop, out, st);
+  return fmma::launch_forward16_t<__half>(latent, L, layers, seed, start, stop, out, st);
+}
 
 bool mma_backward_supported(int dtype, int64_t latent_size, unsigned flags) {
   return mma_forward_supported(dtype, latent_size, flags);

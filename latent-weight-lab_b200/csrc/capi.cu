@@ -113,6 +113,19 @@ static int fht_call(bool backward, int dtype, const void* in, void* out, int64_t
     }
     return LWL_OK;
   }
+  if (backward && mma16_forward_supported(dtype, L, flags)) {
+    const size_t need = mma16_backward_workspace_bytes(L, start, stop);
+    if (need > 0 && (ws == nullptr || ws_bytes < need)) {
+      set_error("workspace of %zu bytes required, %zu given", need, ws ? ws_bytes : (size_t)0);
+      return LWL_ERR_WORKSPACE;
+    }
+    if (mma16_backward(dtype, in, L, layers, seed, start, stop, out, ws, reinterpret_cast<cudaStream_t>(stream)) !=
+        0) {
+      set_error("2^16 backward launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+      return LWL_ERR_CUDA;
+    }
+    return LWL_OK;
+  }
   FhtPlan plan;
   plan_fht(a, plan);
   if (plan.ws_bytes > 0 && (ws == nullptr || ws_bytes < plan.ws_bytes)) {
@@ -128,6 +141,7 @@ static size_t fht_ws(bool backward, int dtype, int64_t L, int64_t size, int laye
   if (!backward && mma_forward_supported(dtype, L, flags)) return 0;
   if (!backward && mma16_forward_supported(dtype, L, flags)) return 0;
   if (backward && mma_backward_supported(dtype, L, flags)) return mma_backward_workspace_bytes(L, start, stop);
+  if (backward && mma16_forward_supported(dtype, L, flags)) return mma16_backward_workspace_bytes(L, start, stop);
   FhtArgs a;
   std::memset(&a, 0, sizeof(a));
   a.dtype = dtype;
@@ -573,6 +587,7 @@ int lwl_fht_launch_count(int dtype, int64_t latent_size, int64_t size, int layer
   if (!backward && lwl::mma_forward_supported(dtype, latent_size, flags)) return 1;
   if (!backward && lwl::mma16_forward_supported(dtype, latent_size, flags)) return 1;
   if (backward && lwl::mma_backward_supported(dtype, latent_size, flags)) return 2;
+  if (backward && lwl::mma16_forward_supported(dtype, latent_size, flags)) return 2;
   lwl::FhtArgs a;
   std::memset(&a, 0, sizeof(a));
   a.dtype = dtype;

@@ -654,6 +654,197 @@ int launch_backward_t(const void* grad, int64_t L, int layers, int n, uint32_t s
 
 
 // ---------------------------------------------------------------------------
+// Block size 2^16 backward (16-bit dtypes): the transposed chain
+// grad_z = sum_b [S0 H S1 ... H S_layers g_b][0:L] with the same building
+// blocks as fht16_forward_kernel -- per step a hi pass (with that step's
+// signs) and the 2^15 transform of each tile; the last pass A multiplies by
+// S0 and accumulates into tensor memory (both tiles: 512 columns, 65536 fp32
+// partial sums per CTA).  Each CTA writes one [L] partial row, tile by tile
+// through shared memory; fht15_reduce_kernel sums the rows deterministically.
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    fht16_backward_kernel(const T* __restrict__ grad, int64_t L, int layers, uint32_t seed32, float scale_base,
+                          int64_t first_block, int64_t nblocks, int64_t start, int64_t stop,
+                          float* __restrict__ partial) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint16_t* z0 = reinterpret_cast<uint16_t*>(smem);
+  uint16_t* z1 = z0 + kB;
+  uint16_t* xs = z1 + kB;
+  uint32_t* sw = reinterpret_cast<uint32_t*>(xs + kB);  // [tile][layer][kWordsPad]
+  __shared__ float red[kThreads / 32];
+  __shared__ uint32_t tmem_base_shared;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
+  const uint32_t zb[2] = {(uint32_t)__cvta_generic_to_shared(z0), (uint32_t)__cvta_generic_to_shared(z1)};
+  const uint32_t xb = (uint32_t)__cvta_generic_to_shared(xs);
+  Frags f;
+  make_frags(f, g, t, kLog);
+
+  if (w == 0) {
+    uint32_t dst = (uint32_t)__cvta_generic_to_shared(&tmem_base_shared);
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;\n" ::"r"(dst));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;\n");
+  // warp w: lanes 32*(w%4).., columns 64*(w/4).. of tile 0 and 256 + 64*(w/4).. of tile 1
+  const uint32_t tbase = tmem_base_shared + ((uint32_t)(32 * (w & 3)) << 16) + (uint32_t)(64 * (w >> 2));
+  {
+    float zf[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < 16; ++k) tmem_st8(tbase + 8 * (k & 7) + 256 * (k >> 3), zf);
+    tmem_wait_st();
+  }
+  const bool vec_ok = ((start & 7) == 0) && ((reinterpret_cast<uintptr_t>(grad) & 15) == 0);
+
+  for (int64_t bi = blockIdx.x; bi < nblocks; bi += gridDim.x) {
+    const int64_t b = first_block + bi;
+    const int64_t bbase = b * 2 * kB;
+    __syncthreads();  // the previous block's final runs are done with the buffers and sign tables
+    for (int i = tid; i < 2 * (layers + 1) * kWords; i += kThreads) {
+      const int per = (layers + 1) * kWords, j = i / per, r = i - j * per, l = r / kWords, wd = r - l * kWords;
+      sw[(4 * j + l) * kWordsPad + spad(wd)] = sign_word(block_layer_key(seed32, b, l), 1024 * j + wd);
+    }
+    // 8 gradient values of tile j at tile position p0 (zero outside [start, stop))
+    auto load8 = [&](int j, int p0, float* v) {
+      const int64_t gi = bbase + (int64_t)kB * j + p0;
+      if (vec_ok && gi >= start && gi + 8 <= stop) {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(grad + (gi - start)));
+        const T* ev = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = Cvt<T>::to_f(ev[e]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int64_t gg = gi + e;
+          v[e] = (gg >= start && gg < stop) ? Cvt<T>::to_f(grad[gg - start]) : 0.0f;
+        }
+      }
+    };
+    // squared norm of the block's gradient (read again from L2 by the first hi pass)
+    float ss = 0.0f;
+    for (int c = tid; c < 2 * (kB / 8); c += kThreads) {
+      float v[8];
+      load8(c >= kB / 8, 8 * (c & (kB / 8 - 1)), v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[w] = ss;
+    __syncthreads();
+    int k0 = 0;
+    {
+      float s2 = 0.0f;
+      for (int i = 0; i < kThreads / 32; ++i) s2 += red[i];
+      if (s2 > 0.0f) {
+        frexpf(sqrtf(s2), &k0);
+        k0 -= 12;
+      }
+    }
+    const float in_scale = ldexpf(1.0f, -k0), scale = ldexpf(1.0f, k0) * scale_base;
+    for (int st = 0; st < layers; ++st) {
+      const int l = layers - st;  // signs S_l before this step's transform
+      const uint32_t* s0 = sw + (4 * 0 + l) * kWordsPad;
+      const uint32_t* s1 = sw + (4 * 1 + l) * kWordsPad;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int p0 = 8 * (tid + kThreads * q);
+        float a[8], bv[8];
+        if (st == 0) {
+          load8(0, p0, a);
+          load8(1, p0, bv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            a[e] *= in_scale;
+            bv[e] *= in_scale;
+          }
+        } else {
+          unpack_h8(*reinterpret_cast<const uint4*>(z0 + lay_ab(p0)), a);
+          unpack_h8(*reinterpret_cast<const uint4*>(z1 + lay_ab(p0)), bv);
+        }
+        const uint32_t m0 = s0[spad(p0 >> 5)] >> (p0 & 31), m1 = s1[spad(p0 >> 5)] >> (p0 & 31);
+        uint32_t o0[4], o1[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          float u[2], v[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const float x0 = ((m0 >> (e + h)) & 1u) ? a[e + h] : -a[e + h];
+            const float x1 = ((m1 >> (e + h)) & 1u) ? bv[e + h] : -bv[e + h];
+            u[h] = x0 + x1;
+            v[h] = x0 - x1;
+          }
+          o0[e >> 1] = pack_h2(u[0], u[1]);
+          o1[e >> 1] = pack_h2(v[0], v[1]);
+        }
+        *reinterpret_cast<uint4*>(z0 + lay_ab(p0)) = make_uint4(o0[0], o0[1], o0[2], o0[3]);
+        *reinterpret_cast<uint4*>(z1 + lay_ab(p0)) = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+      }
+      __syncthreads();
+#pragma unroll 1
+      for (int j = 0; j < 2; ++j) {
+        run<1, false, false>(f, zb[j], xb, nullptr, nullptr, w, lane, g, t);
+        __syncthreads();
+        if (st + 1 < layers)
+          run<0, false, false>(f, xb, zb[j], nullptr, nullptr, w, lane, g, t);
+        else
+          run_final_acc(f, xb, sw + (4 * j + 0) * kWordsPad, scale, tbase + 256 * j, w, lane, g, t);
+        __syncthreads();
+      }
+    }
+  }
+  // this CTA's partial row, one tile at a time through shared memory (fp32,
+  // 128 KB over z0 | z1) for coalesced stores
+  float* prow = reinterpret_cast<float*>(smem);
+#pragma unroll 1
+  for (int j = 0; j < 2; ++j) {
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float acc[8];
+      tmem_ld8(tbase + 256 * j + 8 * k, acc);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int R = g + 8 * ((i >> 1) & 1), C = 2 * t + (i & 1) + 8 * (i >> 2);
+        prow[dep_a(w, k, R, C)] = acc[i];
+      }
+    }
+    __syncthreads();
+    for (int64_t pp = tid; pp < kB; pp += kThreads) {
+      const int64_t q = (int64_t)kB * j + pp;
+      if (q < L) partial[(int64_t)blockIdx.x * L + q] = prow[pp];
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;\n");
+  if (w == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;\n" ::"r"(tmem_base_shared));
+}
+
+template <typename T>
+int launch_backward16_t(const void* grad, int64_t L, int layers, uint64_t seed, int64_t start, int64_t stop,
+                        void* grad_latent, void* workspace, cudaStream_t st) {
+  const int64_t B = 2 * kB;
+  const int64_t first = start / B, last = (stop + B - 1) / B;
+  if (last <= first) return cudaMemsetAsync(grad_latent, 0, size_t(L) * 2, st) == cudaSuccess ? 0 : -1;
+  int* err = reinterpret_cast<int*>(workspace);
+  float* partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kBwdHeader);
+  if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess) return -1;
+  if (!set_max_smem((const void*)fht16_backward_kernel<T>, (int)kSmem16)) return -1;
+  const int64_t nb = last - first, sms = sm_count();
+  const int grid = (int)(nb < sms ? nb : sms);
+  const float scale_base = (float)(std::pow(layer_correction(kLog), layers) * std::pow(2.0, -0.5 * layers));
+  fht16_backward_kernel<T><<<grid, kThreads, kSmem16, st>>>(reinterpret_cast<const T*>(grad), L, layers,
+                                                            fold_seed(seed), scale_base, first, nb, start, stop,
+                                                            partial);
+  if (cudaGetLastError() != cudaSuccess) return -1;
+  const int rb = (int)((L + 255) / 256);
+  fht15_reduce_kernel<T><<<rb, 256, 0, st>>>(partial, grid, L, err, reinterpret_cast<T*>(grad_latent));
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// ---------------------------------------------------------------------------
 // Grouped backward: the latent gradients of many generators in one launch
 // (the projection side of a model's weight cache).  The 2^15-coordinate
 // tiles of all descriptors form one list; CTA c takes the contiguous range
@@ -1271,6 +1462,21 @@ int mma16_forward(int dtype, const void* latent, int64_t L, int layers, uint64_t
   if (dtype == LWL_BF16)
     return fmma::launch_forward16_t<__nv_bfloat16>(latent, L, layers, seed, start, stop, out, st);
   return fmma::launch_forward16_t<__half>(latent, L, layers, seed, start, stop, out, st);
+}
+
+size_t mma16_backward_workspace_bytes(int64_t latent_size, int64_t start, int64_t stop) {
+  const int64_t B = 2 * fmma::kB;
+  const int64_t nb = (stop + B - 1) / B - start / B;
+  if (nb <= 0) return 0;
+  const int64_t grid = nb < fmma::sm_count() ? nb : fmma::sm_count();
+  return fmma::kBwdHeader + size_t(grid) * size_t(latent_size) * 4;
+}
+
+int mma16_backward(int dtype, const void* grad, int64_t L, int layers, uint64_t seed, int64_t start, int64_t stop,
+                   void* grad_latent, void* workspace, cudaStream_t st) {
+  if (dtype == LWL_BF16)
+    return fmma::launch_backward16_t<__nv_bfloat16>(grad, L, layers, seed, start, stop, grad_latent, workspace, st);
+  return fmma::launch_backward16_t<__half>(grad, L, layers, seed, start, stop, grad_latent, workspace, st);
 }
 
 bool mma_backward_supported(int dtype, int64_t latent_size, unsigned flags) {

@@ -23,6 +23,9 @@ int mma_backward_grouped(int dtype, int count, const lwl_fht_backward_desc* desc
 bool mma16_forward_supported(int dtype, int64_t latent_size, unsigned flags);
 int mma16_forward(int dtype, const void* latent, int64_t L, int layers, uint64_t seed, int64_t start, int64_t stop,
                   void* out, cudaStream_t st);
+size_t mma16_backward_workspace_bytes(int64_t latent_size, int64_t start, int64_t stop);
+int mma16_backward(int dtype, const void* grad, int64_t L, int layers, uint64_t seed, int64_t start, int64_t stop,
+                   void* grad_latent, void* workspace, cudaStream_t st);
 bool mma_backward_supported(int dtype, int64_t latent_size, unsigned flags);
 size_t mma_backward_workspace_bytes(int64_t latent_size, int64_t start, int64_t stop);
 int mma_backward(int dtype, const void* grad, int64_t latent_size, int layers, uint64_t seed, int64_t start,

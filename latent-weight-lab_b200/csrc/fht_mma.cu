@@ -339,6 +339,12 @@ int launch_forward16_t(const void* latent, int64_t L, int layers, uint64_t seed,
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
+// fp32 partial-row staging of a 2^15 tile: the accumulator-layout writer varies
+// position bits 5-7 and 9-10 across a warp (32-way bank conflicts on the
+// plain index); XOR-ing them into bits 0-4 spreads them over all 32 banks,
+// and the consecutive reader sees a warp-uniform XOR.
+__device__ __forceinline__ int prow_swz(int p) { return p ^ (((p >> 5) & 7) | (((p >> 9) & 3) << 3)); }
+
 // ---------------------------------------------------------------------------
 // Backward: grad_z = sum_b [S0 Ĥ S1 ... Ĥ S_layers g_b][0:L].  Same runs as the
 // forward with the sign layers reversed; the per-block result (fp32, from the
@@ -593,14 +599,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       int R = g + 8 * ((i >> 1) & 1), C = 2 * t + (i & 1) + 8 * (i >> 2);
-      prow[dep_a(w, k, R, C)] = acc[i];
+      prow[prow_swz(dep_a(w, k, R, C))] = acc[i];
     }
   }
   __syncthreads();
   // fold the 2^(15-n) blocks of the tile onto the latent positions
   for (int64_t p = tid; p < L; p += kThreads) {
     float v = 0.0f;
-    for (int j = 0; j < (kB >> n); ++j) v += prow[(j << n) + p];
+    for (int j = 0; j < (kB >> n); ++j) v += prow[prow_swz((int)((j << n) + p))];
     partial[(int64_t)blockIdx.x * L + p] = v;
   }
   asm volatile("tcgen05.fence::before_thread_sync;\n");
@@ -807,13 +813,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int R = g + 8 * ((i >> 1) & 1), C = 2 * t + (i & 1) + 8 * (i >> 2);
-        prow[dep_a(w, k, R, C)] = acc[i];
+        prow[prow_swz(dep_a(w, k, R, C))] = acc[i];
       }
     }
     __syncthreads();
     for (int64_t pp = tid; pp < kB; pp += kThreads) {
       const int64_t q = (int64_t)kB * j + pp;
-      if (q < L) partial[(int64_t)blockIdx.x * L + q] = prow[pp];
+      if (q < L) partial[(int64_t)blockIdx.x * L + q] = prow[prow_swz((int)pp)];
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;\n");
@@ -939,14 +945,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         int R = g + 8 * ((i >> 1) & 1), C = 2 * t + (i & 1) + 8 * (i >> 2);
-        prow[dep_a(w, k, R, C)] = acc[i];
+        prow[prow_swz(dep_a(w, k, R, C))] = acc[i];
       }
     }
     __syncthreads();
     float* dst = partial + D.row_off + (int64_t)(blockIdx.x - D.c_lo) * D.L;
     for (int64_t p = tid; p < D.L; p += kThreads) {
       float v = 0.0f;
-      for (int j = 0; j < (kB >> D.n); ++j) v += prow[(j << D.n) + p];
+      for (int j = 0; j < (kB >> D.n); ++j) v += prow[prow_swz((int)((j << D.n) + p))];
       dst[p] = v;
     }
     zero_acc();

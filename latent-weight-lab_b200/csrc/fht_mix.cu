@@ -150,13 +150,14 @@ __global__ void __launch_bounds__(kThreads) fht_mix_kernel(const T* __restrict__
         v[e] = (ln & m) ? o - v[e] : v[e] + o;
       }
     }
-    if (nw > 1) {  // bits of the warp within the row, through shared memory
+    if (nw > 1) {  // bits of the warp within the row, through shared memory; only the
+                   // nw warps of the row group synchronise (named barrier 1 + rg)
       // row group rg owns buf[rg * P, (rg + 1) * P); element p at p ^ ((p >> 5) & 31),
       // conflict-free for the lane-strided writes and the consecutive gathers
       float* rbuf = buf + rg * P;
 #pragma unroll
       for (int e = 0; e < E; ++e) rbuf[swz(pos(e))] = v[e];
-      __syncthreads();
+      asm volatile("bar.sync %0, %1;\n" ::"r"(1 + rg), "r"(nw * 32) : "memory");
       for (int q = wr * 32 + lane; q < 1024; q += nw * 32) {
         float u[8];
 #pragma unroll
@@ -174,10 +175,10 @@ __global__ void __launch_bounds__(kThreads) fht_mix_kernel(const T* __restrict__
         for (int j = 0; j < 8; ++j)
           if (j < nw) rbuf[swz(q + 1024 * j)] = u[j];
       }
-      __syncthreads();
+      asm volatile("bar.sync %0, %1;\n" ::"r"(1 + rg), "r"(nw * 32) : "memory");
 #pragma unroll
       for (int e = 0; e < E; ++e) v[e] = rbuf[swz(pos(e))];
-      __syncthreads();  // the next rows' exchange reuses the buffer
+      asm volatile("bar.sync %0, %1;\n" ::"r"(1 + rg), "r"(nw * 32) : "memory");  // the next rows' exchange reuses the buffer
     }
     T* yr = y + row * F;
 #pragma unroll

@@ -113,7 +113,7 @@ static int fht_call(bool backward, int dtype, const void* in, void* out, int64_t
     }
     return LWL_OK;
   }
-  if (backward && mma16_forward_supported(dtype, L, flags)) {
+  if (backward && mma16_backward_supported(dtype, L, flags)) {
     const size_t need = mma16_backward_workspace_bytes(L, start, stop);
     if (need > 0 && (ws == nullptr || ws_bytes < need)) {
       set_error("workspace of %zu bytes required, %zu given", need, ws ? ws_bytes : (size_t)0);
@@ -141,7 +141,7 @@ static size_t fht_ws(bool backward, int dtype, int64_t L, int64_t size, int laye
   if (!backward && mma_forward_supported(dtype, L, flags)) return 0;
   if (!backward && mma16_forward_supported(dtype, L, flags)) return 0;
   if (backward && mma_backward_supported(dtype, L, flags)) return mma_backward_workspace_bytes(L, start, stop);
-  if (backward && mma16_forward_supported(dtype, L, flags)) return mma16_backward_workspace_bytes(L, start, stop);
+  if (backward && mma16_backward_supported(dtype, L, flags)) return mma16_backward_workspace_bytes(L, start, stop);
   FhtArgs a;
   std::memset(&a, 0, sizeof(a));
   a.dtype = dtype;
@@ -587,7 +587,7 @@ int lwl_fht_launch_count(int dtype, int64_t latent_size, int64_t size, int layer
   if (!backward && lwl::mma_forward_supported(dtype, latent_size, flags)) return 1;
   if (!backward && lwl::mma16_forward_supported(dtype, latent_size, flags)) return 1;
   if (backward && lwl::mma_backward_supported(dtype, latent_size, flags)) return 2;
-  if (backward && lwl::mma16_forward_supported(dtype, latent_size, flags)) return 2;
+  if (backward && lwl::mma16_backward_supported(dtype, latent_size, flags)) return 2;
   lwl::FhtArgs a;
   std::memset(&a, 0, sizeof(a));
   a.dtype = dtype;

@@ -21,6 +21,7 @@ int mma_forward_grouped(int dtype, int count, const lwl_fht_forward_desc* descs,
 size_t mma_backward_grouped_workspace_bytes(int count, const lwl_fht_backward_desc* descs);
 int mma_backward_grouped(int dtype, int count, const lwl_fht_backward_desc* descs, void* workspace, cudaStream_t st);
 bool mma16_forward_supported(int dtype, int64_t latent_size, unsigned flags);
+bool mma16_backward_supported(int dtype, int64_t latent_size, unsigned flags);
 int mma16_forward(int dtype, const void* latent, int64_t L, int layers, uint64_t seed, int64_t start, int64_t stop,
                   void* out, cudaStream_t st);
 size_t mma16_backward_workspace_bytes(int64_t latent_size, int64_t start, int64_t stop);

@@ -168,7 +168,7 @@ def test_slice_equals_full_bf16_headline_shape(nat):
     assert torch.equal(part, full[5 * B + 77: 9 * B + 3])
 
 
-@pytest.mark.parametrize("logb", range(5, 17))
+@pytest.mark.parametrize("logb", range(5, 18))
 @pytest.mark.parametrize("layers", [1, 2, 3])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
 def test_every_block_size_half(nat, logb, layers, dtype):
@@ -180,6 +180,18 @@ def test_every_block_size_half(nat, logb, layers, dtype):
     start, stop = B // 3, size - 7
     _check_forward(nat, L, size, layers, 321, start, stop, dtype)
     _check_backward(nat, L, size, layers, 321, start, stop, dtype)
+
+
+@pytest.mark.parametrize("L, size, start, stop", [
+    (131072, 20 * 131072, 0, 20 * 131072),  # aligned: vector loads and stores, every CTA several blocks
+    (108618, 7 * 131072 + 5, 8, 7 * 131072 - 8),  # the C1 latent, ragged slice
+    (70000, 160 * 131072, 131072, 159 * 131072),  # more blocks than SMs, block-aligned slice
+])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+def test_block_2p17_tensor_memory_kernels(nat, L, size, start, stop, dtype):
+    """Padded block 2^17: the whole block parked in tensor memory between layers."""
+    _check_forward(nat, L, size, 3, 2024, start, stop, dtype)
+    _check_backward(nat, L, size, 3, 2024, start, stop, dtype)
 
 
 @pytest.mark.parametrize("logb", range(17, 24))

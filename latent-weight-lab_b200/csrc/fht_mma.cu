@@ -197,6 +197,25 @@ int launch_forward_t(const FwdGroup& G, cudaStream_t st) {
 // an fp32 workspace pass per layer and per high-bit group.
 constexpr size_t kSmem16 = 3 * kB * 2 + 2 * 4 * kWordsPad * 4;
 
+// Two 16-bit values of type T packed in one word (low half first) -> float2.
+template <typename T> __device__ __forceinline__ float2 w2f(uint32_t v);
+template <> __device__ __forceinline__ float2 w2f<__half>(uint32_t v) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&v));
+}
+template <> __device__ __forceinline__ float2 w2f<__nv_bfloat16>(uint32_t v) {
+  return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+}
+
+// Raw words of src[q0 .. q0+7] restricted to [0, n): the elements outside are
+// zero.  For the chunks a caller's predicated 16-byte load did not cover.
+__device__ __forceinline__ void gather8_words(const uint16_t* src, int64_t q0, int64_t n, uint32_t* r) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const uint32_t bits = (q0 + e >= 0 && q0 + e < n) ? (uint32_t)src[q0 + e] : 0u;
+    r[e >> 1] = (e & 1) ? (r[e >> 1] | (bits << 16)) : bits;
+  }
+}
+
 __device__ __forceinline__ void unpack_h8(const uint4 v, float* f) {
   const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -247,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int k0 = k0_shared;
   const float in_scale = ldexpf(1.0f, -k0), out_scale = ldexpf(1.0f, k0) * scale_base;
   const bool vec_ok = ((start & 7) == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
-  const bool lat_vec = (reinterpret_cast<uintptr_t>(latent) & 15) == 0;
+  const bool lat_tail = (reinterpret_cast<uintptr_t>(latent) & 15) != 0 || (L & 7) != 0;
 
   for (int64_t bi = blockIdx.x; bi < nblocks; bi += gridDim.x) {
     const int64_t b = first_block + bi;
@@ -262,46 +281,67 @@ __global__ void __launch_bounds__(kThreads, 1)
       // hi butterfly of layer l (signs S_l first), written in the pass-B input layout
       const uint32_t* s0 = sw + (4 * 0 + l) * kWordsPad;
       const uint32_t* s1 = sw + (4 * 1 + l) * kWordsPad;
-      for (int c = tid; c < kB / 8; c += kThreads) {
-        const int p0 = 8 * c;
-        float a[8], bv[8];
-        if (l == 0) {
+      // two halves of 4 chunks per thread; in layer 0 all 8 latent loads of a
+      // half are in flight at once (predicated 16-byte loads when the latent
+      // is aligned and a multiple of 8 long, else element by element)
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        uint32_t raw[2][16];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) {
+            const int p0 = 8 * (tid + kThreads * (4 * h + qq));
+            uint4 r = make_uint4(0u, 0u, 0u, 0u);
+            if (l > 0) {
+              r = *reinterpret_cast<const uint4*>((j ? z1 : z0) + lay_ab(p0));
+            } else if (!lat_tail) {
+              const int64_t q0 = (int64_t)kB * j + p0;
+              if (q0 < L) r = __ldg(reinterpret_cast<const uint4*>(latent + q0));
+            }
+            raw[j][4 * qq] = r.x, raw[j][4 * qq + 1] = r.y, raw[j][4 * qq + 2] = r.z, raw[j][4 * qq + 3] = r.w;
+          }
+        }
+        if (l == 0 && lat_tail) {
 #pragma unroll
           for (int j = 0; j < 2; ++j) {
-            float* v = j ? bv : a;
-            const int64_t q0 = (int64_t)kB * j + p0;
-            if (q0 + 8 <= L && lat_vec) {
-              const uint4 raw = __ldg(reinterpret_cast<const uint4*>(latent + q0));
-              const T* ev = reinterpret_cast<const T*>(&raw);
 #pragma unroll
-              for (int e = 0; e < 8; ++e) v[e] = Cvt<T>::to_f(ev[e]) * in_scale;
-            } else {
+            for (int qq = 0; qq < 4; ++qq)
+              gather8_words(reinterpret_cast<const uint16_t*>(latent),
+                            (int64_t)kB * j + 8 * (tid + kThreads * (4 * h + qq)), L, &raw[j][4 * qq]);
+          }
+        }
 #pragma unroll
-              for (int e = 0; e < 8; ++e) v[e] = (q0 + e < L) ? Cvt<T>::to_f(latent[q0 + e]) * in_scale : 0.0f;
+        for (int qq = 0; qq < 4; ++qq) {
+          const int p0 = 8 * (tid + kThreads * (4 * h + qq));
+          float a[8], bv[8];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f0 = l == 0 ? w2f<T>(raw[0][4 * qq + e]) : w2f<__half>(raw[0][4 * qq + e]);
+            const float2 f1 = l == 0 ? w2f<T>(raw[1][4 * qq + e]) : w2f<__half>(raw[1][4 * qq + e]);
+            const float sc = l == 0 ? in_scale : 1.0f;
+            a[2 * e] = f0.x * sc, a[2 * e + 1] = f0.y * sc;
+            bv[2 * e] = f1.x * sc, bv[2 * e + 1] = f1.y * sc;
+          }
+          // sign bit set -> +1, clear -> -1 (block_fht.py:55-81)
+          const uint32_t m0 = s0[spad(p0 >> 5)] >> (p0 & 31), m1 = s1[spad(p0 >> 5)] >> (p0 & 31);
+          uint32_t o0[4], o1[4];
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            float u[2], v[2];
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const float x0 = ((m0 >> (e + hh)) & 1u) ? a[e + hh] : -a[e + hh];
+              const float x1 = ((m1 >> (e + hh)) & 1u) ? bv[e + hh] : -bv[e + hh];
+              u[hh] = x0 + x1;
+              v[hh] = x0 - x1;
             }
+            o0[e >> 1] = pack_h2(u[0], u[1]);
+            o1[e >> 1] = pack_h2(v[0], v[1]);
           }
-        } else {
-          unpack_h8(*reinterpret_cast<const uint4*>(z0 + lay_ab(p0)), a);
-          unpack_h8(*reinterpret_cast<const uint4*>(z1 + lay_ab(p0)), bv);
+          *reinterpret_cast<uint4*>(z0 + lay_ab(p0)) = make_uint4(o0[0], o0[1], o0[2], o0[3]);
+          *reinterpret_cast<uint4*>(z1 + lay_ab(p0)) = make_uint4(o1[0], o1[1], o1[2], o1[3]);
         }
-        // sign bit set -> +1, clear -> -1 (block_fht.py:55-81)
-        const uint32_t m0 = s0[spad(p0 >> 5)] >> (p0 & 31), m1 = s1[spad(p0 >> 5)] >> (p0 & 31);
-        uint32_t o0[4], o1[4];
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          float u[2], v[2];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const float x0 = ((m0 >> (e + h)) & 1u) ? a[e + h] : -a[e + h];
-            const float x1 = ((m1 >> (e + h)) & 1u) ? bv[e + h] : -bv[e + h];
-            u[h] = x0 + x1;
-            v[h] = x0 - x1;
-          }
-          o0[e >> 1] = pack_h2(u[0], u[1]);
-          o1[e >> 1] = pack_h2(v[0], v[1]);
-        }
-        *reinterpret_cast<uint4*>(z0 + lay_ab(p0)) = make_uint4(o0[0], o0[1], o0[2], o0[3]);
-        *reinterpret_cast<uint4*>(z1 + lay_ab(p0)) = make_uint4(o1[0], o1[1], o1[2], o1[3]);
       }
       __syncthreads();
       // 2^15 transform of each tile: pass B (z_j -> x), pass A (x -> z_j), or
@@ -441,6 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const float in_scale = ldexpf(1.0f, -k0), out_scale = ldexpf(1.0f, k0) * scale_base;
   const bool vec_ok = ((start & 7) == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
   const bool lat_vec = (reinterpret_cast<uintptr_t>(latent) & 15) == 0;
+  const bool lat_tail = !lat_vec || (L & 7) != 0;
 
   for (int64_t bi = blockIdx.x; bi < nblocks; bi += gridDim.x) {
     const int64_t b = first_block + bi;
@@ -456,24 +497,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int h = 0; h < 2; ++h) {
         uint32_t v[4][16];
         if (l == 0) {
+          // all 16 loads in flight at once (predicated 16-byte loads) when the
+          // latent is aligned and a multiple of 8 long; else chunk by chunk
+          if (!lat_tail) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+#pragma unroll
+              for (int qq = 0; qq < 4; ++qq) {
+                const int64_t q0 = (int64_t)kB * j + 8 * (tid + kThreads * (4 * h + qq));
+                uint4 r = make_uint4(0u, 0u, 0u, 0u);
+                if (q0 < L) r = __ldg(reinterpret_cast<const uint4*>(latent + q0));
+                v[j][4 * qq] = r.x, v[j][4 * qq + 1] = r.y, v[j][4 * qq + 2] = r.z, v[j][4 * qq + 3] = r.w;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+#pragma unroll
+              for (int qq = 0; qq < 4; ++qq)
+                gather8_words(reinterpret_cast<const uint16_t*>(latent),
+                              (int64_t)kB * j + 8 * (tid + kThreads * (4 * h + qq)), L, &v[j][4 * qq]);
+            }
+          }
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
 #pragma unroll
-            for (int qq = 0; qq < 4; ++qq) {
-              const int c = tid + kThreads * (4 * h + qq);
-              const int64_t q0 = (int64_t)kB * j + 8 * c;
-              float fv[8];
-              if (q0 + 8 <= L && lat_vec) {
-                const uint4 raw = __ldg(reinterpret_cast<const uint4*>(latent + q0));
-                const T* ev = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) fv[e] = Cvt<T>::to_f(ev[e]) * in_scale;
-              } else {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) fv[e] = (q0 + e < L) ? Cvt<T>::to_f(latent[q0 + e]) * in_scale : 0.0f;
-              }
-#pragma unroll
-              for (int e = 0; e < 4; ++e) v[j][4 * qq + e] = pack_h2(fv[2 * e], fv[2 * e + 1]);
+            for (int r = 0; r < 16; ++r) {
+              const float2 fv = w2f<T>(v[j][r]);
+              v[j][r] = pack_h2(fv.x * in_scale, fv.y * in_scale);
             }
           }
         } else {
@@ -936,29 +987,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int per = (layers + 1) * kWords, j = i / per, r = i - j * per, l = r / kWords, wd = r - l * kWords;
       sw[(4 * j + l) * kWordsPad + spad(wd)] = sign_word(block_layer_key(seed32, b, l), 1024 * j + wd);
     }
-    // 8 gradient values of tile j at tile position p0 (zero outside [start, stop))
-    auto load8 = [&](int j, int p0, float* v) {
-      const int64_t gi = bbase + (int64_t)kB * j + p0;
-      if (vec_ok && gi >= start && gi + 8 <= stop) {
-        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(grad + (gi - start)));
-        const T* ev = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = Cvt<T>::to_f(ev[e]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int64_t gg = gi + e;
-          v[e] = (gg >= start && gg < stop) ? Cvt<T>::to_f(grad[gg - start]) : 0.0f;
-        }
-      }
-    };
+    // Gradient chunks (8 values at block position p) as raw words: 16-byte
+    // loads with no per-chunk test when the whole block lies inside
+    // [start, stop) and the gradient is aligned, else element by element
+    // with zeros outside the slice.
+    const bool blk_full = vec_ok && bbase >= start && bbase + 2 * kB <= stop;
+    const uint16_t* g16 = reinterpret_cast<const uint16_t*>(grad);
     // squared norm of the block's gradient (read again from L2 by the first hi pass)
     float ss = 0.0f;
-    for (int c = tid; c < 2 * (kB / 8); c += kThreads) {
-      float v[8];
-      load8(c >= kB / 8, 8 * (c & (kB / 8 - 1)), v);
+#pragma unroll 1
+    for (int h = 0; h < 2; ++h) {
+      uint32_t r[8][4];
+      if (blk_full) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+        for (int u = 0; u < 8; ++u) {
+          const uint4 x = __ldg(reinterpret_cast<const uint4*>(grad + (bbase - start) + 8 * (tid + kThreads * (8 * h + u))));
+          r[u][0] = x.x, r[u][1] = x.y, r[u][2] = x.z, r[u][3] = x.w;
+        }
+      } else {
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          gather8_words(g16, bbase + 8 * (tid + kThreads * (8 * h + u)) - start, stop - start, r[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 fv = w2f<T>(r[u][e]);
+          ss += fv.x * fv.x + fv.y * fv.y;
+        }
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -978,39 +1036,67 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int l = layers - st;  // signs S_l before this step's transform
       const uint32_t* s0 = sw + (4 * 0 + l) * kWordsPad;
       const uint32_t* s1 = sw + (4 * 1 + l) * kWordsPad;
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        uint32_t raw[2][16];
+        if (st > 0) {
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const int p0 = 8 * (tid + kThreads * q);
-        float a[8], bv[8];
-        if (st == 0) {
-          load8(0, p0, a);
-          load8(1, p0, bv);
+          for (int j = 0; j < 2; ++j) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            a[e] *= in_scale;
-            bv[e] *= in_scale;
+            for (int qq = 0; qq < 4; ++qq) {
+              const uint4 x = *reinterpret_cast<const uint4*>((j ? z1 : z0) + lay_ab(8 * (tid + kThreads * (4 * h + qq))));
+              raw[j][4 * qq] = x.x, raw[j][4 * qq + 1] = x.y, raw[j][4 * qq + 2] = x.z, raw[j][4 * qq + 3] = x.w;
+            }
+          }
+        } else if (blk_full) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq) {
+              const uint4 x = __ldg(reinterpret_cast<const uint4*>(grad + (bbase - start) + (int64_t)kB * j +
+                                                                   8 * (tid + kThreads * (4 * h + qq))));
+              raw[j][4 * qq] = x.x, raw[j][4 * qq + 1] = x.y, raw[j][4 * qq + 2] = x.z, raw[j][4 * qq + 3] = x.w;
+            }
           }
         } else {
-          unpack_h8(*reinterpret_cast<const uint4*>(z0 + lay_ab(p0)), a);
-          unpack_h8(*reinterpret_cast<const uint4*>(z1 + lay_ab(p0)), bv);
-        }
-        const uint32_t m0 = s0[spad(p0 >> 5)] >> (p0 & 31), m1 = s1[spad(p0 >> 5)] >> (p0 & 31);
-        uint32_t o0[4], o1[4];
 #pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          float u[2], v[2];
+          for (int j = 0; j < 2; ++j) {
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const float x0 = ((m0 >> (e + h)) & 1u) ? a[e + h] : -a[e + h];
-            const float x1 = ((m1 >> (e + h)) & 1u) ? bv[e + h] : -bv[e + h];
-            u[h] = x0 + x1;
-            v[h] = x0 - x1;
+            for (int qq = 0; qq < 4; ++qq)
+              gather8_words(g16, bbase + (int64_t)kB * j + 8 * (tid + kThreads * (4 * h + qq)) - start, stop - start,
+                            &raw[j][4 * qq]);
           }
-          o0[e >> 1] = pack_h2(u[0], u[1]);
-          o1[e >> 1] = pack_h2(v[0], v[1]);
         }
-        *reinterpret_cast<uint4*>(z0 + lay_ab(p0)) = make_uint4(o0[0], o0[1], o0[2], o0[3]);
-        *reinterpret_cast<uint4*>(z1 + lay_ab(p0)) = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+          const int p0 = 8 * (tid + kThreads * (4 * h + qq));
+          float a[8], bv[8];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f0 = st == 0 ? w2f<T>(raw[0][4 * qq + e]) : w2f<__half>(raw[0][4 * qq + e]);
+            const float2 f1 = st == 0 ? w2f<T>(raw[1][4 * qq + e]) : w2f<__half>(raw[1][4 * qq + e]);
+            const float sc = st == 0 ? in_scale : 1.0f;
+            a[2 * e] = f0.x * sc, a[2 * e + 1] = f0.y * sc;
+            bv[2 * e] = f1.x * sc, bv[2 * e + 1] = f1.y * sc;
+          }
+          const uint32_t m0 = s0[spad(p0 >> 5)] >> (p0 & 31), m1 = s1[spad(p0 >> 5)] >> (p0 & 31);
+          uint32_t o0[4], o1[4];
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            float u[2], v[2];
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const float x0 = ((m0 >> (e + hh)) & 1u) ? a[e + hh] : -a[e + hh];
+              const float x1 = ((m1 >> (e + hh)) & 1u) ? bv[e + hh] : -bv[e + hh];
+              u[hh] = x0 + x1;
+              v[hh] = x0 - x1;
+            }
+            o0[e >> 1] = pack_h2(u[0], u[1]);
+            o1[e >> 1] = pack_h2(v[0], v[1]);
+          }
+          *reinterpret_cast<uint4*>(z0 + lay_ab(p0)) = make_uint4(o0[0], o0[1], o0[2], o0[3]);
+          *reinterpret_cast<uint4*>(z1 + lay_ab(p0)) = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+        }
       }
       __syncthreads();
 #pragma unroll 1
@@ -1121,29 +1207,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int per = (layers + 1) * kWords, j = i / per, r = i - j * per, l = r / kWords, wd = r - l * kWords;
       sw[(4 * j + l) * kWordsPad + spad(wd)] = sign_word(block_layer_key(seed32, b, l), 1024 * j + wd);
     }
-    // 8 gradient values of tile j at tile position p0 (zero outside [start, stop))
-    auto load8 = [&](int j, int p0, float* v) {
-      const int64_t gi = bbase + (int64_t)kB * j + p0;
-      if (vec_ok && gi >= start && gi + 8 <= stop) {
-        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(grad + (gi - start)));
-        const T* ev = reinterpret_cast<const T*>(&raw);
+    // gradient chunks as raw words, as in fht16_backward_kernel
+    const bool blk_full = vec_ok && bbase >= start && bbase + 4 * kB <= stop;
+    const uint16_t* g16 = reinterpret_cast<const uint16_t*>(grad);
+    float ss = 0.0f;
+#pragma unroll 1
+    for (int h = 0; h < 4; ++h) {
+      uint32_t r[8][4];
+      if (blk_full) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = Cvt<T>::to_f(ev[e]);
+        for (int u = 0; u < 8; ++u) {
+          const uint4 x = __ldg(reinterpret_cast<const uint4*>(grad + (bbase - start) + 8 * (tid + kThreads * (8 * h + u))));
+          r[u][0] = x.x, r[u][1] = x.y, r[u][2] = x.z, r[u][3] = x.w;
+        }
       } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int64_t gg = gi + e;
-          v[e] = (gg >= start && gg < stop) ? Cvt<T>::to_f(grad[gg - start]) : 0.0f;
+        for (int u = 0; u < 8; ++u)
+          gather8_words(g16, bbase + 8 * (tid + kThreads * (8 * h + u)) - start, stop - start, r[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 fv = w2f<T>(r[u][e]);
+          ss += fv.x * fv.x + fv.y * fv.y;
         }
       }
-    };
-    float ss = 0.0f;
-#pragma unroll 8
-    for (int c = tid; c < 4 * (kB / 8); c += kThreads) {
-      float v[8];
-      load8(c / (kB / 8), 8 * (c & (kB / 8 - 1)), v);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -1165,14 +1254,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int h = 0; h < 2; ++h) {
         uint32_t v[4][16];
         if (st == 0) {
+          if (blk_full) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+#pragma unroll
+              for (int qq = 0; qq < 4; ++qq) {
+                const uint4 x = __ldg(reinterpret_cast<const uint4*>(grad + (bbase - start) + (int64_t)kB * j +
+                                                                     8 * (tid + kThreads * (4 * h + qq))));
+                v[j][4 * qq] = x.x, v[j][4 * qq + 1] = x.y, v[j][4 * qq + 2] = x.z, v[j][4 * qq + 3] = x.w;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+#pragma unroll
+              for (int qq = 0; qq < 4; ++qq)
+                gather8_words(g16, bbase + (int64_t)kB * j + 8 * (tid + kThreads * (4 * h + qq)) - start,
+                              stop - start, &v[j][4 * qq]);
+            }
+          }
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
 #pragma unroll
-            for (int qq = 0; qq < 4; ++qq) {
-              float fv[8];
-              load8(j, 8 * (tid + kThreads * (4 * h + qq)), fv);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) v[j][4 * qq + e] = pack_h2(fv[2 * e] * in_scale, fv[2 * e + 1] * in_scale);
+            for (int r = 0; r < 16; ++r) {
+              const float2 fv = w2f<T>(v[j][r]);
+              v[j][r] = pack_h2(fv.x * in_scale, fv.y * in_scale);
             }
           }
         } else {

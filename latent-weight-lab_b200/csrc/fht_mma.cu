@@ -363,242 +363,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// ---------------------------------------------------------------------------
-// Block size 2^17 forward (16-bit dtypes): the whole block lives in tensor
-// memory between layers.  Each thread parks chunks tid + 512 q (q = 0..7, 8
-// fp16 values each) of each of the 4 tiles in its own TMEM lane: 4 columns per
-// chunk, 32 per tile, 128 per thread; the 4 warps of a lane quadrant fill the
-// 512 columns.  Per layer:
-//   hi pass -- the 2-bit butterfly between the tiles (position bits 15, 16)
-//              with the layer's signs, entirely in registers/TMEM (layer 0
-//              reads the latent from global memory instead);
-//   per tile -- unpark into the shared buffer (pass-B input layout), pass B,
-//              pass A, park again; the last layer ends in the staged copy-out.
-// Shared memory: one tile buffer, the exchange buffer and the 4 tiles' sign
-// tables.  The hi butterflies carry their 1/2, so the block norm stays in
-// [2^11, 2^12) after the prescale.
-constexpr size_t kSmem17 = 2 * kB * 2 + 16 * kWordsPad * 4;
-
-__device__ __forceinline__ void tm_ld16(uint32_t taddr, uint32_t* r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tm_st16(uint32_t taddr, const uint32_t* r) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
-          taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-}
-__device__ __forceinline__ void tm_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
-__device__ __forceinline__ void tm_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
-
-// Signs S_l (bit set -> +1) and the 4-point butterfly over tile bits 0 and 1
-// with its 1/2, in fp32 and rounded once (block_fht.py:55-81), on the half h
-// (chunks tid + kThreads q, q = 4h .. 4h+3) of a thread's parked values:
-// v[j][4 (q - 4h) + e] holds positions 8 (tid + kThreads q) + 2e, +1 of tile j.
-__device__ __forceinline__ void hi4_butterfly(uint32_t (&v)[4][16], const uint32_t* sw, int l, int h, int tid) {
-#pragma unroll
-  for (int qq = 0; qq < 4; ++qq) {
-    const int p0 = 8 * (tid + kThreads * (4 * h + qq));
-    uint32_t m[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) m[j] = sw[(4 * j + l) * kWordsPad + spad(p0 >> 5)] >> (p0 & 31);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int r = 4 * qq + e;
-      float2 a[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        a[j] = __half22float2(*reinterpret_cast<const __half2*>(&v[j][r]));
-        if (!((m[j] >> (2 * e)) & 1u)) a[j].x = -a[j].x;
-        if (!((m[j] >> (2 * e + 1)) & 1u)) a[j].y = -a[j].y;
-      }
-      const float2 b0 = make_float2(a[0].x + a[1].x, a[0].y + a[1].y);
-      const float2 b1 = make_float2(a[0].x - a[1].x, a[0].y - a[1].y);
-      const float2 b2 = make_float2(a[2].x + a[3].x, a[2].y + a[3].y);
-      const float2 b3 = make_float2(a[2].x - a[3].x, a[2].y - a[3].y);
-      v[0][r] = pack_h2(0.5f * (b0.x + b2.x), 0.5f * (b0.y + b2.y));
-      v[1][r] = pack_h2(0.5f * (b1.x + b3.x), 0.5f * (b1.y + b3.y));
-      v[2][r] = pack_h2(0.5f * (b0.x - b2.x), 0.5f * (b0.y - b2.y));
-      v[3][r] = pack_h2(0.5f * (b1.x - b3.x), 0.5f * (b1.y - b3.y));
-    }
-  }
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kThreads, 1)
-    fht17_forward_kernel(const T* __restrict__ latent, int64_t L, int layers, uint32_t seed32, float scale_base,
-                         int64_t first_block, int64_t nblocks, int64_t start, int64_t stop, T* __restrict__ out) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  uint16_t* zs = reinterpret_cast<uint16_t*>(smem);      // the tile being transformed
-  uint16_t* xs = zs + kB;                                // exchange buffer
-  uint32_t* sw = reinterpret_cast<uint32_t*>(xs + kB);   // [tile][layer][kWordsPad]
-  __shared__ float red[kThreads / 32];
-  __shared__ int k0_shared;
-  __shared__ uint32_t tmem_base_shared;
-  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
-  const uint32_t zb = (uint32_t)__cvta_generic_to_shared(zs), xb = (uint32_t)__cvta_generic_to_shared(xs);
-  Frags f;
-  make_frags(f, g, t, kLog);
-  if (w == 0) {
-    uint32_t dst = (uint32_t)__cvta_generic_to_shared(&tmem_base_shared);
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;\n" ::"r"(dst));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
-  }
-  asm volatile("tcgen05.fence::before_thread_sync;\n");
-  __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;\n");
-  // tile j of this thread: lanes of quadrant w % 4, columns 128 * (w / 4) + 32 j (+ 4 q for chunk q)
-  const uint32_t tt0 = tmem_base_shared + ((uint32_t)(32 * (w & 3)) << 16) + (uint32_t)(128 * (w >> 2));
-
-  // power-of-two prescale: the block norm (the padded latent) into [2^11, 2^12)
-  float ss = 0.0f;
-  for (int64_t i = tid; i < L; i += kThreads) {
-    const float v = Cvt<T>::to_f(latent[i]);
-    ss += v * v;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if (lane == 0) red[w] = ss;
-  __syncthreads();
-  if (tid == 0) {
-    float s2 = 0.0f;
-    for (int i = 0; i < kThreads / 32; ++i) s2 += red[i];
-    int e = 0;
-    if (s2 > 0.0f) {
-      frexpf(sqrtf(s2), &e);
-      e -= 12;
-    }
-    k0_shared = e;
-  }
-  __syncthreads();
-  const int k0 = k0_shared;
-  const float in_scale = ldexpf(1.0f, -k0), out_scale = ldexpf(1.0f, k0) * scale_base;
-  const bool vec_ok = ((start & 7) == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
-  const bool lat_vec = (reinterpret_cast<uintptr_t>(latent) & 15) == 0;
-  const bool lat_tail = !lat_vec || (L & 7) != 0;
-
-  for (int64_t bi = blockIdx.x; bi < nblocks; bi += gridDim.x) {
-    const int64_t b = first_block + bi;
-    __syncthreads();  // the previous block's copy-out is done with the buffers and sign tables
-    for (int i = tid; i < 4 * (layers + 1) * kWords; i += kThreads) {
-      const int per = (layers + 1) * kWords, j = i / per, r = i - j * per, l = r / kWords, wd = r - l * kWords;
-      sw[(4 * j + l) * kWordsPad + spad(wd)] = sign_word(block_layer_key(seed32, b, l), 1024 * j + wd);
-    }
-    __syncthreads();
-    for (int l = 0; l < layers; ++l) {
-      // hi pass: two halves of 4 chunks per thread, 4 tiles x 4 chunks x 4 registers
-#pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        uint32_t v[4][16];
-        if (l == 0) {
-          // all 16 loads in flight at once (predicated 16-byte loads) when the
-          // latent is aligned and a multiple of 8 long; else chunk by chunk
-          if (!lat_tail) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-#pragma unroll
-              for (int qq = 0; qq < 4; ++qq) {
-                const int64_t q0 = (int64_t)kB * j + 8 * (tid + kThreads * (4 * h + qq));
-                uint4 r = make_uint4(0u, 0u, 0u, 0u);
-                if (q0 < L) r = __ldg(reinterpret_cast<const uint4*>(latent + q0));
-                v[j][4 * qq] = r.x, v[j][4 * qq + 1] = r.y, v[j][4 * qq + 2] = r.z, v[j][4 * qq + 3] = r.w;
-              }
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-#pragma unroll
-              for (int qq = 0; qq < 4; ++qq)
-                gather8_words(reinterpret_cast<const uint16_t*>(latent),
-                              (int64_t)kB * j + 8 * (tid + kThreads * (4 * h + qq)), L, &v[j][4 * qq]);
-            }
-          }
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-#pragma unroll
-            for (int r = 0; r < 16; ++r) {
-              const float2 fv = w2f<T>(v[j][r]);
-              v[j][r] = pack_h2(fv.x * in_scale, fv.y * in_scale);
-            }
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) tm_ld16(tt0 + 32 * j + 16 * h, v[j]);
-          tm_wait_ld();
-        }
-        hi4_butterfly(v, sw, l, h, tid);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) tm_st16(tt0 + 32 * j + 16 * h, v[j]);
-      }
-      tm_wait_st();
-      // per tile: unpark into the shared buffer, the 2^15 transform, park again
-#pragma unroll 1
-      for (int j = 0; j < 4; ++j) {
-#pragma unroll 1
-        for (int h = 0; h < 2; ++h) {
-          uint32_t v[16];
-          tm_ld16(tt0 + 32 * j + 16 * h, v);
-          tm_wait_ld();
-#pragma unroll
-          for (int qq = 0; qq < 4; ++qq) {
-            const int p0 = 8 * (tid + kThreads * (4 * h + qq));
-            *reinterpret_cast<uint4*>(zs + lay_ab(p0)) = make_uint4(v[4 * qq], v[4 * qq + 1], v[4 * qq + 2], v[4 * qq + 3]);
-          }
-        }
-        __syncthreads();
-        run<1, false, false>(f, zb, xb, nullptr, nullptr, w, lane, g, t);
-        __syncthreads();
-        if (l + 1 < layers) {
-          run<0, false, false>(f, xb, zb, nullptr, nullptr, w, lane, g, t);
-          __syncthreads();
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
-            uint32_t v[16];
-#pragma unroll
-            for (int qq = 0; qq < 4; ++qq) {
-              const int p0 = 8 * (tid + kThreads * (4 * h + qq));
-              const uint4 u = *reinterpret_cast<const uint4*>(zs + lay_ab(p0));
-              v[4 * qq] = u.x, v[4 * qq + 1] = u.y, v[4 * qq + 2] = u.z, v[4 * qq + 3] = u.w;
-            }
-            tm_st16(tt0 + 32 * j + 16 * h, v);
-          }
-          tm_wait_st();
-        } else {
-          run_final<T>(f, xb, zb, zs, sw + (4 * j + layers) * kWordsPad, out_scale, out, 4 * b + j, start, stop,
-                       vec_ok, w, lane, g, t);
-        }
-        __syncthreads();
-      }
-    }
-  }
-  asm volatile("tcgen05.fence::before_thread_sync;\n");
-  __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;\n");
-  if (w == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;\n" ::"r"(tmem_base_shared));
-}
-
-template <typename T>
-int launch_forward17_t(const void* latent, int64_t L, int layers, uint64_t seed, int64_t start, int64_t stop,
-                       void* out, cudaStream_t st) {
-  const int64_t B = 4 * kB;
-  const int64_t first = start / B, last = (stop + B - 1) / B;
-  if (last <= first) return 0;
-  if (!set_max_smem((const void*)fht17_forward_kernel<T>, (int)kSmem17)) return -1;
-  const int64_t nb = last - first, sms = sm_count();
-  const int grid = (int)(nb < sms ? nb : sms);
-  const float scale_base = (float)std::pow(layer_correction(kLog), layers);
-  fht17_forward_kernel<T><<<grid, kThreads, kSmem17, st>>>(reinterpret_cast<const T*>(latent), L, layers,
-                                                           fold_seed(seed), scale_base, first, nb, start, stop,
-                                                           reinterpret_cast<T*>(out));
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
-}
-
 template <typename T>
 int launch_forward16_t(const void* latent, int64_t L, int layers, uint64_t seed, int64_t start, int64_t stop,
                        void* out, cudaStream_t st) {
@@ -620,6 +384,7 @@ int launch_forward16_t(const void* latent, int64_t L, int layers, uint64_t seed,
 // plain index); XOR-ing them into bits 0-4 spreads them over all 32 banks,
 // and the consecutive reader sees a warp-uniform XOR.
 __device__ __forceinline__ int prow_swz(int p) { return p ^ (((p >> 5) & 7) | (((p >> 9) & 3) << 3)); }
+
 
 // ---------------------------------------------------------------------------
 // Backward: grad_z = sum_b [S0 Ĥ S1 ... Ĥ S_layers g_b][0:L].  Same runs as the
@@ -1161,251 +926,7 @@ int launch_backward16_t(const void* grad, int64_t L, int layers, uint64_t seed, 
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
-// ---------------------------------------------------------------------------
-// Block size 2^17 backward (16-bit dtypes): the transposed chain of
-// fht17_forward_kernel.  The block is parked in tensor memory between steps
-// exactly as in the forward (512 columns), so there is no room for the fp32
-// accumulator there: each tile's final pass A (scale, signs S0) is held in
-// registers, staged as fp32 over the two shared buffers (128 KB) and added,
-// coalesced, into this CTA's partial row (L2-resident: one [L] fp32 row per
-// CTA); the CTA's first block writes its row instead of reading it.
-template <typename T>
-__global__ void __launch_bounds__(kThreads, 1)
-    fht17_backward_kernel(const T* __restrict__ grad, int64_t L, int layers, uint32_t seed32, float scale_base,
-                          int64_t first_block, int64_t nblocks, int64_t start, int64_t stop,
-                          float* __restrict__ partial) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  uint16_t* zs = reinterpret_cast<uint16_t*>(smem);
-  uint16_t* xs = zs + kB;
-  uint32_t* sw = reinterpret_cast<uint32_t*>(xs + kB);  // [tile][layer][kWordsPad]
-  float* stg = reinterpret_cast<float*>(smem);          // fp32 staging of one tile over zs | xs
-  __shared__ float red[kThreads / 32];
-  __shared__ uint32_t tmem_base_shared;
-  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
-  const uint32_t zb = (uint32_t)__cvta_generic_to_shared(zs), xb = (uint32_t)__cvta_generic_to_shared(xs);
-  Frags f;
-  make_frags(f, g, t, kLog);
-  if (w == 0) {
-    uint32_t dst = (uint32_t)__cvta_generic_to_shared(&tmem_base_shared);
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;\n" ::"r"(dst));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
-  }
-  asm volatile("tcgen05.fence::before_thread_sync;\n");
-  __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;\n");
-  const uint32_t tt0 = tmem_base_shared + ((uint32_t)(32 * (w & 3)) << 16) + (uint32_t)(128 * (w >> 2));
-  const bool vec_ok = ((start & 7) == 0) && ((reinterpret_cast<uintptr_t>(grad) & 15) == 0);
-  float* prow = partial + (int64_t)blockIdx.x * L;
-  const bool row_vec = (L & 3) == 0 && (reinterpret_cast<uintptr_t>(partial) & 15) == 0;
-
-  for (int64_t bi = blockIdx.x; bi < nblocks; bi += gridDim.x) {
-    const int64_t b = first_block + bi;
-    const int64_t bbase = b * 4 * kB;
-    const bool first = bi == blockIdx.x;
-    __syncthreads();  // the previous block's row update is done with the buffers and sign tables
-    for (int i = tid; i < 4 * (layers + 1) * kWords; i += kThreads) {
-      const int per = (layers + 1) * kWords, j = i / per, r = i - j * per, l = r / kWords, wd = r - l * kWords;
-      sw[(4 * j + l) * kWordsPad + spad(wd)] = sign_word(block_layer_key(seed32, b, l), 1024 * j + wd);
-    }
-    // gradient chunks as raw words, as in fht16_backward_kernel
-    const bool blk_full = vec_ok && bbase >= start && bbase + 4 * kB <= stop;
-    const uint16_t* g16 = reinterpret_cast<const uint16_t*>(grad);
-    float ss = 0.0f;
-#pragma unroll 1
-    for (int h = 0; h < 4; ++h) {
-      uint32_t r[8][4];
-      if (blk_full) {
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const uint4 x = __ldg(reinterpret_cast<const uint4*>(grad + (bbase - start) + 8 * (tid + kThreads * (8 * h + u))));
-          r[u][0] = x.x, r[u][1] = x.y, r[u][2] = x.z, r[u][3] = x.w;
-        }
-      } else {
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          gather8_words(g16, bbase + 8 * (tid + kThreads * (8 * h + u)) - start, stop - start, r[u]);
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 fv = w2f<T>(r[u][e]);
-          ss += fv.x * fv.x + fv.y * fv.y;
-        }
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) red[w] = ss;
-    __syncthreads();
-    int k0 = 0;
-    {
-      float s2 = 0.0f;
-      for (int i = 0; i < kThreads / 32; ++i) s2 += red[i];
-      if (s2 > 0.0f) {
-        frexpf(sqrtf(s2), &k0);
-        k0 -= 12;
-      }
-    }
-    const float in_scale = ldexpf(1.0f, -k0), scale = ldexpf(1.0f, k0) * scale_base;
-    for (int st = 0; st < layers; ++st) {
-      const int l = layers - st;  // signs S_l before this step's transform
-#pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        uint32_t v[4][16];
-        if (st == 0) {
-          if (blk_full) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-#pragma unroll
-              for (int qq = 0; qq < 4; ++qq) {
-                const uint4 x = __ldg(reinterpret_cast<const uint4*>(grad + (bbase - start) + (int64_t)kB * j +
-                                                                     8 * (tid + kThreads * (4 * h + qq))));
-                v[j][4 * qq] = x.x, v[j][4 * qq + 1] = x.y, v[j][4 * qq + 2] = x.z, v[j][4 * qq + 3] = x.w;
-              }
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-#pragma unroll
-              for (int qq = 0; qq < 4; ++qq)
-                gather8_words(g16, bbase + (int64_t)kB * j + 8 * (tid + kThreads * (4 * h + qq)) - start,
-                              stop - start, &v[j][4 * qq]);
-            }
-          }
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-#pragma unroll
-            for (int r = 0; r < 16; ++r) {
-              const float2 fv = w2f<T>(v[j][r]);
-              v[j][r] = pack_h2(fv.x * in_scale, fv.y * in_scale);
-            }
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) tm_ld16(tt0 + 32 * j + 16 * h, v[j]);
-          tm_wait_ld();
-        }
-        hi4_butterfly(v, sw, l, h, tid);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) tm_st16(tt0 + 32 * j + 16 * h, v[j]);
-      }
-      tm_wait_st();
-#pragma unroll 1
-      for (int j = 0; j < 4; ++j) {
-#pragma unroll 1
-        for (int h = 0; h < 2; ++h) {
-          uint32_t v[16];
-          tm_ld16(tt0 + 32 * j + 16 * h, v);
-          tm_wait_ld();
-#pragma unroll
-          for (int qq = 0; qq < 4; ++qq) {
-            const int p0 = 8 * (tid + kThreads * (4 * h + qq));
-            *reinterpret_cast<uint4*>(zs + lay_ab(p0)) = make_uint4(v[4 * qq], v[4 * qq + 1], v[4 * qq + 2], v[4 * qq + 3]);
-          }
-        }
-        __syncthreads();
-        run<1, false, false>(f, zb, xb, nullptr, nullptr, w, lane, g, t);
-        __syncthreads();
-        if (st + 1 < layers) {
-          run<0, false, false>(f, xb, zb, nullptr, nullptr, w, lane, g, t);
-          __syncthreads();
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
-            uint32_t v[16];
-#pragma unroll
-            for (int qq = 0; qq < 4; ++qq) {
-              const int p0 = 8 * (tid + kThreads * (4 * h + qq));
-              const uint4 u = *reinterpret_cast<const uint4*>(zs + lay_ab(p0));
-              v[4 * qq] = u.x, v[4 * qq + 1] = u.y, v[4 * qq + 2] = u.z, v[4 * qq + 3] = u.w;
-            }
-            tm_st16(tt0 + 32 * j + 16 * h, v);
-          }
-          tm_wait_st();
-        } else {
-          // final pass A of tile j: scale, signs S0, fp32 staging, row update
-          const uint32_t* s0 = sw + (4 * j + 0) * kWordsPad;
-          float c[8][8];
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            final_tile(f, xb, w, k, lane, c[k]);
-            // c[k][i]: row g + 8((i>>1)&1), column 2t + (i&1) + 8(i>>2) of pass A,
-            // i.e. position base + k + 8((i>>1)&1) + 16(i&1) + 2048(i>>2)
-            const int wb = dep_a(w, 0, g, 2 * t) >> 5;
-            const uint32_t u0 = ~s0[spad(wb)], u1 = ~s0[spad(wb + 64)];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int bit = k + 8 * ((i >> 1) & 1) + 16 * (i & 1);
-              const uint32_t u = (i >> 2) ? u1 : u0;
-              c[k][i] = __uint_as_float(__float_as_uint(c[k][i] * scale) ^ ((u << (31 - bit)) & 0x80000000u));
-            }
-          }
-          __syncthreads();  // every warp is done reading xs
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int R = g + 8 * ((i >> 1) & 1), C = 2 * t + (i & 1) + 8 * (i >> 2);
-              stg[prow_swz(dep_a(w, k, R, C))] = c[k][i];
-            }
-          }
-          __syncthreads();
-          // row update: the CTA's first block stores, later ones add with
-          // fire-and-forget reductions in L2 (no round trip; one thread owns
-          // each address, so the additions keep program order)
-          const int64_t q0 = (int64_t)kB * j;
-          if (first) {
-            for (int pp = tid; pp < kB; pp += kThreads) {
-              const int64_t q = q0 + pp;
-              if (q < L) prow[q] = stg[prow_swz(pp)];
-            }
-          } else if (row_vec) {
-            for (int pp = 4 * tid; pp < kB; pp += 4 * kThreads) {
-              const int64_t q = q0 + pp;
-              if (q < L)  // L % 4 == 0: all four are inside
-                asm volatile("red.global.v4.f32.add [%0], {%1, %2, %3, %4};\n" ::"l"(prow + q),
-                             "f"(stg[prow_swz(pp)]), "f"(stg[prow_swz(pp + 1)]), "f"(stg[prow_swz(pp + 2)]),
-                             "f"(stg[prow_swz(pp + 3)])
-                             : "memory");
-            }
-          } else {
-            for (int pp = tid; pp < kB; pp += kThreads) {
-              const int64_t q = q0 + pp;
-              if (q < L) atomicAdd(prow + q, stg[prow_swz(pp)]);
-            }
-          }
-        }
-        __syncthreads();
-      }
-    }
-  }
-  asm volatile("tcgen05.fence::before_thread_sync;\n");
-  __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;\n");
-  if (w == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;\n" ::"r"(tmem_base_shared));
-}
-
-template <typename T>
-int launch_backward17_t(const void* grad, int64_t L, int layers, uint64_t seed, int64_t start, int64_t stop,
-                        void* grad_latent, void* workspace, cudaStream_t st) {
-  const int64_t B = 4 * kB;
-  const int64_t first = start / B, last = (stop + B - 1) / B;
-  if (last <= first) return cudaMemsetAsync(grad_latent, 0, size_t(L) * 2, st) == cudaSuccess ? 0 : -1;
-  int* err = reinterpret_cast<int*>(workspace);
-  float* partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kBwdHeader);
-  if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess) return -1;
-  if (!set_max_smem((const void*)fht17_backward_kernel<T>, (int)kSmem17)) return -1;
-  const int64_t nb = last - first, sms = sm_count();
-  const int grid = (int)(nb < sms ? nb : sms);
-  const float scale_base = (float)std::pow(layer_correction(kLog), layers);
-  fht17_backward_kernel<T><<<grid, kThreads, kSmem17, st>>>(reinterpret_cast<const T*>(grad), L, layers,
-                                                            fold_seed(seed), scale_base, first, nb, start, stop,
-                                                            partial);
-  if (cudaGetLastError() != cudaSuccess) return -1;
-  const int rb = (int)((L + 255) / 256);
-  fht15_reduce_kernel<T><<<rb, 256, 0, st>>>(partial, grid, L, err, reinterpret_cast<T*>(grad_latent));
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
-}
+#include "fht_parked.cuh"
 
 // ---------------------------------------------------------------------------
 // Grouped backward: the latent gradients of many generators in one launch
@@ -2025,8 +1546,8 @@ int mma16_forward(int dtype, const void* latent, int64_t L, int layers, uint64_t
                   void* out, cudaStream_t st) {
   if (next_pow2(L) == 4 * fmma::kB) {
     if (dtype == LWL_BF16)
-      return fmma::launch_forward17_t<__nv_bfloat16>(latent, L, layers, seed, start, stop, out, st);
-    return fmma::launch_forward17_t<__half>(latent, L, layers, seed, start, stop, out, st);
+      return fmma::launch_forward_parked<__nv_bfloat16, 4>(latent, L, layers, seed, start, stop, out, st);
+    return fmma::launch_forward_parked<__half, 4>(latent, L, layers, seed, start, stop, out, st);
   }
   if (dtype == LWL_BF16)
     return fmma::launch_forward16_t<__nv_bfloat16>(latent, L, layers, seed, start, stop, out, st);
@@ -2049,8 +1570,8 @@ int mma16_backward(int dtype, const void* grad, int64_t L, int layers, uint64_t 
                    void* grad_latent, void* workspace, cudaStream_t st) {
   if (next_pow2(L) == 4 * fmma::kB) {
     if (dtype == LWL_BF16)
-      return fmma::launch_backward17_t<__nv_bfloat16>(grad, L, layers, seed, start, stop, grad_latent, workspace, st);
-    return fmma::launch_backward17_t<__half>(grad, L, layers, seed, start, stop, grad_latent, workspace, st);
+      return fmma::launch_backward_parked<__nv_bfloat16, 4>(grad, L, layers, seed, start, stop, grad_latent, workspace, st);
+    return fmma::launch_backward_parked<__half, 4>(grad, L, layers, seed, start, stop, grad_latent, workspace, st);
   }
   if (dtype == LWL_BF16)
     return fmma::launch_backward16_t<__nv_bfloat16>(grad, L, layers, seed, start, stop, grad_latent, workspace, st);

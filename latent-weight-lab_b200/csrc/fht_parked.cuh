@@ -8,7 +8,7 @@
 // owner reads or writes them (tcgen05.ld/st 32x32b.x16 and their waits), so
 // parking needs no barrier.  H_B = H_NT (x) H_32768 and the factors commute:
 //   hi pass   -- the butterfly between the tiles (position bits 15 and, for
-//                NT = 4, 16) on the parked chunks, in registers;
+//                NT = 4, 16) on the parked chunks, in packed fp16 registers;
 //   tile runs -- each tile unparked into shared memory, the tensor-core passes
 //                of the 2^15 transform (run, run_final), parked again.
 // Chunk slots: "by position" means chunk c holds positions 8c .. 8c+7 and sits
@@ -51,40 +51,46 @@ __device__ __forceinline__ void tm_wait_st() { asm volatile("tcgen05.wait::st.sy
 
 // The hi butterfly on half h of a thread's chunks (chunks tid + kThreads q,
 // q = 4h .. 4h+3; v[j][4 (q - 4h) + e] holds elements 2e, 2e+1 of chunk q of
-// tile j), in fp32 and rounded once.  With sgn (the sign table of tile 0 for
-// one layer; tile j's at +4 j kWordsPad) the signs come first, looked up by
-// position -- sign bit set -> +1 (block_fht.py:55-81).
+// tile j), in packed fp16.  With sgn (the sign table of tile 0 for one layer;
+// tile j's at +4 j kWordsPad) the signs come first, looked up by position --
+// sign bit set -> +1 (block_fht.py:55-81) -- as one XOR of the two fp16 sign
+// bits per word: ((~bits) & 3) * 0x40008000 puts bit 0 at bit 15 and bit 1 at
+// bit 31 (the partial products do not overlap).  A 1-bit butterfly rounds
+// exactly as an fp32 sum rounded once; the 2-bit one (NT = 4) pre-scales by
+// the exact 1/2 and rounds after each level.
 template <int NT>
 __device__ __forceinline__ void hi_butterfly(uint32_t (&v)[NT][16], const uint32_t* sgn, int h, int tid) {
+  const __half2 half2_05 = __float2half2_rn(0.5f);
 #pragma unroll
   for (int qq = 0; qq < 4; ++qq) {
     const int p0 = 8 * (tid + kThreads * (4 * h + qq));
     uint32_t m[NT];
 #pragma unroll
-    for (int j = 0; j < NT; ++j) m[j] = sgn ? sgn[4 * j * kWordsPad + spad(p0 >> 5)] >> (p0 & 31) : 0xffffffffu;
+    for (int j = 0; j < NT; ++j) m[j] = sgn ? ~(sgn[4 * j * kWordsPad + spad(p0 >> 5)] >> (p0 & 31)) : 0u;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int r = 4 * qq + e;
-      float2 a[NT];
+      __half2 a[NT];
 #pragma unroll
       for (int j = 0; j < NT; ++j) {
-        a[j] = __half22float2(*reinterpret_cast<const __half2*>(&v[j][r]));
-        if (!((m[j] >> (2 * e)) & 1u)) a[j].x = -a[j].x;
-        if (!((m[j] >> (2 * e + 1)) & 1u)) a[j].y = -a[j].y;
+        const uint32_t x = v[j][r] ^ ((((m[j] >> (2 * e)) & 3u) * 0x40008000u) & 0x80008000u);
+        a[j] = *reinterpret_cast<const __half2*>(&x);
+        if (NT == 4) a[j] = __hmul2(a[j], half2_05);
       }
+      __half2 o[NT];
       if (NT == 2) {
-        v[0][r] = pack_h2(a[0].x + a[1].x, a[0].y + a[1].y);
-        v[1][r] = pack_h2(a[0].x - a[1].x, a[0].y - a[1].y);
+        o[0] = __hadd2(a[0], a[1]);
+        o[1] = __hsub2(a[0], a[1]);
       } else {
-        const float2 b0 = make_float2(a[0].x + a[1].x, a[0].y + a[1].y);
-        const float2 b1 = make_float2(a[0].x - a[1].x, a[0].y - a[1].y);
-        const float2 b2 = make_float2(a[2].x + a[3].x, a[2].y + a[3].y);
-        const float2 b3 = make_float2(a[2].x - a[3].x, a[2].y - a[3].y);
-        v[0][r] = pack_h2(0.5f * (b0.x + b2.x), 0.5f * (b0.y + b2.y));
-        v[1][r] = pack_h2(0.5f * (b1.x + b3.x), 0.5f * (b1.y + b3.y));
-        v[2][r] = pack_h2(0.5f * (b0.x - b2.x), 0.5f * (b0.y - b2.y));
-        v[3][r] = pack_h2(0.5f * (b1.x - b3.x), 0.5f * (b1.y - b3.y));
+        const __half2 b0 = __hadd2(a[0], a[1]), b1 = __hsub2(a[0], a[1]);
+        const __half2 b2 = __hadd2(a[2], a[3]), b3 = __hsub2(a[2], a[3]);
+        o[0] = __hadd2(b0, b2);
+        o[1] = __hadd2(b1, b3);
+        o[2] = __hsub2(b0, b2);
+        o[3] = __hsub2(b1, b3);
       }
+#pragma unroll
+      for (int j = 0; j < NT; ++j) v[j][r] = *reinterpret_cast<const uint32_t*>(&o[j]);
     }
   }
 }

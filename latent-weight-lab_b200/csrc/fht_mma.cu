@@ -216,6 +216,23 @@ __device__ __forceinline__ void gather8_words(const uint16_t* src, int64_t q0, i
   }
 }
 
+// 1-bit hi butterfly of one chunk (8 values, 4 packed fp16 words) of tile 0
+// and tile 1 at the same positions, in place: signs first (m0 / m1 = the
+// inverted sign bits of the chunk from bit 0; sign bit set -> +1,
+// block_fht.py:55-81) as one XOR per word, then sum and difference.  An fp16
+// sum of two fp16 values rounds exactly like the fp32 sum rounded once.
+__device__ __forceinline__ void hi2_chunk(uint32_t* x0, uint32_t* x1, uint32_t m0, uint32_t m1) {
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const uint32_t u0 = x0[e] ^ ((((m0 >> (2 * e)) & 3u) * 0x40008000u) & 0x80008000u);
+    const uint32_t u1 = x1[e] ^ ((((m1 >> (2 * e)) & 3u) * 0x40008000u) & 0x80008000u);
+    const __half2 a0 = *reinterpret_cast<const __half2*>(&u0), a1 = *reinterpret_cast<const __half2*>(&u1);
+    const __half2 s = __hadd2(a0, a1), d = __hsub2(a0, a1);
+    x0[e] = *reinterpret_cast<const uint32_t*>(&s);
+    x1[e] = *reinterpret_cast<const uint32_t*>(&d);
+  }
+}
+
 __device__ __forceinline__ void unpack_h8(const uint4 v, float* f) {
   const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -311,34 +328,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                             (int64_t)kB * j + 8 * (tid + kThreads * (4 * h + qq)), L, &raw[j][4 * qq]);
           }
         }
+        if (l == 0) {  // the input words, scaled, into packed fp16
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+#pragma unroll
+            for (int r = 0; r < 16; ++r) {
+              const float2 fv = w2f<T>(raw[j][r]);
+              raw[j][r] = pack_h2(fv.x * in_scale, fv.y * in_scale);
+            }
+          }
+        }
 #pragma unroll
         for (int qq = 0; qq < 4; ++qq) {
           const int p0 = 8 * (tid + kThreads * (4 * h + qq));
-          float a[8], bv[8];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f0 = l == 0 ? w2f<T>(raw[0][4 * qq + e]) : w2f<__half>(raw[0][4 * qq + e]);
-            const float2 f1 = l == 0 ? w2f<T>(raw[1][4 * qq + e]) : w2f<__half>(raw[1][4 * qq + e]);
-            const float sc = l == 0 ? in_scale : 1.0f;
-            a[2 * e] = f0.x * sc, a[2 * e + 1] = f0.y * sc;
-            bv[2 * e] = f1.x * sc, bv[2 * e + 1] = f1.y * sc;
-          }
-          // sign bit set -> +1, clear -> -1 (block_fht.py:55-81)
-          const uint32_t m0 = s0[spad(p0 >> 5)] >> (p0 & 31), m1 = s1[spad(p0 >> 5)] >> (p0 & 31);
-          uint32_t o0[4], o1[4];
-#pragma unroll
-          for (int e = 0; e < 8; e += 2) {
-            float u[2], v[2];
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              const float x0 = ((m0 >> (e + hh)) & 1u) ? a[e + hh] : -a[e + hh];
-              const float x1 = ((m1 >> (e + hh)) & 1u) ? bv[e + hh] : -bv[e + hh];
-              u[hh] = x0 + x1;
-              v[hh] = x0 - x1;
-            }
-            o0[e >> 1] = pack_h2(u[0], u[1]);
-            o1[e >> 1] = pack_h2(v[0], v[1]);
-          }
+          uint32_t* o0 = &raw[0][4 * qq];
+          uint32_t* o1 = &raw[1][4 * qq];
+          hi2_chunk(o0, o1, ~(s0[spad(p0 >> 5)] >> (p0 & 31)), ~(s1[spad(p0 >> 5)] >> (p0 & 31)));
           *reinterpret_cast<uint4*>(z0 + lay_ab(p0)) = make_uint4(o0[0], o0[1], o0[2], o0[3]);
           *reinterpret_cast<uint4*>(z1 + lay_ab(p0)) = make_uint4(o1[0], o1[1], o1[2], o1[3]);
         }
@@ -832,33 +837,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                             &raw[j][4 * qq]);
           }
         }
+        if (st == 0) {  // the input words, scaled, into packed fp16
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+#pragma unroll
+            for (int r = 0; r < 16; ++r) {
+              const float2 fv = w2f<T>(raw[j][r]);
+              raw[j][r] = pack_h2(fv.x * in_scale, fv.y * in_scale);
+            }
+          }
+        }
 #pragma unroll
         for (int qq = 0; qq < 4; ++qq) {
           const int p0 = 8 * (tid + kThreads * (4 * h + qq));
-          float a[8], bv[8];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f0 = st == 0 ? w2f<T>(raw[0][4 * qq + e]) : w2f<__half>(raw[0][4 * qq + e]);
-            const float2 f1 = st == 0 ? w2f<T>(raw[1][4 * qq + e]) : w2f<__half>(raw[1][4 * qq + e]);
-            const float sc = st == 0 ? in_scale : 1.0f;
-            a[2 * e] = f0.x * sc, a[2 * e + 1] = f0.y * sc;
-            bv[2 * e] = f1.x * sc, bv[2 * e + 1] = f1.y * sc;
-          }
-          const uint32_t m0 = s0[spad(p0 >> 5)] >> (p0 & 31), m1 = s1[spad(p0 >> 5)] >> (p0 & 31);
-          uint32_t o0[4], o1[4];
-#pragma unroll
-          for (int e = 0; e < 8; e += 2) {
-            float u[2], v[2];
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              const float x0 = ((m0 >> (e + hh)) & 1u) ? a[e + hh] : -a[e + hh];
-              const float x1 = ((m1 >> (e + hh)) & 1u) ? bv[e + hh] : -bv[e + hh];
-              u[hh] = x0 + x1;
-              v[hh] = x0 - x1;
-            }
-            o0[e >> 1] = pack_h2(u[0], u[1]);
-            o1[e >> 1] = pack_h2(v[0], v[1]);
-          }
+          uint32_t* o0 = &raw[0][4 * qq];
+          uint32_t* o1 = &raw[1][4 * qq];
+          hi2_chunk(o0, o1, ~(s0[spad(p0 >> 5)] >> (p0 & 31)), ~(s1[spad(p0 >> 5)] >> (p0 & 31)));
           *reinterpret_cast<uint4*>(z0 + lay_ab(p0)) = make_uint4(o0[0], o0[1], o0[2], o0[3]);
           *reinterpret_cast<uint4*>(z1 + lay_ab(p0)) = make_uint4(o1[0], o1[1], o1[2], o1[3]);
         }

@@ -267,8 +267,11 @@ __device__ __forceinline__ void write_exchange(uint32_t (*d)[4], uint32_t base, 
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const uint32_t sel = h ? 0x7632u : 0x5410u;
-      int p = Pass<PASS>::dep(w, 0, g + 8 * (j & 1), 2 * t + h + 8 * (j >> 1));
-      uint32_t addr = base + 2u * (uint32_t)Pass<PASS>::lay_out(p);
+      // dep and lay_out are XOR-linear over disjoint bit fields: the thread's
+      // offset (formed once per run) XOR a compile-time constant per (j, h)
+      const int off = Pass<PASS>::lay_out(Pass<PASS>::dep(w, 0, g, 2 * t)) ^
+                      Pass<PASS>::lay_out(Pass<PASS>::dep(0, 0, 8 * (j & 1), h + 8 * (j >> 1)));
+      uint32_t addr = base + 2u * (uint32_t)off;
       uint32_t v0 = prmt(d[0][j], d[1][j], sel), v1 = prmt(d[2][j], d[3][j], sel);
       uint32_t v2 = prmt(d[4][j], d[5][j], sel), v3 = prmt(d[6][j], d[7][j], sel);
       asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};\n" ::"r"(addr), "r"(v0), "r"(v1), "r"(v2), "r"(v3));
@@ -279,8 +282,10 @@ __device__ __forceinline__ void write_exchange(uint32_t (*d)[4], uint32_t base, 
 template <int PASS>
 __device__ __forceinline__ void load_tile(uint32_t base, int w, int k, int lane, uint32_t* x) {
   int mm = lane >> 3, rr = lane & 7;
-  int p = Pass<PASS>::dep(w, k, 8 * (mm & 1), rr + 8 * (mm >> 1));
-  ldsm4(base + 2u * (uint32_t)Pass<PASS>::lay_in(p), x[0], x[1], x[2], x[3]);
+  // the thread's offset XOR a compile-time constant per sub-tile k (see write_exchange)
+  const int off = Pass<PASS>::lay_in(Pass<PASS>::dep(w, 0, 8 * (mm & 1), rr + 8 * (mm >> 1))) ^
+                  Pass<PASS>::lay_in(Pass<PASS>::dep(0, k, 0, 0));
+  ldsm4(base + 2u * (uint32_t)off, x[0], x[1], x[2], x[3]);
 }
 
 // One run of pass PASS: read the input buffer, row + col transforms (and for
@@ -394,8 +399,10 @@ __device__ __forceinline__ void run_final(const Frags& f, uint32_t in_base, uint
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const uint32_t sel = h ? 0x7632u : 0x5410u;
-      int p = dep_a(w, 0, g + 8 * (j & 1), 2 * t + h + 8 * (j >> 1));
-      uint32_t addr = stage_base + 16u * (uint32_t)lay_nat_chunk(p >> 3);
+      // XOR-linear as in write_exchange; positions 8-aligned after >> 3 on both parts
+      const int cidx = lay_nat_chunk(dep_a(w, 0, g, 2 * t) >> 3) ^
+                       lay_nat_chunk(dep_a(0, 0, 8 * (j & 1), h + 8 * (j >> 1)) >> 3);
+      uint32_t addr = stage_base + 16u * (uint32_t)cidx;
       uint32_t v0 = prmt(o[0][j], o[1][j], sel), v1 = prmt(o[2][j], o[3][j], sel);
       uint32_t v2 = prmt(o[4][j], o[5][j], sel), v3 = prmt(o[6][j], o[7][j], sel);
       asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};\n" ::"r"(addr), "r"(v0), "r"(v1), "r"(v2), "r"(v3));

@@ -174,10 +174,133 @@ __device__ void do_run(const TileParams& p, const TileCtx& c, const RunDesc& rd,
   }
 }
 
+// Single-run tiles (the run both reads the source and writes the sink) with
+// the group above the two lowest tile bits and at least two column bits --
+// the high-bit pass of large blocks: each thread takes 4 consecutive columns,
+// i.e. 4 consecutive positions per row, so a row is one 16-byte workspace
+// access (8 bytes for 16-bit types) and one sign word instead of four.  Four
+// times the bytes in flight of the scalar loop, which is latency-bound there.
+// Accesses that are unaligned or cross the slice/latent edge fall back to
+// scalars.
+template <typename T, int SRC, int DST, int GR>
+__device__ void do_run_v4(const TileParams& p, const TileCtx& c, const RunDesc& rd, const uint32_t* signs,
+                          int words_per_slot) {
+  const int glo = rd.glo;
+  const int ncols = 1 << (p.e - GR);
+  const int lowmask = (1 << glo) - 1;
+  const int kshift = glo - p.cb + p.tlo;
+  for (int col = 4 * threadIdx.x; col < ncols; col += 4 * blockDim.x) {
+    const int base = (col & lowmask) | ((col >> glo) << (glo + GR));
+    int64_t pos0, blk;
+    tile_coords(p, c, base, pos0, blk);
+    const int64_t bb = blk * p.B;
+    const int64_t wrow = (blk - p.first_block) * p.B;
+    const bool brow_ok = (blk - p.first_block) < p.nblocks;
+    float v[4][1 << GR];
+#pragma unroll
+    for (int k = 0; k < (1 << GR); ++k) {
+      const int64_t pos = pos0 + ((int64_t)k << kshift);
+      if (SRC == SRC_WS) {
+        const float* src = reinterpret_cast<const float*>(p.src) + wrow + pos;
+        if (brow_ok && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+          const float4 x = *reinterpret_cast<const float4*>(src);
+          v[0][k] = x.x, v[1][k] = x.y, v[2][k] = x.z, v[3][k] = x.w;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) v[i][k] = brow_ok ? src[i] : 0.0f;
+        }
+      } else {
+        // source elements idx .. idx+3, valid for idx+i in [0, hi) (slice: g in [start, stop))
+        const int64_t idx = SRC == SRC_LATENT ? pos : bb + pos - p.start;
+        const int64_t hi = SRC == SRC_LATENT ? p.L : p.stop - p.start;
+        const T* src = reinterpret_cast<const T*>(p.src) + idx;
+        if (idx >= 0 && idx + 4 <= hi && (reinterpret_cast<uintptr_t>(src) & (4 * sizeof(T) - 1)) == 0) {
+          if (sizeof(T) == 2) {
+            const uint2 x = *reinterpret_cast<const uint2*>(src);
+            const T* e = reinterpret_cast<const T*>(&x);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i][k] = Cvt<T>::to_f(e[i]);
+          } else {
+            const float4 x = *reinterpret_cast<const float4*>(src);
+            v[0][k] = Cvt<T>::to_f(reinterpret_cast<const T*>(&x)[0]);
+            v[1][k] = Cvt<T>::to_f(reinterpret_cast<const T*>(&x)[1]);
+            v[2][k] = Cvt<T>::to_f(reinterpret_cast<const T*>(&x)[2]);
+            v[3][k] = Cvt<T>::to_f(reinterpret_cast<const T*>(&x)[3]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) v[i][k] = (idx + i >= 0 && idx + i < hi) ? Cvt<T>::to_f(src[i]) : 0.0f;
+        }
+      }
+      if (p.pre_slot >= 0) {
+        const int t = base + (k << glo);
+        const uint32_t w = signs[p.pre_slot * words_per_slot + (t >> p.wshift)] >> (pos & 31);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i][k] = ((w >> i) & 1u) ? v[i][k] : -v[i][k];
+      }
+    }
+    for (int f = 0; f < rd.nfht; ++f) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) butterflies<GR>(v[i]);
+      const int s = rd.slot[f];
+      if (s >= 0) {
+        const float sc = p.scale;
+        const uint32_t* sws = signs + s * words_per_slot;
+#pragma unroll
+        for (int k = 0; k < (1 << GR); ++k) {
+          const int t = base + (k << glo);
+          const int64_t pos = pos0 + ((int64_t)k << kshift);
+          const uint32_t w = sws[t >> p.wshift] >> (pos & 31);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) v[i][k] *= ((w >> i) & 1u) ? sc : -sc;
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < (1 << GR); ++k) {
+      const int64_t pos = pos0 + ((int64_t)k << kshift);
+      if (DST == DST_SLICE) {
+        const int64_t idx = bb + pos - p.start, hi = p.stop - p.start;
+        T* dst = reinterpret_cast<T*>(p.dst) + idx;
+        if (idx >= 0 && idx + 4 <= hi && (reinterpret_cast<uintptr_t>(dst) & (4 * sizeof(T) - 1)) == 0) {
+          if (sizeof(T) == 2) {
+            uint2 x;
+            T* e = reinterpret_cast<T*>(&x);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) e[i] = Cvt<T>::from_f(v[i][k]);
+            *reinterpret_cast<uint2*>(dst) = x;
+          } else {
+            *reinterpret_cast<float4*>(dst) = make_float4(v[0][k], v[1][k], v[2][k], v[3][k]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (idx + i >= 0 && idx + i < hi) dst[i] = Cvt<T>::from_f(v[i][k]);
+        }
+      } else if (brow_ok) {
+        float* dst = reinterpret_cast<float*>(p.dst) + wrow + pos;
+        if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+          *reinterpret_cast<float4*>(dst) = make_float4(v[0][k], v[1][k], v[2][k], v[3][k]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = v[i][k];
+        }
+      }
+    }
+  }
+}
+
 template <typename T, int SRC, int DST>
 __device__ __forceinline__ void dispatch_run(const TileParams& p, const TileCtx& c, const RunDesc& rd,
                                              float* data, const uint32_t* signs, int wps, bool first,
                                              bool last) {
+  if (DST != DST_ACC && first && last && rd.glo >= 2 && p.cb >= 2 && p.wshift >= 2 && rd.gr >= 1 && rd.gr <= 3) {
+    switch (rd.gr) {
+      case 1: do_run_v4<T, SRC, DST, 1>(p, c, rd, signs, wps); return;
+      case 2: do_run_v4<T, SRC, DST, 2>(p, c, rd, signs, wps); return;
+      default: do_run_v4<T, SRC, DST, 3>(p, c, rd, signs, wps); return;
+    }
+  }
   switch (rd.gr) {
     case 0: do_run<T, SRC, DST, 0>(p, c, rd, data, signs, wps, first, last); break;
     case 1: do_run<T, SRC, DST, 1>(p, c, rd, data, signs, wps, first, last); break;

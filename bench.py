@@ -48,7 +48,12 @@ def _peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling while the timed region runs."""
+    """nvidia-smi clock / throttle sampling while the timed region runs.
+
+    The GPU is named by its UUID (the CUDA ordinal inside a container need not
+    match nvidia-smi's index).  A reader thread collects the lines; entering
+    waits (at most 5 s) for the first sample so that sampling covers the whole
+    timed region, which the caller starts after entering."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -58,28 +63,53 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.lines: list[str] = []
+        self.thread = None
+        self.error = None
+
+    def _gpu_id(self) -> str:
+        try:
+            import torch
+
+            uuid = str(torch.cuda.get_device_properties(self.gpu).uuid)
+            if uuid:
+                return uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        except Exception:  # older torch or no device: fall back to the ordinal
+            pass
+        return str(self.gpu)
+
+    def _reader(self):
+        for ln in self.proc.stdout:
+            if ln.strip():
+                self.lines.append(ln)
 
     def __enter__(self):
+        import threading
+
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            first = self.proc.stdout.readline()  # sampler is running before the timed region starts
-            if first.strip():
-                self.lines.append(first)
-        except OSError:
-            self.proc = None
+                ["nvidia-smi", f"--id={self._gpu_id()}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+            self.thread = threading.Thread(target=self._reader, daemon=True)
+            self.thread.start()
+            t0 = time.time()
+            while not self.lines and self.proc.poll() is None and time.time() - t0 < 5.0:
+                time.sleep(0.01)
+        except OSError as exc:
+            self.proc, self.error = None, str(exc)
         return self
 
     def __exit__(self, *exc):
         if self.proc is not None:
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                _, err = self.proc.communicate(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = self.lines[1:] + [ln for ln in out.splitlines() if ln.strip()]
+                _, err = self.proc.communicate()
+            if self.thread is not None:
+                self.thread.join(timeout=2)
+            if err and not self.lines:
+                self.error = err.strip().splitlines()[-1][:200]
 
     def summary(self) -> dict:
         sm, mx, reasons = [], 0.0, set()
@@ -96,13 +126,24 @@ class ClockSampler:
             for name, val in zip(names, parts[4:8]):
                 if val.lower() == "active":
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+               "reasons": sorted(reasons), "samples": len(sm)}
+        if not sm and self.error:
+            out["error"] = self.error
+        return out
 
 
 def _dist_env():
     return int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), \
         int(os.environ.get("LOCAL_RANK", "0"))
+
+
+def host_threads() -> int:
+    """Host cores this process may use (OMP_NUM_THREADS, which torchrun sets to 1, is ignored)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
 def cpu_sample(threads: int, seconds: float = 10.0, chunk_blocks: int = 64) -> dict:
@@ -127,6 +168,7 @@ def cpu_sample(threads: int, seconds: float = 10.0, chunk_blocks: int = 64) -> d
             break
     coords = done * size
     return {"value": coords / dt / 1e9, "unit": "Gcoords/s", "cores": threads, "kind": "port",
+            "elapsed_s": dt, "coords": coords,
             "sample": f"{done} x {chunk_blocks} blocks of {BLOCK} (fwd+bwd, fp32 math, layers={LAYERS}) "
                       f"of the bench workload in {dt:.1f}s"}
 
@@ -139,25 +181,30 @@ def _config(n: int) -> dict:
 
 
 def run_reference(args) -> None:
+    """The reference algorithm on the host cores (oracle/ C port, OpenMP over every
+    core this process may use).  The reference has no multi-GPU path, so under
+    torchrun rank 0 alone runs it, with all host cores, and its value does not
+    grow with N.  Each step is a timed, bounded sample of the workload."""
     _, rank, _ = _dist_env()
     if rank != 0:
         return
-    from oracle import oracle as orc
-
-    threads = orc.max_threads()
+    threads = host_threads()
     for _ in range(max(args.warmup, 0)):
-        cpu_sample(threads, seconds=0.5)
-    per_step = max(0.25, min(8.0, 150.0 / max(args.steps, 1)))  # whole run stays within a few minutes
-    vals = [cpu_sample(threads, seconds=per_step)["value"] for _ in range(args.steps)]
-    value = statistics.median(vals)
+        cpu_sample(threads, seconds=0.2)
+    per_step = max(0.2, min(4.0, 100.0 / max(args.steps, 1)))  # whole run stays within a couple of minutes
+    samples = [cpu_sample(threads, seconds=per_step) for _ in range(args.steps)]
+    value = statistics.median(x["value"] for x in samples)
+    ms_step = statistics.median(1e3 * x["elapsed_s"] for x in samples)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "Gcoords/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * COORDS_PER_GPU / (value * 1e9),
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": _config(args.gpus),
         "cpu_baseline": {"value": value, "unit": "Gcoords/s", "cores": threads, "kind": "port",
-                         "sample": f"per step: ~{per_step:.2f} s of fwd+bwd over 64-block chunks of the workload, fp32 math "
-                                   "(oracle/ C restatement of the reference algorithm, OpenMP)"},
+                         "sample": f"per step: {samples[0]['coords']} coordinates (~{per_step:.2f} s) of fwd+bwd over "
+                                   "64-block chunks of the workload, fp32 math (oracle/ C restatement of the "
+                                   "reference algorithm, OpenMP); one process on all host cores at every N, since "
+                                   "the reference has no multi-GPU path"},
         "e2e": {"value": value, "unit": "Gcoords/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -222,12 +269,14 @@ def run_ours(args) -> None:
         fwd()
         bwd()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     ev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # the clock sampler starts first; the barrier then lines all ranks up
+    # right before the timed region
     with ClockSampler(dev.index) as clk:
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         t0.record(stream)
         for a, b, c in ev:
             a.record(stream)
@@ -280,6 +329,8 @@ def run_ours(args) -> None:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e2e_ms = float(tt.item())
 
+    mlp = None if args.no_mlp else measure_mlp_pair(dev, world, max(args.steps, 10), args.warmup)
+
     if rank == 0:
         peaks = _peaks()
         fm, bm = statistics.median(f_ms), statistics.median(b_ms)
@@ -308,13 +359,179 @@ def run_ours(args) -> None:
             "clocks": clk.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:
-            from oracle import oracle as orc
-
-            line["cpu_baseline"] = cpu_sample(orc.max_threads())
+            line["cpu_baseline"] = cpu_sample(host_threads())
+            if mlp is not None:
+                mlp["cpu_baseline"] = cpu_mlp_sample(host_threads())
+        if mlp is not None:
+            line["mlp_pair"] = mlp
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+MLP_T, MLP_D, MLP_F = 8 * 1024, 768, 3072
+
+
+def measure_mlp_pair(dev, world: int, steps: int, warmup: int) -> dict:
+    """C3: GPT-2-small MLP pair y = W2 GELU(W1 x) (W1 [3072,768], W2 [768,3072],
+    each a BlockFHTLinear with its own seed, latent 32768, layers 3, bf16),
+    forward + backward to both latents and x, 8192 tokens per GPU.  Device
+    time of the step replayed as one CUDA graph, then end to end through the
+    public module API: x copied in from pinned host memory and the latent and
+    input gradients read back every step.  Under torchrun each rank runs its
+    own tokens and the latent gradients are all-reduced (data parallel)."""
+    import torch
+    import torch.distributed as dist
+
+    from latent_weight_lab import BlockFHTLinear
+
+    torch.manual_seed(0)
+    up = BlockFHTLinear(MLP_D, MLP_F, latent_dim=32768, layers=3, seed=11).to(dev, torch.bfloat16)
+    down = BlockFHTLinear(MLP_F, MLP_D, latent_dim=32768, layers=3, seed=12).to(dev, torch.bfloat16)
+    x = torch.randn(MLP_T, MLP_D, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    gy = torch.randn(MLP_T, MLP_D, device=dev, dtype=torch.bfloat16)
+    lat = [up.generator.latent, down.generator.latent]
+
+    def step():
+        up.generator.latent.grad = down.generator.latent.grad = x.grad = None
+        down(torch.nn.functional.gelu(up(x))).backward(gy)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    up.generator.latent.grad = down.generator.latent.grad = x.grad = None
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        down(torch.nn.functional.gelu(up(x))).backward(gy)
+    flat = torch.cat([p.grad.reshape(-1) for p in lat]) if world > 1 else None
+
+    def dev_step():
+        graph.replay()
+        if world > 1:
+            torch.cat([p.grad.reshape(-1) for p in lat], out=flat)
+            dist.all_reduce(flat)
+
+    def timed(fn, n):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / n
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    ms = timed(dev_step, steps)
+    x_host = x.detach().cpu().pin_memory()
+    out_host = [torch.empty(p.numel(), dtype=p.dtype).pin_memory() for p in lat] + \
+        [torch.empty(x.shape, dtype=x.dtype).pin_memory()]
+
+    def e2e_step():
+        with torch.no_grad():
+            x.copy_(x_host, non_blocking=True)
+        step()
+        if world > 1:
+            for p in lat:
+                dist.all_reduce(p.grad)
+        for h, d in zip(out_host, [p.grad.reshape(-1) for p in lat] + [x.grad]):
+            h.copy_(d, non_blocking=True)
+
+    ms_e2e = timed(e2e_step, max(3, steps // 2))
+    flops = 6.0 * 2 * MLP_D * MLP_F * MLP_T  # per GPU: fwd 2*in*out, bwd 4*in*out, two matrices
+    peaks = _peaks()
+    achieved = flops / (ms * 1e-3) / 1e12
+    return {
+        "metric": "fused BlockFHTLinear tokens/s (C3 MLP pair fwd+bwd)",
+        "value": world * MLP_T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "n_gpus": world,
+        "config": {"workload": "C3 MLP pair 768->3072->768, 8192 tokens/GPU, latents 32768 (block 32768), layers 3",
+                   "path": "weights generated by liblwl_b200 (one launch per matrix), GEMMs by cuBLAS, latent "
+                           "projection by liblwl_b200; the whole step replayed as one CUDA graph",
+                   "parallelism": f"data parallel x{world}" + (" (NCCL all-reduce of the latent gradients)"
+                                                                 if world > 1 else "")},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / peaks["bf16_tflops"], "traffic": None, "peak_source": peaks["source"],
+                     "flops_per_step": flops},
+        "e2e": {"value": world * MLP_T / (ms_e2e * 1e-3), "unit": "tokens/s", "ms_per_step": ms_e2e,
+                "h2d_bytes_per_step": MLP_T * MLP_D * 2,
+                "d2h_bytes_per_step": 2 * 32768 * 2 + MLP_T * MLP_D * 2,
+                "api": "BlockFHTLinear modules, eager (x in, latent and input gradients out)"},
+    }
+
+
+def cpu_mlp_sample(threads: int, tokens: int = 512) -> dict:
+    """The C3 step with the reference algorithm on host cores at reduced tokens:
+    both weights generated by the oracle port (fp32, OpenMP), the GEMMs and GELU
+    in numpy fp32, the latent projections by the oracle port.  tokens/s."""
+    import numpy as np
+
+    from oracle import oracle as orc
+
+    rng = np.random.default_rng(0)
+    z1 = (0.02 * rng.standard_normal(32768)).astype(np.float32)
+    z2 = (0.02 * rng.standard_normal(32768)).astype(np.float32)
+    x = rng.standard_normal((tokens, MLP_D)).astype(np.float32)
+    gy = rng.standard_normal((tokens, MLP_D)).astype(np.float32)
+    n = MLP_D * MLP_F
+
+    def gelu(v):
+        return 0.5 * v * (1.0 + np.tanh(0.7978845608 * (v + 0.044715 * v ** 3)))
+
+    def dgelu(v):
+        t = np.tanh(0.7978845608 * (v + 0.044715 * v ** 3))
+        return 0.5 * (1 + t) + 0.5 * v * (1 - t * t) * 0.7978845608 * (1 + 3 * 0.044715 * v * v)
+
+    def generate():
+        w1 = orc.fht_forward(z1, n, 3, 11, 0, n, threads=threads).reshape(MLP_F, MLP_D)
+        w2 = orc.fht_forward(z2, n, 3, 12, 0, n, threads=threads).reshape(MLP_D, MLP_F)
+        return w1, w2
+
+    def gemms(w1, w2):
+        h = x @ w1.T
+        a = gelu(h)
+        gh = (gy @ w2) * dgelu(h)
+        gw2 = gy.T @ a
+        gw1 = gh.T @ x
+        gx = gh @ w1
+        return gw1, gw2, gx
+
+    def project(gw1, gw2):
+        orc.fht_backward(np.ascontiguousarray(gw1).reshape(-1), 32768, n, 3, 11, 0, n, threads=threads)
+        orc.fht_backward(np.ascontiguousarray(gw2).reshape(-1), 32768, n, 3, 12, 0, n, threads=threads)
+
+    def timed(fn, *a):
+        fn(*a)
+        t0, k = time.perf_counter(), 0
+        while True:
+            out = fn(*a)
+            k += 1
+            if time.perf_counter() - t0 > 2.0:
+                return out, (time.perf_counter() - t0) / k
+
+    (w1, w2), t_gen = timed(generate)
+    (gw1, gw2, _), t_gemm = timed(gemms, w1, w2)
+    _, t_proj = timed(project, gw1, gw2)
+    # the generation and projection are per step; the GEMMs scale with tokens
+    dt = t_gen + t_proj + t_gemm * (MLP_T / tokens)
+    return {"value": MLP_T / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"C3 fwd+bwd timed in parts on host cores: weight generation {t_gen * 1e3:.0f} ms and latent "
+                      f"projection {t_proj * 1e3:.0f} ms per step (oracle/ C port, fp32), GEMMs + GELU in numpy fp32 "
+                      f"{t_gemm * 1e3:.0f} ms at {tokens} tokens, scaled to {MLP_T} tokens: {dt * 1e3:.0f} ms per step"}
+
 
 
 def run_mlp(args) -> None:
@@ -827,6 +1044,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-mlp", action="store_true", help="skip the C3 MLP-pair keys of the default line")
     ap.add_argument("--workload", choices=["fht", "mlp", "sweep", "gpt2", "gpt2xl", "linear", "mix"], default="fht")
     ap.add_argument("--latent-mode", choices=["ratio", "literal"], default="ratio")
     ap.add_argument("--min-log", type=int, default=5)

@@ -39,6 +39,11 @@ typedef enum lwl_dtype { LWL_F32 = 0, LWL_BF16 = 1, LWL_F16 = 2 } lwl_dtype;
 
 /* Flags for the transform entry points. */
 #define LWL_FLAG_EXACT 1u /* bf16/fp16: force fp32 arithmetic end to end (no tensor-core factors) */
+/* Testing only (lwl_fht_backward, tensor-core path): every CTA leaves its first
+ * gradient copy unissued and polls its bounded wait only 256 times, so the wait
+ * gives up with no copy in flight.  The result is NaN and
+ * lwl_fht_backward_status reports LWL_ERR_TIMEOUT; the context stays usable. */
+#define LWL_FLAG_TEST_WAIT_TIMEOUT 0x80000000u
 
 /* Library version (major*10000 + minor*100 + patch). */
 int lwl_version(void);
@@ -120,6 +125,16 @@ typedef struct lwl_fht_backward_desc {
 size_t lwl_fht_backward_grouped_workspace_bytes(int dtype, int count, const lwl_fht_backward_desc* descs,
                                                 unsigned flags);
 
+/* After a lwl_fht_backward call with these arguments and this workspace:
+ * synchronises `stream`, then returns LWL_ERR_TIMEOUT (with a message) if a
+ * bounded device-side wait of that call gave up, else LWL_OK.  Only the
+ * tensor-core backward (16-bit, padded block <= 2^15) waits on the device; it
+ * keeps the error word at the start of its workspace and poisons the gradient
+ * with NaN on a time-out.  Other paths always report LWL_OK.  No reference
+ * counterpart (the reference's kernels do not wait on the device). */
+int lwl_fht_backward_status(int dtype, int64_t latent_size, int64_t size, int layers, int64_t start,
+                            int64_t stop, unsigned flags, const void* workspace, void* stream);
+
 /* count lwl_fht_backward calls as one kernel + one reduce launch per 96
  * generators (16-bit dtypes, padded block size <= 2^15; other generators run
  * one by one inside the call): each CTA takes a contiguous range of all
@@ -147,6 +162,12 @@ size_t lwl_linear_forward_workspace_bytes(void);
 int lwl_linear_forward(int dtype, const void* x, int64_t tokens, int64_t in_features, const void* latent,
                        int64_t latent_size, int64_t out_features, int layers, uint64_t seed, float weight_scale,
                        void* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/* After a lwl_linear_forward / lwl_linear_forward_ex / lwl_tc_linear_dense
+ * call with this workspace: synchronises `stream` and returns
+ * LWL_ERR_TIMEOUT if a bounded pipeline wait of that call gave up, else
+ * LWL_OK.  No reference counterpart. */
+int lwl_linear_forward_status(const void* workspace, void* stream);
 
 /* Workspace for lwl_linear_backward: the generated W, grad_W (both [out, in]
  * in dtype), the transform workspace and 4 MiB for cuBLAS. */
@@ -204,8 +225,11 @@ int lwl_tc_linear_dense(const void* x, int64_t tokens, int64_t in_features, cons
 int lwl_fht_launch_count(int dtype, int64_t latent_size, int64_t size, int layers, int64_t start,
                          int64_t stop, int backward, unsigned flags);
 
-/* Same result as lwl_fht_backward, for callers that cannot allocate device
- * memory (no workspace argument).  No counterpart in the reference.
+/* The latent gradient of lwl_fht_backward, for callers that cannot allocate
+ * device memory (no workspace argument).  No counterpart in the reference.
+ * It always runs the fp32 tile engine, so fp32 results match
+ * lwl_fht_backward's and bf16 / fp16 results match them up to rounding
+ * (lwl_fht_backward may take the tensor-core path there).
  * Intended for code that has no device allocator at hand, e.g. a plugin
  * called from a host runtime that owns all device memory, or a callback whose
  * memory policy forbids allocating.  The per-CTA partial gradients live in a
@@ -216,7 +240,10 @@ int lwl_fht_launch_count(int dtype, int64_t latent_size, int64_t size, int layer
  *    (cudaGetSymbolAddress with that device current); make that first call
  *    before any stream capture;
  *  - all calls on a device share the array; calls that overlap on the GPU
- *    race on it and give wrong results: order them on one stream. */
+ *    race on it and give wrong results: order them on one stream;
+ *  - the looked-up address is kept for the life of the process, so it does
+ *    not survive cudaDeviceReset (or another teardown of the device's primary
+ *    context): do not call this entry point on a device after resetting it. */
 int lwl_fht_backward_noalloc(int dtype, const void* grad_out, int64_t latent_size, int64_t size,
                              int layers, uint64_t seed, int64_t start, int64_t stop, void* grad_latent,
                              unsigned flags, void* stream);

@@ -30,6 +30,8 @@ void set_error(const char* fmt, ...) {
   va_end(ap);
 }
 
+void clear_error() { g_err[0] = 0; }
+
 __global__ void sign_words_kernel(uint32_t key, int64_t first_word, int64_t count, uint32_t* out) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x)
     out[i] = sign_word(key, first_word + i);
@@ -107,7 +109,8 @@ static int fht_call(bool backward, int dtype, const void* in, void* out, int64_t
       set_error("workspace of %zu bytes required, %zu given", need, ws ? ws_bytes : (size_t)0);
       return LWL_ERR_WORKSPACE;
     }
-    if (mma_backward(dtype, in, L, layers, seed, start, stop, out, ws, reinterpret_cast<cudaStream_t>(stream)) != 0) {
+    if (mma_backward(dtype, in, L, layers, seed, start, stop, out, ws, reinterpret_cast<cudaStream_t>(stream),
+                     (flags & LWL_FLAG_TEST_WAIT_TIMEOUT) ? 1 : 0) != 0) {
       set_error("tensor-core backward launch failed: %s", cudaGetErrorString(cudaGetLastError()));
       return LWL_ERR_CUDA;
     }
@@ -272,6 +275,47 @@ int lwl_fht_backward(int dtype, const void* grad_out, int64_t latent_size, int64
                      size_t workspace_bytes, unsigned flags, void* stream) {
   return lwl::fht_call(true, dtype, grad_out, grad_latent, latent_size, size, layers, seed, start, stop,
                        workspace, workspace_bytes, flags, stream);
+}
+
+// Reads a device error word written by a call's bounded waits (synchronises
+// the stream first, so the call that wrote it has finished).
+static int read_error_word(const void* word, void* stream, const char* what) {
+  lwl::clear_error();
+  int host = 0;
+  LWL_CUDA_TRY(cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)));
+  LWL_CUDA_TRY(cudaMemcpy(&host, word, sizeof(int), cudaMemcpyDeviceToHost));
+  if (host != 0) {
+    lwl::set_error("%s: a bounded device-side wait gave up (error word %d); the result was poisoned with NaN", what,
+                   host);
+    return LWL_ERR_TIMEOUT;
+  }
+  return LWL_OK;
+}
+
+int lwl_fht_backward_status(int dtype, int64_t latent_size, int64_t size, int layers, int64_t start, int64_t stop,
+                            unsigned flags, const void* workspace, void* stream) {
+  lwl::clear_error();
+  int st = lwl::validate_fht(dtype, latent_size, size, layers, start, stop);
+  if (st) return st;
+  // only the tensor-core backward waits on the device; it keeps its error word
+  // at the start of a non-empty workspace
+  if (!lwl::mma_backward_supported(dtype, latent_size, flags) ||
+      lwl::mma_backward_workspace_bytes(latent_size, start, stop) == 0)
+    return LWL_OK;
+  if (!workspace) {
+    lwl::set_error("null workspace");
+    return LWL_ERR_INVALID;
+  }
+  return read_error_word(workspace, stream, "lwl_fht_backward");
+}
+
+int lwl_linear_forward_status(const void* workspace, void* stream) {
+  if (!workspace) {
+    lwl::clear_error();
+    lwl::set_error("null workspace");
+    return LWL_ERR_INVALID;
+  }
+  return read_error_word(workspace, stream, "lwl_linear_forward");
 }
 
 int lwl_fht_forward_grouped(int dtype, int count, const lwl_fht_forward_desc* descs, unsigned flags,

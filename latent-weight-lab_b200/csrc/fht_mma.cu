@@ -17,10 +17,10 @@
 // lay_ab / lay_ba make both sides bank-conflict free.
 //
 // Arithmetic: fp16 operands and intermediates with orthonormal factors
-// (H16/4, H8/2).  The latent is pre-scaled by a power of two so its L2 norm
-// sits in [2^11, 2^12) -- every intermediate element is bounded by the
-// block's norm, so nothing overflows, and typical elements stay far from
-// subnormals.  The last column transform accumulates in fp32, is rescaled
+// (H16/4, H8/2).  The input is pre-scaled by a power of two, taken from its
+// largest magnitude, so that the block's L2 norm is below 2^12 -- every
+// intermediate element is bounded by the block's norm, so nothing overflows,
+// and typical elements stay far from subnormals (prescale_exponent).  The last column transform accumulates in fp32, is rescaled
 // and rounded once to the output dtype.  Signs are XORed into packed pairs:
 // positions p and p+16 share a register, so one shift + LOP3 flips both.
 #include <cmath>
@@ -78,25 +78,20 @@ __global__ void __launch_bounds__(kThreads, 1) fht15_forward_kernel(const __grid
     if (layers == 2) __syncthreads();
     if (di != cur) {
       make_frags(f, g, t, n);
-      // power-of-two prescale: tile L2 norm into [2^11, 2^12)
-      float ss = 0.0f;
+      // power-of-two prescale from the largest magnitude (block norm below 2^12)
+      float mx = 0.0f;
       for (int64_t i = tid; i < L; i += kThreads) {
         float v = Cvt<T>::to_f(latent[i]);
-        ss += v * v;
+        mx = fmaxf(mx, fabsf(v));
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      if (lane == 0) red[w] = ss;
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (lane == 0) red[w] = mx;
       __syncthreads();
       if (tid == 0) {
         float s = 0.0f;
-        for (int i = 0; i < kThreads / 32; ++i) s += red[i];
-        s *= (float)(kB >> n);  // the tile holds 2^(15-n) copies of the latent
-        int e = 0;
-        if (s > 0.0f) {
-          frexpf(sqrtf(s), &e);  // norm = m * 2^e with m in [0.5, 1)
-          e -= 12;
-        }
+        for (int i = 0; i < kThreads / 32; ++i) s = fmaxf(s, red[i]);
+        int e = prescale_exponent(s, n);
         k0_shared = e;
       }
       __syncthreads();
@@ -259,24 +254,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t xb = (uint32_t)__cvta_generic_to_shared(xs);
   Frags f;
   make_frags(f, g, t, kLog);
-  // power-of-two prescale: the block norm (the padded latent) into [2^11, 2^12)
-  float ss = 0.0f;
+  // power-of-two prescale from the largest magnitude (block norm below 2^12)
+  float mx = 0.0f;
   for (int64_t i = tid; i < L; i += kThreads) {
     const float v = Cvt<T>::to_f(latent[i]);
-    ss += v * v;
+    mx = fmaxf(mx, fabsf(v));
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if (lane == 0) red[w] = ss;
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) red[w] = mx;
   __syncthreads();
   if (tid == 0) {
     float s2 = 0.0f;
-    for (int i = 0; i < kThreads / 32; ++i) s2 += red[i];
-    int e = 0;
-    if (s2 > 0.0f) {
-      frexpf(sqrtf(s2), &e);
-      e -= 12;
-    }
+    for (int i = 0; i < kThreads / 32; ++i) s2 = fmaxf(s2, red[i]);
+    int e = prescale_exponent(s2, 16);
     k0_shared = e;
   }
   __syncthreads();
@@ -446,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fht15_backward_kernel(const T* __restrict__ grad, int64_t L, int layers, int n, uint32_t seed32, float corr,
                           int64_t first_block,
                           int64_t nblocks, int64_t start, int64_t stop, float* __restrict__ partial,
-                          int* __restrict__ err) {
+                          int* __restrict__ err, int test_stall) {
   extern __shared__ __align__(128) unsigned char smem[];
   uint16_t* xbuf = reinterpret_cast<uint16_t*>(smem);
   uint16_t* ybuf = xbuf + kB;
@@ -507,7 +498,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
   uint32_t phase = 0;
-  if (tid == 0 && blockIdx.x < nblocks && bulk_ok(first_block + blockIdx.x)) issue(first_block + blockIdx.x);
+  // Bounded waits: (1 << 22) polls normally.  test_stall (LWL_FLAG_TEST_WAIT_TIMEOUT)
+  // leaves the first copy unissued and polls 256 times, so the first wait gives
+  // up with no copy in flight and the call reports LWL_ERR_TIMEOUT.
+  const int polls = test_stall ? 256 : (1 << 22);
+  bool inflight = false;  // thread 0: a bulk copy was issued and has not been waited for
+  if (tid == 0 && !test_stall && blockIdx.x < nblocks && bulk_ok(first_block + blockIdx.x)) {
+    issue(first_block + blockIdx.x);
+    inflight = true;
+  }
 
   for (int64_t bi = blockIdx.x; bi < nblocks; bi += gridDim.x) {
     const int64_t blk = first_block + bi;
@@ -519,14 +518,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       sw[l * kWordsPad + spad(wd)] =
           sign_word(block_layer_key(seed32, (blk << (kLog - n)) + (p >> n), l), (p & Bm) >> 5);
     }
-    // gradient chunks of this block into registers, with their squared norm
+    // gradient chunks of this block into registers, with their largest magnitude
     uint4 raw[8];
-    float ss = 0.0f;
+    float mx = 0.0f;
     const bool bulk = bulk_ok(blk);
     if (bulk) {
       // bounded wait for the bulk copy; on time-out record the failure and stop
       uint32_t done = 0;
-      for (int it = 0; it < (1 << 22) && !done; ++it) {
+      for (int it = 0; it < polls && !done; ++it) {
         asm volatile(
             "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
             : "=r"(done)
@@ -536,6 +535,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!done) {
         abort_flag = 1;
         atomicExch(err, 1);
+      } else {
+        inflight = false;
       }
       phase ^= 1u;
     }
@@ -558,12 +559,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         float v = Cvt<T>::to_f(ev[e]);
-        ss += v * v;
+        mx = fmaxf(mx, fabsf(v));
       }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) red[w] = ss;
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[w] = mx;
     __syncthreads();
     if (abort_flag) break;  // uniform: set before the barrier above
     // the stage buffer is free again: fetch the next block while this one runs
@@ -572,6 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (nb < nblocks && bulk_ok(first_block + nb)) {
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
         issue(first_block + nb);
+        inflight = true;
       }
     }
     // every thread forms the prescale exponent from the warp sums (same
@@ -579,11 +581,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int k0 = 0;
     {
       float s = 0.0f;
-      for (int i = 0; i < kThreads / 32; ++i) s += red[i];
-      if (s > 0.0f) {
-        frexpf(sqrtf(s), &k0);
-        k0 -= 12;
-      }
+      for (int i = 0; i < kThreads / 32; ++i) s = fmaxf(s, red[i]);
+      k0 = prescale_exponent(s, n);
     }
     const float in_scale = ldexpf(1.0f, -k0);
 #pragma unroll
@@ -623,7 +622,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       run_final_acc(f, xb, sw, scale, tbase, w, lane, g, t);
     }
   }
-  if (abort_flag && tid == 0) {
+  if (abort_flag && tid == 0 && inflight) {
     // let an outstanding copy land before the CTA exits (bounded)
     uint32_t done = 0;
     for (int it = 0; it < (1 << 22) && !done; ++it) {
@@ -687,7 +686,8 @@ constexpr size_t kBwdHeader = 256;  // workspace: [error word | pad] then the pa
 template <typename T>
 int launch_backward_t(const void* grad, int64_t L, int layers, int n, uint32_t seed32, int64_t first_block,
                       int64_t nblocks,
-                      int64_t start, int64_t stop, void* grad_latent, void* workspace, cudaStream_t st) {
+                      int64_t start, int64_t stop, void* grad_latent, void* workspace, cudaStream_t st,
+                      int test_stall) {
   int* err = reinterpret_cast<int*>(workspace);
   float* partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kBwdHeader);
   if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess) return -1;
@@ -697,7 +697,8 @@ int launch_backward_t(const void* grad, int64_t L, int layers, int n, uint32_t s
   const float corr = (float)std::pow(layer_correction(n), layers);
   fht15_backward_kernel<T><<<grid, kThreads, kSmemBwd, st>>>(reinterpret_cast<const T*>(grad), L, layers, n, seed32,
                                                              corr,
-                                                             first_block, nblocks, start, stop, partial, err);
+                                                             first_block, nblocks, start, stop, partial, err,
+                                                             test_stall);
   if (cudaGetLastError() != cudaSuccess) return -1;
   int rb = (int)((L + 255) / 256);
   fht15_reduce_kernel<T><<<rb, 256, 0, st>>>(partial, grid, L, err, reinterpret_cast<T*>(grad_latent));
@@ -763,8 +764,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // with zeros outside the slice.
     const bool blk_full = vec_ok && bbase >= start && bbase + 2 * kB <= stop;
     const uint16_t* g16 = reinterpret_cast<const uint16_t*>(grad);
-    // squared norm of the block's gradient (read again from L2 by the first hi pass)
-    float ss = 0.0f;
+    // largest magnitude of the block's gradient (read again from L2 by the first hi pass)
+    float mx = 0.0f;
 #pragma unroll 1
     for (int h = 0; h < 2; ++h) {
       uint32_t r[8][4];
@@ -784,22 +785,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 fv = w2f<T>(r[u][e]);
-          ss += fv.x * fv.x + fv.y * fv.y;
+          mx = fmaxf(mx, fmaxf(fabsf(fv.x), fabsf(fv.y)));
         }
       }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) red[w] = ss;
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[w] = mx;
     __syncthreads();
     int k0 = 0;
     {
       float s2 = 0.0f;
-      for (int i = 0; i < kThreads / 32; ++i) s2 += red[i];
-      if (s2 > 0.0f) {
-        frexpf(sqrtf(s2), &k0);
-        k0 -= 12;
-      }
+      for (int i = 0; i < kThreads / 32; ++i) s2 = fmaxf(s2, red[i]);
+      k0 = prescale_exponent(s2, 16);
     }
     const float in_scale = ldexpf(1.0f, -k0), scale = ldexpf(1.0f, k0) * scale_base;
     for (int st = 0; st < layers; ++st) {
@@ -1066,7 +1064,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           sign_word(block_layer_key(D.seed32, (blk << (kLog - n)) + (p >> n), l), (p & Bm) >> 5);
     }
     uint4 raw[8];
-    float ss = 0.0f;
+    float mx = 0.0f;
     const bool bulk = bulk_ok(D, blk);
     if (bulk) {
       uint32_t done = 0;
@@ -1102,12 +1100,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         float v = Cvt<T>::to_f(ev[e]);
-        ss += v * v;
+        mx = fmaxf(mx, fabsf(v));
       }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) red[w] = ss;
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[w] = mx;
     __syncthreads();
     if (abort_flag) break;  // uniform: set before the barrier above
     if (tid == 0) {
@@ -1125,11 +1123,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int k0 = 0;
     {
       float s2 = 0.0f;
-      for (int q = 0; q < kThreads / 32; ++q) s2 += red[q];
-      if (s2 > 0.0f) {
-        frexpf(sqrtf(s2), &k0);
-        k0 -= 12;
-      }
+      for (int q = 0; q < kThreads / 32; ++q) s2 = fmaxf(s2, red[q]);
+      k0 = prescale_exponent(s2, n);
     }
     const float in_scale = ldexpf(1.0f, -k0);
 #pragma unroll
@@ -1363,26 +1358,22 @@ __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_consta
       int sl = i / kWords, wd = i - sl * kWords;
       sw[sl * kWordsPad + spad(wd)] = sign_word(block_layer_key(p.seed32, b, p.slot_layer[sl]), j * kWords + wd);
     }
-    // tile norm (first read), then scaled fp16 landing in the first run's layout (second read, from L2)
-    float ss = 0.0f;
+    // tile's largest magnitude (first read), then scaled fp16 landing in the first run's layout (second read, from L2)
+    float mx = 0.0f;
     for (int c = tid; c < kB / 8; c += kThreads) {
       float v[8];
       lo_load8<T>(p, b, tbase + 8 * c, v);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+      for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(v[e]));
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) red[w] = ss;
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[w] = mx;
     __syncthreads();
     if (tid == 0) {
       float s = 0.0f;
-      for (int i = 0; i < kThreads / 32; ++i) s += red[i];
-      int e = 0;
-      if (s > 0.0f) {
-        frexpf(sqrtf(s), &e);
-        e -= 12;
-      }
+      for (int i = 0; i < kThreads / 32; ++i) s = fmaxf(s, red[i]);
+      int e = prescale_exponent(s, kLog);
       k0_shared = e;
     }
     __syncthreads();
@@ -1585,7 +1576,7 @@ size_t mma_backward_workspace_bytes(int64_t latent_size, int64_t start, int64_t 
 }
 
 int mma_backward(int dtype, const void* grad, int64_t L, int layers, uint64_t seed, int64_t start, int64_t stop,
-                 void* grad_latent, void* workspace, cudaStream_t st) {
+                 void* grad_latent, void* workspace, cudaStream_t st, int test_stall) {
   const int64_t B = fmma::kB;
   int64_t first = start / B, last = (stop + B - 1) / B;
   if (last <= first) {
@@ -1594,9 +1585,9 @@ int mma_backward(int dtype, const void* grad, int64_t L, int layers, uint64_t se
   uint32_t s32 = fold_seed(seed);
   if (dtype == LWL_BF16)
     return fmma::launch_backward_t<__nv_bfloat16>(grad, L, layers, ilog2(next_pow2(L)), s32, first, last - first, start, stop, grad_latent,
-                                                  workspace, st);
+                                                  workspace, st, test_stall);
   return fmma::launch_backward_t<__half>(grad, L, layers, ilog2(next_pow2(L)), s32, first, last - first, start, stop, grad_latent,
-                                         workspace, st);
+                                         workspace, st, test_stall);
 }
 
 size_t mma_backward_grouped_workspace_bytes(int count, const lwl_fht_backward_desc* descs) {

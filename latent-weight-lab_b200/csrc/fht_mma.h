@@ -29,8 +29,9 @@ int mma16_backward(int dtype, const void* grad, int64_t L, int layers, uint64_t 
                    void* grad_latent, void* workspace, cudaStream_t st);
 bool mma_backward_supported(int dtype, int64_t latent_size, unsigned flags);
 size_t mma_backward_workspace_bytes(int64_t latent_size, int64_t start, int64_t stop);
+// test_stall != 0: the first bounded wait of every CTA gives up (LWL_FLAG_TEST_WAIT_TIMEOUT).
 int mma_backward(int dtype, const void* grad, int64_t latent_size, int layers, uint64_t seed, int64_t start,
-                 int64_t stop, void* grad_latent, void* workspace, cudaStream_t st);
+                 int64_t stop, void* grad_latent, void* workspace, cudaStream_t st, int test_stall = 0);
 
 // Low-15-bit pass of large blocks (B = 2^16 .. 2^23, 16-bit dtypes) on the
 // tensor-core tile kernel: one 2^15 tile per work item, input/output and signs

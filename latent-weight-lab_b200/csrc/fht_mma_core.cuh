@@ -111,6 +111,24 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 }
 __device__ __forceinline__ int hsign(int i, int j) { return (__popc(i & j) & 1) ? -1 : 1; }
 
+// Power-of-two prescale exponent k0 for an fp16 transform of 2^nbits-element
+// blocks whose largest magnitude is `maxabs`.  After scaling by 2^-k0 the
+// largest element is below 2^(12 - ceil(nbits/2)), so a block's L2 norm --
+// which bounds every element of every orthonormal partial transform of it --
+// stays below 2^12, far inside fp16.  Taken from the maximum rather than a
+// sum of squares, the exponent is exact for every finite input: a float sum
+// of squares overflows above |v| ~ 1.8e19 and flushes to zero below
+// ~1e-19, both of which are legal bf16 values.  k0 is clamped to +-120 so
+// that 2^-k0 and 2^k0 stay normal floats; blocks beyond that (all elements
+// below 2^-108 or an infinity) keep the nearest representable scale.
+__device__ __forceinline__ int prescale_exponent(float maxabs, int nbits) {
+  if (!(maxabs > 0.0f) || isinf(maxabs)) return 0;
+  int e = 0;
+  frexpf(maxabs, &e);  // maxabs < 2^e
+  const int k0 = e - (12 - ((nbits + 1) >> 1));
+  return k0 < -120 ? -120 : (k0 > 120 ? 120 : k0);
+}
+
 template <typename T> __device__ __forceinline__ uint32_t pack_out(float lo, float hi);
 template <> __device__ __forceinline__ uint32_t pack_out<__nv_bfloat16>(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);

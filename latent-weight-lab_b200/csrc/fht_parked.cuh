@@ -171,24 +171,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tbase = parked_alloc(&tmem_slot, NT * 128, w);
   const uint32_t tt0 = tbase + ((uint32_t)(32 * (w & 3)) << 16) + (uint32_t)(NT * 32 * (w >> 2));
 
-  // power-of-two prescale: the block norm (the padded latent) into [2^11, 2^12)
-  float ss = 0.0f;
+  // power-of-two prescale from the largest magnitude (block norm below 2^12)
+  float mx = 0.0f;
   for (int64_t i = tid; i < L; i += kThreads) {
     const float v = Cvt<T>::to_f(latent[i]);
-    ss += v * v;
+    mx = fmaxf(mx, fabsf(v));
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if (lane == 0) red[w] = ss;
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) red[w] = mx;
   __syncthreads();
   if (tid == 0) {
     float s2 = 0.0f;
-    for (int i = 0; i < kThreads / 32; ++i) s2 += red[i];
-    int e = 0;
-    if (s2 > 0.0f) {
-      frexpf(sqrtf(s2), &e);
-      e -= 12;
-    }
+    for (int i = 0; i < kThreads / 32; ++i) s2 = fmaxf(s2, red[i]);
+    int e = prescale_exponent(s2, kLog + (NT == 4 ? 2 : 1));
     k0_shared = e;
   }
   __syncthreads();
@@ -336,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the whole block lies inside [start, stop) and the gradient is aligned,
     // else element by element with zeros outside the slice
     const bool blk_full = vec_ok && bbase >= start && bbase + NT * kB <= stop;
-    float ss = 0.0f;
+    float mx = 0.0f;
 #pragma unroll 1
     for (int h = 0; h < NT; ++h) {
       uint32_t r[8][4];
@@ -357,22 +353,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 fv = w2f<T>(r[u][e]);
-          ss += fv.x * fv.x + fv.y * fv.y;
+          mx = fmaxf(mx, fmaxf(fabsf(fv.x), fabsf(fv.y)));
         }
       }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) red[w] = ss;
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[w] = mx;
     __syncthreads();
     int k0 = 0;
     {
       float s2 = 0.0f;
-      for (int i = 0; i < kThreads / 32; ++i) s2 += red[i];
-      if (s2 > 0.0f) {
-        frexpf(sqrtf(s2), &k0);
-        k0 -= 12;
-      }
+      for (int i = 0; i < kThreads / 32; ++i) s2 = fmaxf(s2, red[i]);
+      k0 = prescale_exponent(s2, kLog + (NT == 4 ? 2 : 1));
     }
     const float in_scale = ldexpf(1.0f, -k0), scale = ldexpf(1.0f, k0) * scale_base;
 

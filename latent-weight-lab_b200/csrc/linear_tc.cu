@@ -152,24 +152,19 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   int k0 = 0;
   if (GEN) {
     const __nv_bfloat16* latent = reinterpret_cast<const __nv_bfloat16*>(P.latent);
-    float ss = 0.0f;
+    float mx = 0.0f;
     for (int64_t i = tid; i < P.L; i += kLinThreads) {
       float v = __bfloat162float(latent[i]);
-      ss += v * v;
+      mx = fmaxf(mx, fabsf(v));
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) red[w] = ss;
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[w] = mx;
     __syncthreads();
     if (tid == 0) {
       float s = 0.0f;
-      for (int i = 0; i < kLinThreads / 32; ++i) s += red[i];
-      s *= (float)(kB >> n);
-      int e = 0;
-      if (s > 0.0f) {
-        frexpf(sqrtf(s), &e);
-        e -= 12;
-      }
+      for (int i = 0; i < kLinThreads / 32; ++i) s = fmaxf(s, red[i]);
+      int e = prescale_exponent(s, n);
       k0_sh = e;
     }
     __syncthreads();

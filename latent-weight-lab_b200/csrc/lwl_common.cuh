@@ -72,6 +72,8 @@ inline size_t dtype_bytes(int dtype) { return dtype == LWL_F32 ? 4 : 2; }
 
 // Thread-local error text for lwl_last_error().
 void set_error(const char* fmt, ...);
+// Empties the calling thread's error text (every entry point starts with it).
+void clear_error();
 
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device):
 // the attribute belongs to the device, so a process that drives several GPUs

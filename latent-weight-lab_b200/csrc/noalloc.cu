@@ -18,7 +18,14 @@
 //    clearing, but calls whose executions overlap on the GPU (different
 //    streams without ordering) race on it and give wrong results;
 //  * the device address of the array is looked up once per device on that
-//    device's first call (cudaGetSymbolAddress, with that device current).
+//    device's first call (cudaGetSymbolAddress, with that device current) and
+//    kept for the life of the process, so it is not valid across a
+//    cudaDeviceReset (or any other teardown of the device's primary context):
+//    a process that resets a device must not call this entry point on it
+//    again;
+//  * the partials are summed by the fp32 tile engine for every dtype, so for
+//    bf16 / fp16 the result equals lwl_fht_backward's up to rounding (that
+//    entry point may take the tensor-core path, which rounds differently).
 #include <mutex>
 
 #include "fht_engine.h"
@@ -65,6 +72,7 @@ extern "C" int lwl_fht_backward_noalloc(int dtype, const void* grad_out, int64_t
                                         int layers, uint64_t seed, int64_t start, int64_t stop, void* grad_latent,
                                         unsigned flags, void* stream) {
   using namespace lwl;
+  clear_error();
   // bad arguments are rejected before any device work
   if (dtype != LWL_F32 && dtype != LWL_BF16 && dtype != LWL_F16) {
     set_error("unsupported dtype code %d (expected 0=fp32, 1=bf16, 2=fp16)", dtype);

@@ -22,6 +22,7 @@ _LOAD_ERROR: Exception | None = None
 
 LWL_F32, LWL_BF16, LWL_F16 = 0, 1, 2
 FLAG_EXACT = 1
+FLAG_TEST_WAIT_TIMEOUT = 0x80000000  # testing only: the tensor-core backward's first bounded wait gives up
 _DTYPE_CODE = {torch.float32: LWL_F32, torch.bfloat16: LWL_BF16, torch.float16: LWL_F16}
 
 
@@ -76,6 +77,10 @@ def _declare(lib: ctypes.CDLL) -> None:
         fn = getattr(lib, name)
         fn.restype = ci
         fn.argtypes = [ci, vp, i64, i64, ci, u64, i64, i64, vp, vp, sz, cu, vp]
+    lib.lwl_fht_backward_status.restype = ci
+    lib.lwl_fht_backward_status.argtypes = [ci, i64, i64, ci, i64, i64, cu, vp, vp]
+    lib.lwl_linear_forward_status.restype = ci
+    lib.lwl_linear_forward_status.argtypes = [vp, vp]
 
 
 class ForwardDesc(ctypes.Structure):

@@ -31,25 +31,28 @@ def _latent(L, seed, dtype, scale=1.0):
     return z.to(dtype)
 
 
-def _check_forward(nat, L, size, layers, seed, start, stop, dtype, flags=0):
-    z = _latent(L, 1000 + L + layers, dtype)
+def _check_forward(nat, L, size, layers, seed, start, stop, dtype, flags=0, scale=1.0, tol=None):
+    z = _latent(L, 1000 + L + layers, dtype, scale)
     y = nat.fht_forward(z.cuda(), size, layers, seed, start, stop, flags=flags)
     torch.cuda.synchronize()
     ref = orc.fht_forward(z.float().numpy(), size, layers, seed, start, stop)
     assert y.dtype == dtype and y.shape == (stop - start,)
     if stop > start:
         err = rel_l2(y.float().cpu().numpy(), ref)
-        assert err < TOL[dtype], f"forward rel-L2 {err:.3e} (L={L} size={size} layers={layers} {dtype})"
+        assert err < (tol or TOL[dtype]), f"forward rel-L2 {err:.3e} (L={L} size={size} layers={layers} {dtype})"
+        return err
+    return 0.0
 
 
-def _check_backward(nat, L, size, layers, seed, start, stop, dtype, flags=0):
-    g = _latent(stop - start, 77 + L, dtype)
+def _check_backward(nat, L, size, layers, seed, start, stop, dtype, flags=0, scale=1.0, tol=None):
+    g = _latent(stop - start, 77 + L, dtype, scale)
     grad = nat.fht_backward(g.cuda(), L, size, layers, seed, start, stop, flags=flags)
     torch.cuda.synchronize()
     ref = orc.fht_backward(g.float().numpy(), L, size, layers, seed, start, stop)
     assert grad.dtype == dtype and grad.shape == (L,)
     err = rel_l2(grad.float().cpu().numpy(), ref)
-    assert err < TOL[dtype], f"backward rel-L2 {err:.3e} (L={L} size={size} layers={layers} {dtype})"
+    assert err < (tol or TOL[dtype]), f"backward rel-L2 {err:.3e} (L={L} size={size} layers={layers} {dtype})"
+    return err
 
 
 CASES = [
@@ -203,6 +206,91 @@ def test_large_block_sizes_bf16(nat, logb, layers):
     size = 2 * B + 13
     _check_forward(nat, L, size, layers, 99, 17, size - 3, torch.bfloat16)
     _check_backward(nat, L, size, layers, 99, 17, size - 3, torch.bfloat16)
+
+
+@pytest.mark.parametrize("logb", [18, 20])
+@pytest.mark.parametrize("layers", [1, 3])
+def test_large_block_sizes_fp16(nat, logb, layers):
+    """fp16 above 2^17: the 8-byte vector loads and stores of the high-bit pass with fp16 data."""
+    B = 1 << logb
+    L = B - 1000
+    size = 2 * B + 13
+    _check_forward(nat, L, size, layers, 99, 17, size - 3, torch.float16)
+    _check_backward(nat, L, size, layers, 99, 17, size - 3, torch.float16)
+
+
+# bf16 / fp16 latents far from N(0,1): the tensor-core kernels pre-scale each
+# block by a power of two taken from its largest magnitude, so tiny and huge
+# (but finite) inputs keep full relative accuracy.
+EXTREME_BLOCKS = [10, 15, 16, 17, 18]
+
+
+@pytest.mark.parametrize("logb", EXTREME_BLOCKS)
+@pytest.mark.parametrize("scale", [1e-25, 1e-12, 1e12, 1e20, 1e30])
+def test_extreme_magnitudes_bf16(nat, logb, scale):
+    B = 1 << logb
+    L, size = B - 7, 3 * B + 5
+    _check_forward(nat, L, size, 3, 555, 3, size - 2, torch.bfloat16, scale=scale)
+    _check_backward(nat, L, size, 3, 555, 3, size - 2, torch.bfloat16, scale=scale)
+
+
+@pytest.mark.parametrize("logb", EXTREME_BLOCKS)
+@pytest.mark.parametrize("scale", [1e-3, 60.0])
+def test_extreme_magnitudes_fp16(nat, logb, scale):
+    B = 1 << logb
+    L, size = B - 7, 3 * B + 5
+    _check_forward(nat, L, size, 3, 556, 3, size - 2, torch.float16, scale=scale)
+    _check_backward(nat, L, size, 3, 556, 3, size - 2, torch.float16, scale=scale)
+
+
+@pytest.mark.parametrize("logb", [12, 15, 17])
+def test_single_spike_bf16(nat, logb):
+    """One huge element among ordinary ones (the block's scale follows the spike)."""
+    B = 1 << logb
+    z = torch.randn(B, generator=torch.Generator().manual_seed(3))
+    z[B // 3] = 3e25
+    z = z.bfloat16()
+    size = 2 * B
+    y = nat.fht_forward(z.cuda(), size, 3, 9, 0, size)
+    ref = orc.fht_forward(z.float().numpy(), size, 3, 9, 0, size)
+    assert rel_l2(y.float().cpu().numpy(), ref) < 1e-2
+    g = torch.randn(size, generator=torch.Generator().manual_seed(4))
+    g[5] = -1e30
+    g = g.bfloat16()
+    grad = nat.fht_backward(g.cuda(), B, size, 3, 9, 0, size)
+    refg = orc.fht_backward(g.float().numpy(), B, size, 3, 9, 0, size)
+    assert rel_l2(grad.float().cpu().numpy(), refg) < 1e-2
+
+
+# Measured 16-bit error margins at the shapes that matter (relative L2 against
+# fp32 oracle math on the same rounded inputs, layers 3; 2^28-coordinate runs
+# have the same per-block error).  Measured on a B200: bf16 1.80e-3 / 1.80e-3
+# (fwd / bwd) at 2^15, 1.86e-3 / 1.85e-3 at 2^17, 1.81e-3 / 1.81e-3 at 2^23;
+# fp16 7.2e-4 / 7.1e-4, 9.1e-4 / 9.1e-4, 7.5e-4 / 7.5e-4.  bf16 is dominated
+# by the final rounding to bf16 (relative RMS ~2^-9 / sqrt(3)).  The bounds
+# are regression guards at about 1.5x those values; the gate stays 1e-2.
+MARGIN_CASES = [
+    # (log2 B, blocks, dtype, forward bound, backward bound)
+    (15, 16, torch.bfloat16, 2.7e-3, 2.7e-3),
+    (15, 16, torch.float16, 1.1e-3, 1.1e-3),
+    (17, 4, torch.bfloat16, 2.8e-3, 2.8e-3),
+    (17, 4, torch.float16, 1.4e-3, 1.4e-3),
+    (23, 1, torch.bfloat16, 2.7e-3, 2.7e-3),
+    (23, 1, torch.float16, 1.2e-3, 1.2e-3),
+]
+
+
+@pytest.mark.parametrize("logb, blocks, dtype, fbound, bbound", MARGIN_CASES,
+                         ids=[f"B2^{c[0]}_{'bf16' if c[2] == torch.bfloat16 else 'f16'}" for c in MARGIN_CASES])
+def test_half_error_margin(nat, logb, blocks, dtype, fbound, bbound, record_property):
+    B = 1 << logb
+    size = blocks * B
+    ef = _check_forward(nat, B, size, 3, 123, 0, size, dtype)
+    eb = _check_backward(nat, B, size, 3, 123, 0, size, dtype)
+    record_property("forward_rel_l2", ef)
+    record_property("backward_rel_l2", eb)
+    print(f"MARGIN logb={logb} dtype={dtype} layers=3 forward={ef:.3e} backward={eb:.3e}")
+    assert ef < fbound and eb < bbound
 
 
 def test_grouped_forward_matches_single_calls(nat):

@@ -29,6 +29,8 @@ import time
 from pathlib import Path
 
 REPO = Path(__file__).resolve().parent
+# NCCL's own banner would otherwise share stdout with the JSON line
+os.environ.setdefault("NCCL_DEBUG", "WARN")
 sys.path.insert(0, str(REPO / "latent-weight-lab_b200"))
 sys.path.insert(0, str(REPO))
 
@@ -1037,6 +1039,102 @@ def run_gpt2(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_tp(args) -> None:
+    """Tensor-parallel BlockFHTLinear MLP blocks under torchrun (N GPUs, one node):
+    ColumnParallelBlockFHTLinear (up-projection, output features split, each rank
+    generates only its contiguous rows of W) -> GELU -> RowParallelBlockFHTLinear
+    (down-projection, input features split; every rank generates all of W and keeps
+    its columns; partial outputs all-reduced over NCCL).  Forward + backward to
+    both latents and x, bf16, layers 3.  Strong scaling: every rank sees the same
+    tokens.  Two shapes: C3 (768 -> 3072 -> 768, 8192 tokens, latents 32768) and the
+    C5 MLP (1600 -> 6400 -> 1600, 32768 tokens, latents at ratio 0.01 -> block 2^17).
+    Prints one JSON line per shape on rank 0."""
+    import torch
+    import torch.distributed as dist
+
+    from latent_weight_lab import _native
+    from latent_weight_lab.distributed import ColumnParallelBlockFHTLinear, RowParallelBlockFHTLinear
+
+    world, rank, local = _dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl")
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    _native.load()
+    shapes = [("C3 MLP pair", 768, 3072, 8192, 32768), ("C5 MLP (GPT-2-XL)", 1600, 6400, 32768, 102400)]
+    for name, d, f, tokens, latent in shapes:
+        torch.manual_seed(0)
+        up = ColumnParallelBlockFHTLinear(d, f, latent_dim=latent, layers=3, seed=21).to(dev, torch.bfloat16)
+        down = RowParallelBlockFHTLinear(f, d, latent_dim=latent, layers=3, seed=22).to(dev, torch.bfloat16)
+        x = torch.randn(tokens, d, device=dev, dtype=torch.bfloat16, requires_grad=True)
+        gy = torch.randn(tokens, d, device=dev, dtype=torch.bfloat16)
+
+        def step():
+            up.generator.latent.grad = down.generator.latent.grad = x.grad = None
+            down(torch.nn.functional.gelu(up(x))).backward(gy)
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / args.steps
+        # the collectives of one step on their own: forward all-reduce of the
+        # [tokens, d] partial output plus the two latent-gradient all-reduces
+        ar_ms = 0.0
+        if world > 1:
+            buf = torch.randn(tokens, d, device=dev, dtype=torch.bfloat16)
+            lat = torch.randn(2, latent, device=dev, dtype=torch.bfloat16)
+            for _ in range(3):
+                dist.all_reduce(buf)
+                dist.all_reduce(lat)
+            torch.cuda.synchronize()
+            dist.barrier()
+            c, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            c.record()
+            for _ in range(args.steps):
+                dist.all_reduce(buf)
+                dist.all_reduce(lat)
+            e.record()
+            torch.cuda.synchronize()
+            ar_ms = c.elapsed_time(e) / args.steps
+            t = torch.tensor([ms, ar_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms, ar_ms = (float(v) for v in t.tolist())
+        flops = 6.0 * 2 * d * f * tokens
+        peaks = _peaks()
+        achieved = flops / (ms * 1e-3) / 1e12
+        rows = up.rows[1] - up.rows[0]
+        gen_local = rows * d + d * f  # coordinates generated per rank per forward: own rows of W_up, all of W_down
+        if rank == 0:
+            print(json.dumps({
+                "metric": f"tensor-parallel BlockFHTLinear tokens/s ({name} fwd+bwd)",
+                "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (x ~N(0,1), latents ~N(0,0.02))",
+                "config": {"workload": f"{name}: {d} -> {f} -> {d}, {tokens} tokens, latents {latent}, layers 3",
+                           "parallelism": f"tp{world}: column-split up-projection, row-split down-projection"},
+                "allreduce_ms_per_step": ar_ms,
+                "generated_coords_per_rank": gen_local, "generated_coords_total": 2 * d * f,
+                "generation_redundancy": gen_local * world / (2 * d * f),
+                "roofline": {"bound": "tensor", "achieved": achieved / world, "peak": peaks["bf16_tflops"],
+                             "unit": "TFLOP/s per GPU", "frac": achieved / world / peaks["bf16_tflops"],
+                             "traffic": None, "peak_source": peaks["source"]},
+            }), flush=True)
+        del up, down, x, gy
+        torch.cuda.empty_cache()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1045,7 +1143,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-mlp", action="store_true", help="skip the C3 MLP-pair keys of the default line")
-    ap.add_argument("--workload", choices=["fht", "mlp", "sweep", "gpt2", "gpt2xl", "linear", "mix"], default="fht")
+    ap.add_argument("--workload", choices=["fht", "mlp", "sweep", "gpt2", "gpt2xl", "linear", "mix", "tp"], default="fht")
     ap.add_argument("--latent-mode", choices=["ratio", "literal"], default="ratio")
     ap.add_argument("--min-log", type=int, default=5)
     ap.add_argument("--max-log", type=int, default=23)
@@ -1067,6 +1165,8 @@ def main() -> None:
         run_linear(args)
     elif args.workload == "mix":
         run_mix(args)
+    elif args.workload == "tp":
+        run_tp(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -621,7 +621,8 @@ def run_sweep(args) -> None:
     dev = torch.device("cuda", 0)
     N = COORDS_PER_GPU
     stream = torch.cuda.current_stream(dev).cuda_stream
-    for dt_name, dt, code in (("bf16", torch.bfloat16, _native.LWL_BF16), ("fp32", torch.float32, _native.LWL_F32)):
+    kinds = (("bf16", torch.bfloat16, _native.LWL_BF16), ("fp32", torch.float32, _native.LWL_F32))
+    for dt_name, dt, code in (k for k in kinds if k[0] in args.sweep_dtypes.split(",")):
         y = torch.empty(N, device=dev, dtype=dt)
         g = torch.randn(N, device=dev, dtype=dt)
         for layers in (1, 3):
@@ -1147,6 +1148,7 @@ def main() -> None:
     ap.add_argument("--latent-mode", choices=["ratio", "literal"], default="ratio")
     ap.add_argument("--min-log", type=int, default=5)
     ap.add_argument("--max-log", type=int, default=23)
+    ap.add_argument("--sweep-dtypes", default="bf16,fp32", help="--workload sweep: comma-separated bf16,fp32")
     ap.add_argument("--latent", type=int, default=32768, help="latent size for --workload mlp")
     ap.add_argument("--tokens", type=int, default=32768, help="tokens for --workload linear (mix: rows / 2)")
     ap.add_argument("--features", type=int, default=3072, help="features for --workload mix")

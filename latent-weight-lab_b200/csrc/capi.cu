@@ -129,6 +129,7 @@ static int fht_call(bool backward, int dtype, const void* in, void* out, int64_t
     }
     return LWL_OK;
   }
+  if (fht32_supported(dtype, L, backward, flags)) return fht32_run(a, reinterpret_cast<cudaStream_t>(stream));
   FhtPlan plan;
   plan_fht(a, plan);
   if (plan.ws_bytes > 0 && (ws == nullptr || ws_bytes < plan.ws_bytes)) {
@@ -155,6 +156,7 @@ static size_t fht_ws(bool backward, int dtype, int64_t L, int64_t size, int laye
   a.start = start;
   a.stop = stop;
   a.flags = flags;
+  if (fht32_supported(dtype, L, backward, flags)) return fht32_workspace_bytes(a);
   FhtPlan plan;
   plan_fht(a, plan);
   return plan.ws_bytes;
@@ -642,6 +644,7 @@ int lwl_fht_launch_count(int dtype, int64_t latent_size, int64_t size, int layer
   a.start = start;
   a.stop = stop;
   a.flags = flags;
+  if (lwl::fht32_supported(dtype, latent_size, backward != 0, flags)) return lwl::fht32_launches(a);
   lwl::FhtPlan plan;
   lwl::plan_fht(a, plan);
   return plan.nlaunch + (backward ? 1 : 0);

@@ -45,4 +45,11 @@ struct FhtPlan {
 int plan_fht(const FhtArgs& a, FhtPlan& plan);
 int run_fht(const FhtArgs& a, FhtPlan& plan, cudaStream_t st);
 
+// Register-resident fp32 whole-block kernel (fht32.cu): fp32 dtype or
+// LWL_FLAG_EXACT, padded block 2^5 .. 2^15, forward and backward.
+bool fht32_supported(int dtype, int64_t latent_size, bool backward, unsigned flags);
+size_t fht32_workspace_bytes(const FhtArgs& a);
+int fht32_launches(const FhtArgs& a);  // kernels one call enqueues
+int fht32_run(const FhtArgs& a, cudaStream_t st);
+
 }  // namespace lwl

@@ -389,3 +389,18 @@ def test_two_devices_in_one_process(native_lib):
         x = torch.randn(256, 768, device=dev).bfloat16()
         assert _native.linear_forward(x, zd, 3072, 3, 9) is not None
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("logb", [5, 6, 7, 12, 13, 14, 15])
+@pytest.mark.parametrize("layers", [1, 2, 3])
+def test_fp32_whole_block_slices(nat, logb, layers):
+    """The fp32 whole-block kernel: full tiles unpredicated, the slice's edge tiles
+    bounds-checked (one partial tile, two partial tiles with none full, and
+    partial tiles on both sides of full ones), latent shorter than the block."""
+    B = 1 << logb
+    E = max(B, 1 << 13)  # coordinates per tile
+    L = B - (B // 7 if B > 32 else 0)
+    for size, start, stop in [(3 * E + 5, 0, 3 * E + 5), (3 * E + 5, E // 3, E // 2),
+                              (3 * E + 5, E - 9, E + 11), (5 * E, E // 5, 4 * E + 123)]:
+        _check_forward(nat, L, size, layers, 1234 + logb, start, stop, torch.float32)
+        _check_backward(nat, L, size, layers, 1234 + logb, start, stop, torch.float32)

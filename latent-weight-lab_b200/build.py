@@ -14,6 +14,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG_ROOT = Path(__file__).resolve().parent
@@ -44,7 +45,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     BUILD_DIR.mkdir(exist_ok=True)
     LIB_DIR.mkdir(parents=True, exist_ok=True)
     hdr_mtime = max((h.stat().st_mtime for h in _headers()), default=0.0)
-    objs = []
+    objs, cmds = [], []
     changed = force or not LIB.exists()
     for src in sorted(CSRC.glob("*.cu")):
         obj = BUILD_DIR / (src.stem + ".o")
@@ -54,8 +55,13 @@ def build(force: bool = False, verbose: bool = False) -> Path:
             if verbose:
                 cmd += ["-Xptxas", "-v"]
                 print(" ".join(cmd), flush=True)
-            subprocess.run(cmd, check=True)
-            changed = True
+            cmds.append(cmd)
+    if cmds:
+        # translation units compile independently: one nvcc per file, in parallel
+        with ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as pool:
+            for _ in pool.map(lambda c: subprocess.run(c, check=True), cmds):
+                pass
+        changed = True
     if changed or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
         cuda = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
         cmd = [nvcc, *ARCH, "-shared", "-cudart", "shared", "-o", str(LIB), *map(str, objs),

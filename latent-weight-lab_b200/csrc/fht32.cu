@@ -1,439 +1,14 @@
-// fht32.cu -- whole-block BlockFHT in fp32 arithmetic for padded block sizes
-// 2^5 .. 2^15 (forward and latent-gradient backward).
-//
-// The generic tile engine (fht_tile.cuh) spends most of its time on
-// per-element bookkeeping (64-bit position math, bounds tests, a sign-table
-// read per element).  This kernel instead keeps the data in registers:
-//
-//  * A CTA owns a "tile" of 2^TB consecutive generated coordinates
-//    (2^(TB-n) whole blocks of B = 2^n; TB = 13 for n <= 13, so that four
-//    CTAs of 128 threads share an SM and overlap each other's phases, else
-//    TB = n with 2^(TB-6) threads).  Every thread holds 64 values; the TB tile
-//    bits t are split into 6 register bits, 5 lane bits and TB-11 warp bits.
-//    Three fixed splits ("sets") are used (shown for TB = 15):
-//        A: registers t0..t5,  lanes t6..t10, warps t11..t14
-//        B: registers t6..t11, lanes t0..t4,  warps t5, t12..t14
-//        C: registers t9..t14, lanes t0..t4,  warps t5..t8
-//    (C holds the top six tile bits).  A butterfly over a register bit is
-//    pure register arithmetic.
-//  * Between sets the tile goes through shared memory (one fp32 buffer of
-//    2^TB words plus one pad word per 64).  With that padding the lanes of A
-//    (t6..t10) and of B/C (t0..t4) fall on distinct banks, so every warp
-//    access of both the writer and the reader is conflict free.
-//  * The layer order is scheduled so that neighbouring layers share a set:
-//    3 layers at n = 13..15 take 7 residencies (6 exchanges), at n = 7..12
-//    four (3 exchanges), and at n <= 6 the whole chain runs in registers
-//    (one exchange to lay the output out for coalesced stores).
-//  * Signs: per tile and sign layer, the tile's sign words sit in shared
-//    memory (the reference's stateless hash, lwl_common.cuh); a clear bit
-//    flips the float's sign bit.  The layers' 1/sqrt(B) factors are applied
-//    together, once, to the results (exact for even n, one rounding for odd n).
-//  * The forward ends in set B or C, whose lanes run along t0..t4, so each
-//    warp store writes 32 consecutive outputs.  The backward ends the same
-//    way, sums the tile's blocks through shared memory and adds the result to
-//    this CTA's [L] partial row in global memory (one thread per address, in
-//    tile order, so the sums are deterministic); fht32_reduce_kernel then
-//    sums the rows in a fixed order.
-//
-// Arithmetic is the reference's (fp32 butterflies and signs;
-// latent_weight_lab/block_fht.py:18-33, 84-109) up to the order of the
-// additions and where the normalisation is applied; results agree with the
-// reference to fp32 rounding.
+// fht32.cu -- host side of the fp32 whole-block transform (fht32.cuh):
+// kernel choice, persistent grid, full/edge tile split, launches and the
+// deterministic reduce of the backward's partial rows.
 #include <algorithm>
 #include <cmath>
 #include <cstring>
 
-#include "fht_engine.h"
-#include "lwl_common.cuh"
+#include "fht32.cuh"
 
 namespace lwl {
 namespace f32k {
-
-constexpr int kRegs = 64;  // values per thread (6 register bits)
-constexpr int kMaxSlots = 4;
-
-template <int TB>
-struct Tile {
-  static constexpr int kE = 1 << TB;
-  static constexpr int kThreads = 1 << (TB - 6);
-  static constexpr int kWords = kE / 32;
-  static constexpr int kBufWords = kE + kE / 16;
-  static constexpr size_t kSmem = size_t(kBufWords) * 4 + size_t(kMaxSlots) * kWords * 4;
-  static constexpr int kMinBlocks = TB == 13 ? 4 : 1;
-  // register bits of the sets, as tile-bit masks
-  static constexpr int kA = 0x3F, kB = 0xFC0, kC = 0x3F << (TB - 6);
-  static constexpr int kChi = ((1 << TB) - 1) & ~0xFFF;       // C bits above B
-  static constexpr int kBsub = ((1 << (TB - 6)) - 1) & ~0x3F;  // B bits below C
-};
-
-enum Set : int { SA = 0, SB = 1, SC = 2 };
-
-template <int TB>
-__host__ __device__ constexpr int reg_bit(int set, int j) { return set == SA ? j : (set == SB ? 6 + j : TB - 6 + j); }
-
-// tile index of register rho of this thread = base | spread(rho) (disjoint bits)
-template <int TB, int SET>
-__device__ __forceinline__ int base_of(int lane, int warp) {
-  if (SET == SA) return (lane << 6) | (warp << 11);
-  if (SET == SB) return lane | ((warp & 1) << 5) | ((warp >> 1) << 12);
-  return lane | (warp << 5);
-}
-template <int TB, int SET>
-__host__ __device__ constexpr int spread(int rho) {
-  return SET == SA ? rho : (SET == SB ? rho << 6 : rho << (TB - 6));
-}
-
-// Shared-memory word address of tile element t: four pad words per 64.  For
-// every set the lanes of a warp then hit distinct banks (lanes on t6..t10
-// give bank t0..t4 + 4*lane, so each quarter-warp's 16-byte accesses of four
-// consecutive registers cover all 32 banks; lanes on t0..t4 give
-// lane + const), and pad(base | spread) = pad(base) + pad(spread), so each
-// register's address is the thread's base plus a compile-time offset.  Set A
-// moves four consecutive registers per 16-byte access.
-__host__ __device__ constexpr int pad(int t) { return t + 4 * (t >> 6); }
-
-struct Params {
-  const void* src;  // forward: latent [L]; backward: grad slice [stop - start]
-  void* dst;        // forward: output slice; backward: partial rows [grid][L]
-  int64_t L;
-  int n;            // log2 B (5..15)
-  int layers;
-  uint32_t seed32;
-  float scale;      // 1/sqrt(B)^layers, applied once to the results
-  int64_t start, stop;
-  int64_t first_tile, ntiles, tile_step;  // tiles first_tile + i * tile_step, i < ntiles
-  int row0;                               // backward: first partial row of this launch
-  int slot_layer[kMaxSlots];              // sign layer of slot s, in chain order
-};
-
-template <typename T>
-__device__ __forceinline__ float ld_elem(const T* p) {
-  return Cvt<T>::to_f(p[0]);
-}
-
-// Butterflies over the register bits of SET whose tile bits are in `mask`
-// and below n (tile bits from n up select blocks, not positions).
-template <int TB, int SET>
-__device__ __forceinline__ void xform(float (&v)[kRegs], int mask, int n) {
-#pragma unroll
-  for (int j = 0; j < 6; ++j) {
-    const int tb = reg_bit<TB>(SET, j);
-    if (((mask >> tb) & 1) && tb < n) {
-      const int h = 1 << j;
-#pragma unroll
-      for (int r = 0; r < kRegs; ++r) {
-        if (r & h) continue;
-        const float a = v[r], b = v[r | h];
-        v[r] = a + b;
-        v[r | h] = a - b;
-      }
-    }
-  }
-}
-
-// Sign flips of one layer: a clear sign bit negates (XOR of the float sign
-// bit).  The 1/sqrt(B) of each layer is applied once, at the output.
-__device__ __forceinline__ float flip(float x, uint32_t m) { return __uint_as_float(__float_as_uint(x) ^ m); }
-
-template <int TB, int SET>
-__device__ __forceinline__ void apply_sign(float (&v)[kRegs], const uint32_t* sw, int base) {
-  if (SET == SA) {
-    // t0..t4 are register bits: two words per thread; bit r of ~w moved to bit 31
-    const uint32_t w0 = ~sw[base >> 5], w1 = ~sw[(base >> 5) | 1];
-#pragma unroll
-    for (int r = 0; r < kRegs; ++r) {
-      const uint32_t w = (r & 32) ? w1 : w0;
-      v[r] = flip(v[r], (w << (31 - (r & 31))) & 0x80000000u);
-    }
-  } else {
-    // t0..t4 are the lane: one bit of a (warp-uniform) word per register;
-    // (base >> 5) and (spread >> 5) have disjoint bits
-    const int sh = 31 - (base & 31);
-    const uint32_t* swb = sw + (base >> 5);
-#pragma unroll
-    for (int r = 0; r < kRegs; ++r) v[r] = flip(v[r], (~swb[spread<TB, SET>(r) >> 5] << sh) & 0x80000000u);
-  }
-}
-
-template <int TB, int SET>
-__device__ __forceinline__ void smem_write(const float (&v)[kRegs], float* b) {
-  if (SET == SA) {
-#pragma unroll
-    for (int q = 0; q < kRegs / 4; ++q)
-      *reinterpret_cast<float4*>(b + pad(4 * q)) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-  } else {
-#pragma unroll
-    for (int r = 0; r < kRegs; ++r) b[pad(spread<TB, SET>(r))] = v[r];
-  }
-}
-template <int TB, int SET>
-__device__ __forceinline__ void smem_read(float (&v)[kRegs], const float* b) {
-  if (SET == SA) {
-#pragma unroll
-    for (int q = 0; q < kRegs / 4; ++q) {
-      const float4 x = *reinterpret_cast<const float4*>(b + pad(4 * q));
-      v[4 * q] = x.x, v[4 * q + 1] = x.y, v[4 * q + 2] = x.z, v[4 * q + 3] = x.w;
-    }
-  } else {
-#pragma unroll
-    for (int r = 0; r < kRegs; ++r) v[r] = b[pad(spread<TB, SET>(r))];
-  }
-}
-
-template <int TB, int X, int Y>
-__device__ __forceinline__ void exchange(float (&v)[kRegs], float* buf, int lane, int warp) {
-  __syncthreads();  // every thread has finished reading the buffer
-  smem_write<TB, X>(v, buf + pad(base_of<TB, X>(lane, warp)));
-  __syncthreads();
-  smem_read<TB, Y>(v, buf + pad(base_of<TB, Y>(lane, warp)));
-}
-
-// First residency: the tile's source values in set SET, zero outside the
-// latent (forward) or the slice (backward).
-template <typename T, int TB, int SET, bool BWD, bool FULL>
-__device__ __forceinline__ void load_first(float (&v)[kRegs], const Params& p, int64_t tile, int base) {
-  constexpr int kE = Tile<TB>::kE;
-  const T* src = reinterpret_cast<const T*>(p.src);
-  const int Bm = (1 << p.n) - 1;
-  if (SET == SA) {
-    // 64 consecutive tile elements per thread: 4-element vector loads where possible
-    const T* s;
-    int lo, hi;  // valid register offsets [lo, hi) relative to s
-    if (BWD) {
-      const int64_t off = (tile << TB) + base - p.start;
-      s = src + off;
-      lo = (int)std::min<int64_t>(std::max<int64_t>(-off, 0), kRegs);
-      hi = (int)std::min<int64_t>(std::max<int64_t>(p.stop - p.start - off, 0), kRegs);
-    } else {
-      // position = t mod B; (base & Bm) and the register offsets have disjoint bits
-      const int pb = base & Bm;
-      s = src + pb;
-      lo = 0;
-      hi = (int)std::min<int64_t>(std::max<int64_t>(p.L - pb, 0), kRegs);
-    }
-    // vector loads need 4-element alignment, which a slice start not divisible by 4 breaks
-    const bool vec = (reinterpret_cast<uintptr_t>(s) & (4 * sizeof(T) - 1)) == 0 &&
-                     ((BWD && FULL) || (lo == 0 && hi == kRegs));
-    if (vec) {
-#pragma unroll
-      for (int q = 0; q < kRegs / 4; ++q) {
-        const int o = BWD ? 4 * q : ((4 * q) & Bm);
-        if (sizeof(T) == 4) {
-          const float4 x = *reinterpret_cast<const float4*>(s + o);
-          v[4 * q] = x.x, v[4 * q + 1] = x.y, v[4 * q + 2] = x.z, v[4 * q + 3] = x.w;
-        } else {
-          const uint2 x = *reinterpret_cast<const uint2*>(s + o);
-          const T* e = reinterpret_cast<const T*>(&x);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) v[4 * q + i] = Cvt<T>::to_f(e[i]);
-        }
-      }
-    } else {
-#pragma unroll
-      for (int r = 0; r < kRegs; ++r) {
-        const int o = BWD ? r : (r & Bm);
-        v[r] = (o >= lo && o < hi) ? ld_elem(s + o) : 0.0f;
-      }
-    }
-  } else if (BWD && FULL) {
-    const T* s = src + ((tile << TB) + base - p.start);
-#pragma unroll
-    for (int r = 0; r < kRegs; ++r) v[r] = ld_elem(s + spread<TB, SET>(r));
-  } else if (BWD) {
-    const int64_t off = (tile << TB) + base - p.start;
-    const T* s = src + off;
-    const int lo = (int)std::min<int64_t>(std::max<int64_t>(-off, 0), kE);
-    const int hi = (int)std::min<int64_t>(std::max<int64_t>(p.stop - p.start - off, 0), kE);
-#pragma unroll
-    for (int r = 0; r < kRegs; ++r) {
-      const int o = spread<TB, SET>(r);
-      v[r] = (o >= lo && o < hi) ? ld_elem(s + o) : 0.0f;
-    }
-  } else {
-    // position = t mod B; (base & Bm) and (spread & Bm) have disjoint bits
-    const int pb = base & Bm;
-    const T* s = src + pb;
-    if (p.L == Bm + 1) {
-#pragma unroll
-      for (int r = 0; r < kRegs; ++r) v[r] = ld_elem(s + (spread<TB, SET>(r) & Bm));
-    } else {
-      const int hi = (int)std::min<int64_t>(p.L - pb, kE);
-#pragma unroll
-      for (int r = 0; r < kRegs; ++r) {
-        const int q = spread<TB, SET>(r) & Bm;
-        v[r] = q < hi ? ld_elem(s + q) : 0.0f;
-      }
-    }
-  }
-}
-
-// Forward output from set B or C (lanes along t0..t4: 32 consecutive outputs per warp store).
-template <typename T, int TB, int SET, bool FULL>
-__device__ __forceinline__ void store_out(const float (&v)[kRegs], const Params& p, int64_t tile, int base) {
-  constexpr int kE = Tile<TB>::kE;
-  const int64_t off = (tile << TB) - p.start + base;
-  T* dst = reinterpret_cast<T*>(p.dst) + off;
-  if (FULL) {
-#pragma unroll
-    for (int r = 0; r < kRegs; ++r) dst[spread<TB, SET>(r)] = Cvt<T>::from_f(v[r] * p.scale);
-    return;
-  }
-  // valid offsets [lo, hi) relative to dst (the whole tile unless it straddles the slice)
-  const int lo = (int)std::min<int64_t>(std::max<int64_t>(-off, 0), kE);
-  const int hi = (int)std::min<int64_t>(std::max<int64_t>(p.stop - p.start - off, 0), kE);
-#pragma unroll
-  for (int r = 0; r < kRegs; ++r) {
-    const int o = spread<TB, SET>(r);
-    if (o >= lo && o < hi) dst[o] = Cvt<T>::from_f(v[r] * p.scale);
-  }
-}
-
-// Backward: the tile's per-block results (set B or C) summed over its blocks
-// into this CTA's partial row.  Thread i owns positions i, i + threads, ...
-// for the whole kernel, so each address sees its additions in tile order.
-template <int TB, int SET>
-__device__ __forceinline__ void accumulate(const float (&v)[kRegs], float* buf, const Params& p, int base, int tid) {
-  __syncthreads();
-  float* wb = buf + pad(base);
-#pragma unroll
-  for (int r = 0; r < kRegs; ++r) wb[pad(spread<TB, SET>(r))] = v[r];
-  __syncthreads();
-  float* row = reinterpret_cast<float*>(p.dst) + (int64_t)(p.row0 + blockIdx.x) * p.L;
-  const int nb = 1 << (TB - p.n);
-  for (int q = tid; q < p.L; q += Tile<TB>::kThreads) {
-    float s = 0.0f;
-    for (int k = 0; k < nb; ++k) s += buf[pad((k << p.n) | q)];
-    atomicAdd(row + q, s * p.scale);  // one thread per address: program order, deterministic
-  }
-}
-
-// Residency schedules.  KCLS 1: n <= 6 (one register set); 2: n = 7..12 (sets
-// A and B); 3: n = 13..15 (A, B and C = the top six bits).  Slot 0 is the
-// pre-sign (no scale); slot l+1 follows network l and carries 1/sqrt(B).
-template <typename T, int TB, int LAYERS, bool BWD, int KCLS, bool FULL>
-__global__ void __launch_bounds__(Tile<TB>::kThreads, Tile<TB>::kMinBlocks)
-    fht32_kernel(const __grid_constant__ Params p) {
-  using Tl = Tile<TB>;
-  extern __shared__ __align__(16) unsigned char smem[];
-  float* buf = reinterpret_cast<float*>(smem);
-  uint32_t* sw = reinterpret_cast<uint32_t*>(buf + Tl::kBufWords);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int n = p.n;
-  if (BWD) {
-    float* row = reinterpret_cast<float*>(p.dst) + (int64_t)(p.row0 + blockIdx.x) * p.L;
-    for (int q = tid; q < p.L; q += Tl::kThreads) row[q] = 0.0f;
-  }
-  const int bA = base_of<TB, SA>(lane, warp), bB = base_of<TB, SB>(lane, warp), bC = base_of<TB, SC>(lane, warp);
-  float v[kRegs];
-  for (int64_t it = blockIdx.x; it < p.ntiles; it += gridDim.x) {
-    const int64_t tile = p.first_tile + it * p.tile_step;
-    __syncthreads();  // the previous tile is done with the sign table
-    {
-      const int wsh = n - 5;  // words per block = 2^(n-5)
-      const int64_t blk0 = tile << (TB - n);
-      for (int i = tid; i < (LAYERS + 1) * Tl::kWords; i += Tl::kThreads) {
-        const int s = i / Tl::kWords, c = i - s * Tl::kWords;
-        sw[i] = sign_word(block_layer_key(p.seed32, blk0 + (c >> wsh), p.slot_layer[s]), c & ((1 << wsh) - 1));
-      }
-    }
-    __syncthreads();
-    const uint32_t* s0 = sw;
-    const uint32_t* s1 = sw + Tl::kWords;
-    const uint32_t* s2 = sw + 2 * Tl::kWords;
-    const uint32_t* s3 = sw + 3 * Tl::kWords;
-    if constexpr (KCLS == 1) {
-      load_first<T, TB, SA, BWD, FULL>(v, p, tile, bA);
-      apply_sign<TB, SA>(v, s0, bA);
-      xform<TB, SA>(v, Tl::kA, n);
-      apply_sign<TB, SA>(v, s1, bA);
-      if (LAYERS >= 2) {
-        xform<TB, SA>(v, Tl::kA, n);
-        apply_sign<TB, SA>(v, s2, bA);
-      }
-      if (LAYERS >= 3) {
-        xform<TB, SA>(v, Tl::kA, n);
-        apply_sign<TB, SA>(v, s3, bA);
-      }
-      exchange<TB, SA, SB>(v, buf, lane, warp);
-      if (BWD) accumulate<TB, SB>(v, buf, p, bB, tid);
-      else store_out<T, TB, SB, FULL>(v, p, tile, bB);
-    } else if constexpr (KCLS == 2) {
-      if (LAYERS == 2) {
-        load_first<T, TB, SB, BWD, FULL>(v, p, tile, bB);
-        apply_sign<TB, SB>(v, s0, bB);
-        xform<TB, SB>(v, Tl::kB, n);
-        exchange<TB, SB, SA>(v, buf, lane, warp);
-        xform<TB, SA>(v, Tl::kA, n);
-        apply_sign<TB, SA>(v, s1, bA);
-        xform<TB, SA>(v, Tl::kA, n);
-        exchange<TB, SA, SB>(v, buf, lane, warp);
-        xform<TB, SB>(v, Tl::kB, n);
-        apply_sign<TB, SB>(v, s2, bB);
-      } else {
-        load_first<T, TB, SA, BWD, FULL>(v, p, tile, bA);
-        apply_sign<TB, SA>(v, s0, bA);
-        xform<TB, SA>(v, Tl::kA, n);
-        exchange<TB, SA, SB>(v, buf, lane, warp);
-        xform<TB, SB>(v, Tl::kB, n);
-        apply_sign<TB, SB>(v, s1, bB);
-        if (LAYERS == 3) {
-          xform<TB, SB>(v, Tl::kB, n);
-          exchange<TB, SB, SA>(v, buf, lane, warp);
-          xform<TB, SA>(v, Tl::kA, n);
-          apply_sign<TB, SA>(v, s2, bA);
-          xform<TB, SA>(v, Tl::kA, n);
-          exchange<TB, SA, SB>(v, buf, lane, warp);
-          xform<TB, SB>(v, Tl::kB, n);
-          apply_sign<TB, SB>(v, s3, bB);
-        }
-      }
-      if (BWD) accumulate<TB, SB>(v, buf, p, bB, tid);
-      else store_out<T, TB, SB, FULL>(v, p, tile, bB);
-    } else {
-      if (LAYERS == 2) {
-        load_first<T, TB, SC, BWD, FULL>(v, p, tile, bC);
-        apply_sign<TB, SC>(v, s0, bC);
-        xform<TB, SC>(v, Tl::kC, n);
-        exchange<TB, SC, SA>(v, buf, lane, warp);
-        xform<TB, SA>(v, Tl::kA, n);
-        exchange<TB, SA, SB>(v, buf, lane, warp);
-        xform<TB, SB>(v, Tl::kBsub, n);
-        apply_sign<TB, SB>(v, s1, bB);
-        xform<TB, SB>(v, Tl::kB, n);
-        exchange<TB, SB, SA>(v, buf, lane, warp);
-        xform<TB, SA>(v, Tl::kA, n);
-        exchange<TB, SA, SC>(v, buf, lane, warp);
-        xform<TB, SC>(v, Tl::kChi, n);
-        apply_sign<TB, SC>(v, s2, bC);
-      } else {
-        load_first<T, TB, SA, BWD, FULL>(v, p, tile, bA);
-        apply_sign<TB, SA>(v, s0, bA);
-        xform<TB, SA>(v, Tl::kA, n);
-        exchange<TB, SA, SB>(v, buf, lane, warp);
-        xform<TB, SB>(v, Tl::kB, n);
-        exchange<TB, SB, SC>(v, buf, lane, warp);
-        xform<TB, SC>(v, Tl::kChi, n);
-        apply_sign<TB, SC>(v, s1, bC);
-        if (LAYERS == 3) {
-          xform<TB, SC>(v, Tl::kC, n);
-          exchange<TB, SC, SA>(v, buf, lane, warp);
-          xform<TB, SA>(v, Tl::kA, n);
-          exchange<TB, SA, SB>(v, buf, lane, warp);
-          xform<TB, SB>(v, Tl::kBsub, n);
-          apply_sign<TB, SB>(v, s2, bB);
-          xform<TB, SB>(v, Tl::kB, n);
-          exchange<TB, SB, SA>(v, buf, lane, warp);
-          xform<TB, SA>(v, Tl::kA, n);
-          exchange<TB, SA, SC>(v, buf, lane, warp);
-          xform<TB, SC>(v, Tl::kChi, n);
-          apply_sign<TB, SC>(v, s3, bC);
-        }
-      }
-      if (BWD) accumulate<TB, SC>(v, buf, p, bC, tid);
-      else store_out<T, TB, SC, FULL>(v, p, tile, bC);
-    }
-  }
-}
 
 int sms() {
   int dev = 0, n = 148;
@@ -441,43 +16,9 @@ int sms() {
   return n;
 }
 
-int tile_bits(int n) { return n <= 13 ? 13 : n; }
-
-// Kernel of one (dtype, tile size, layer count, direction, full tiles), chosen by n.
-template <typename T, int TB, int LAYERS, bool BWD, bool FULL>
-const void* kernel_for(int n) {
-  if constexpr (TB > 13) {
-    return (const void*)fht32_kernel<T, TB, LAYERS, BWD, 3, FULL>;
-  } else {
-    if (n <= 6) return (const void*)fht32_kernel<T, TB, LAYERS, BWD, 1, FULL>;
-    if (n <= 12) return (const void*)fht32_kernel<T, TB, LAYERS, BWD, 2, FULL>;
-    return (const void*)fht32_kernel<T, TB, LAYERS, BWD, 3, FULL>;
-  }
-}
-
-template <typename T, bool BWD, bool FULL>
-const void* pick_tb(int n, int layers, int TB) {
-  if (TB == 13)
-    return layers == 1 ? kernel_for<T, 13, 1, BWD, FULL>(n)
-                       : (layers == 2 ? kernel_for<T, 13, 2, BWD, FULL>(n) : kernel_for<T, 13, 3, BWD, FULL>(n));
-  if (TB == 14)
-    return layers == 1 ? kernel_for<T, 14, 1, BWD, FULL>(n)
-                       : (layers == 2 ? kernel_for<T, 14, 2, BWD, FULL>(n) : kernel_for<T, 14, 3, BWD, FULL>(n));
-  return layers == 1 ? kernel_for<T, 15, 1, BWD, FULL>(n)
-                     : (layers == 2 ? kernel_for<T, 15, 2, BWD, FULL>(n) : kernel_for<T, 15, 3, BWD, FULL>(n));
-}
-
-template <typename T>
-const void* pick(bool bwd, bool full, int n, int layers, int TB) {
-  if (bwd) return full ? pick_tb<T, true, true>(n, layers, TB) : pick_tb<T, true, false>(n, layers, TB);
-  return full ? pick_tb<T, false, true>(n, layers, TB) : pick_tb<T, false, false>(n, layers, TB);
-}
-
 const void* kernel_of(int dtype, bool bwd, bool full, int n, int layers) {
-  const int TB = tile_bits(n);
-  if (dtype == LWL_BF16) return pick<__nv_bfloat16>(bwd, full, n, layers, TB);
-  if (dtype == LWL_F16) return pick<__half>(bwd, full, n, layers, TB);
-  return pick<float>(bwd, full, n, layers, TB);
+  if (dtype == LWL_F32) return bwd ? kernel_f32_bwd(full, n, layers) : kernel_f32_fwd(full, n, layers);
+  return bwd ? kernel_half_bwd(dtype, full, n, layers) : kernel_half_fwd(dtype, full, n, layers);
 }
 
 size_t smem_of(int TB) {

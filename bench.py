@@ -1078,12 +1078,34 @@ def run_tp(args) -> None:
         for _ in range(args.warmup):
             step()
         torch.cuda.synchronize()
+        # the whole step (generation, GEMMs, NCCL collectives, latent projections)
+        # replayed as one CUDA graph when capture works, else eager
+        run, mode, graph = step, "eager", None
+        if not args.eager:
+            try:
+                side = torch.cuda.Stream(dev)
+                side.wait_stream(torch.cuda.current_stream(dev))
+                with torch.cuda.stream(side):
+                    step()
+                torch.cuda.current_stream(dev).wait_stream(side)
+                torch.cuda.synchronize()
+                up.generator.latent.grad = down.generator.latent.grad = x.grad = None
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    down(torch.nn.functional.gelu(up(x))).backward(gy)
+                for _ in range(args.warmup):
+                    graph.replay()
+                torch.cuda.synchronize()
+                run, mode = graph.replay, "one CUDA graph per step"
+            except Exception as exc:  # capture unsupported here: time the eager step
+                mode = f"eager (graph capture failed: {type(exc).__name__})"
+                torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(args.steps):
-            step()
+            run()
         b.record()
         torch.cuda.synchronize()
         ms = a.elapsed_time(b) / args.steps
@@ -1121,7 +1143,8 @@ def run_tp(args) -> None:
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic (x ~N(0,1), latents ~N(0,0.02))",
                 "config": {"workload": f"{name}: {d} -> {f} -> {d}, {tokens} tokens, latents {latent}, layers 3",
-                           "parallelism": f"tp{world}: column-split up-projection, row-split down-projection"},
+                           "parallelism": f"tp{world}: column-split up-projection, row-split down-projection",
+                           "execution": mode},
                 "allreduce_ms_per_step": ar_ms,
                 "generated_coords_per_rank": gen_local, "generated_coords_total": 2 * d * f,
                 "generation_redundancy": gen_local * world / (2 * d * f),
@@ -1129,11 +1152,16 @@ def run_tp(args) -> None:
                              "unit": "TFLOP/s per GPU", "frac": achieved / world / peaks["bf16_tflops"],
                              "traffic": None, "peak_source": peaks["source"]},
             }), flush=True)
+        run = graph = None  # release the captured graph (and its NCCL work) before the next shape
+        torch.cuda.synchronize()
         del up, down, x, gy
         torch.cuda.empty_cache()
     if world > 1:
         dist.barrier()
-        dist.destroy_process_group()
+        # a process group whose collectives were captured in CUDA graphs can
+        # block in destroy_process_group; process exit releases NCCL instead
+        sys.stdout.flush()
+        os._exit(0)
 
 
 def main() -> None:

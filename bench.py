@@ -351,7 +351,8 @@ def run_ours(args) -> None:
             "backward_gcoords_s": COORDS_PER_GPU / (bm * 1e-3) / 1e9,
             "roofline": {"bound": "hbm", "kernel": "forward" if dom_is_f else "backward", "achieved": achieved,
                          "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
-                         "traffic": _traffic_from_profiles("fwd" if dom_is_f else "bwd"),
+                         "traffic": _traffic_from_profiles("fwd" if dom_is_f else "bwd")
+                         if COORDS_PER_GPU == 1 << 28 else None,
                          "peak_source": peaks["source"], "bytes_per_launch": dom_bytes,
                          "ms_per_launch": dom_ms},
             "e2e": {"value": size_total / (e2e_ms * 1e-3) / 1e9, "unit": "Gcoords/s",
@@ -611,7 +612,7 @@ def run_mlp(args) -> None:
 
 def run_sweep(args) -> None:
     """C2 sweep: every padded block size 2^5..2^23, layers 1 and 3, bf16 and fp32,
-    2^28 coordinates per call (latent length = block size); forward and backward
+    2^28 coordinates per call (--log-coords) (latent length = block size); forward and backward
     Gcoords/s, one JSON line per point."""
     import torch
 
@@ -1172,6 +1173,9 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-mlp", action="store_true", help="skip the C3 MLP-pair keys of the default line")
+    ap.add_argument("--log-coords", type=int, default=28,
+                    help="default workload: log2 of the generated coordinates per GPU (28 = the benchmark; "
+                         "smaller values give the reduced cases that ncu captures run on)")
     ap.add_argument("--workload", choices=["fht", "mlp", "sweep", "gpt2", "gpt2xl", "linear", "mix", "tp"], default="fht")
     ap.add_argument("--latent-mode", choices=["ratio", "literal"], default="ratio")
     ap.add_argument("--min-log", type=int, default=5)
@@ -1183,6 +1187,8 @@ def main() -> None:
     ap.add_argument("--xl-layers", type=int, default=48, help="layers for --workload gpt2xl")
     ap.add_argument("--eager", action="store_true", help="--workload mlp without CUDA-graph capture")
     args = ap.parse_args()
+    global COORDS_PER_GPU
+    COORDS_PER_GPU = 1 << args.log_coords
     if args.workload == "mlp":
         run_mlp(args)
     elif args.workload == "sweep":

@@ -332,6 +332,21 @@ def run_ours(args) -> None:
         e2e_ms = float(tt.item())
 
     mlp = None if args.no_mlp else measure_mlp_pair(dev, world, max(args.steps, 10), args.warmup)
+    # the GPT-shaped configurations on the same line: C5 training (data parallel
+    # under torchrun) and, on one GPU, C4 inference; the headline's buffers go first
+    del g, y, ws, mod, grad_host
+    torch.cuda.empty_cache()
+    gpt = {}
+    if not args.no_gpt:
+        for key, fn in (("gpt2xl", lambda: measure_gpt2xl(dev, world, rank, 3, 2)),
+                        ("gpt2", (lambda: measure_gpt2(dev, 10, 3)) if world == 1 else None)):
+            if fn is None:
+                continue
+            try:
+                gpt[key] = fn()
+            except Exception as exc:  # reported on the line; the headline stands on its own
+                gpt[key] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+                torch.cuda.empty_cache()
 
     if rank == 0:
         peaks = _peaks()
@@ -367,6 +382,7 @@ def run_ours(args) -> None:
                 mlp["cpu_baseline"] = cpu_mlp_sample(host_threads())
         if mlp is not None:
             line["mlp_pair"] = mlp
+        line.update(gpt)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -795,7 +811,8 @@ def _native_pow2(v: int) -> int:
     return 1 << (int(v) - 1).bit_length()
 
 
-def run_gpt2xl(args) -> None:
+def measure_gpt2xl(dev, world: int, rank: int, steps: int, warmup: int, n_layer: int = 48,
+                   latent_mode: str = "ratio") -> dict:
     """C5: GPT-2-XL-shaped training step (48 layers, d=1600, 25 heads, MLP 6400,
     seq 1024, batch 32 = 32768 tokens per GPU, vocab 50257 padded to 50304)
     with every qkv / attn-proj / fc / fc-proj weight generated by BlockFHT
@@ -813,19 +830,13 @@ def run_gpt2xl(args) -> None:
     import torch.distributed as dist
     import torch.nn.functional as F
 
-    from latent_weight_lab import BlockFHTLinear, _native
+    from latent_weight_lab import BlockFHTLinear
 
-    world, rank, local = _dist_env()
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
-    _native.load()
     torch.manual_seed(0)
-    n_layer, d, n_head, T, Bsz, vocab = args.xl_layers, 1600, 25, 1024, 32, 50304
+    d, n_head, T, Bsz, vocab = 1600, 25, 1024, 32, 50304
 
     def lin(i, o, seed):
-        lat = max(1, round(i * o * (0.01 if args.latent_mode == "ratio" else 1 / 16)))
+        lat = max(1, round(i * o * (0.01 if latent_mode == "ratio" else 1 / 16)))
         return BlockFHTLinear(i, o, bias=True, latent_dim=lat, layers=3, seed=seed)
 
     class Block(torch.nn.Module):
@@ -888,19 +899,20 @@ def run_gpt2xl(args) -> None:
         opt.step()
         loss_host.copy_(loss.detach(), non_blocking=True)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(dev.index) as clk:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         a.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             step()
         b.record()
         torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / args.steps
+    ms = a.elapsed_time(b) / steps
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -908,34 +920,54 @@ def run_gpt2xl(args) -> None:
         dist.barrier()
     lin_flops_tok = 6 * n_layer * (d * 3 * d + d * d + 2 * d * 4 * d)
     tokens = Bsz * T * world
+    peaks = _peaks()
+    achieved = tokens / world * lin_flops_tok / (ms * 1e-3) / 1e12
+    out = {
+        "metric": "GPT-2-XL training tokens/s, BlockFHT-generated linears (C5)",
+        "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic token ids and targets (uniform, seed 1234 + rank), random-init weights",
+        "config": {"workload": f"C5 GPT-2-XL training step, latent mode {latent_mode}", "batch": Bsz,
+                   "seq_len": T, "layers": n_layer, "d_model": d, "heads": n_head, "vocab_padded": vocab,
+                   "parallelism": f"dp{world} (latent-gradient all-reduce, NCCL)",
+                   "step": "forward + cross-entropy + backward + gradient all-reduce + fused AdamW",
+                   "trainable_params_per_rank": n_grad},
+        "e2e": {"value": tokens / (ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": 2 * Bsz * T * 8,
+                "d2h_bytes_per_step": 4, "note": "token ids in and the loss out are inside every timed step"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / peaks["bf16_tflops"], "traffic": None, "peak_source": peaks["source"],
+                     "counted": "6 * linear FLOPs per token (fwd + grad_x + grad_W); generation, attention "
+                                "and the LM head not counted"},
+        "clocks": clk.summary(),
+    }
+    del model, opt, params, flat_grad
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_gpt2xl(args) -> None:
+    """C5 on its own line (see measure_gpt2xl); under torchrun, data parallel."""
+    import torch
+    import torch.distributed as dist
+
+    from latent_weight_lab import _native
+
+    world, rank, local = _dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    _native.load()
+    line = measure_gpt2xl(dev, world, rank, args.steps, args.warmup, args.xl_layers, args.latent_mode)
     if rank == 0:
-        peaks = _peaks()
-        achieved = tokens / world * lin_flops_tok / (ms * 1e-3) / 1e12
-        line = {
-            "metric": "GPT-2-XL training tokens/s, BlockFHT-generated linears (C5)",
-            "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic token ids and targets (uniform, seed 1234 + rank), random-init weights",
-            "config": {"workload": f"C5 GPT-2-XL training step, latent mode {args.latent_mode}", "batch": Bsz,
-                       "seq_len": T, "layers": n_layer, "d_model": d, "heads": n_head, "vocab_padded": vocab,
-                       "parallelism": f"dp{world} (latent-gradient all-reduce, NCCL)",
-                       "step": "forward + cross-entropy + backward + gradient all-reduce + fused AdamW",
-                       "trainable_params_per_rank": n_grad},
-            "e2e": {"value": tokens / (ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": 2 * Bsz * T * 8,
-                    "d2h_bytes_per_step": 4},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                         "frac": achieved / peaks["bf16_tflops"], "traffic": None, "peak_source": peaks["source"],
-                         "counted": "6 * linear FLOPs per token (fwd + grad_x + grad_W); generation, attention "
-                                    "and the LM head not counted"},
-            "clocks": clk.summary(),
-        }
         print(json.dumps(line), flush=True)
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
 
 
-def run_gpt2(args) -> None:
+def measure_gpt2(dev, steps: int, warmup: int, latent_mode: str = "ratio") -> dict:
     """C4: GPT-2-small-shaped decoder inference (12 layers, d=768, 12 heads, seq 1024,
     batch 8, vocab 50257 padded to 50304) with every qkv / attn-proj / fc / fc-proj
     weight regenerated from its own BlockFHT latent on each forward (bf16, layers=3,
@@ -948,15 +980,13 @@ def run_gpt2(args) -> None:
     import torch
     import torch.nn.functional as F
 
-    from latent_weight_lab import BlockFHTLinear, _native
+    from latent_weight_lab import BlockFHTLinear
 
-    _native.load()
-    dev = torch.device("cuda", 0)
     torch.manual_seed(0)
     n_layer, d, n_head, T, Bsz, vocab = 12, 768, 12, 1024, 8, 50304
 
     def lin(i, o, seed):
-        lat = max(1, round(i * o * (0.01 if args.latent_mode == "ratio" else 1 / 16)))
+        lat = max(1, round(i * o * (0.01 if latent_mode == "ratio" else 1 / 16)))
         return BlockFHTLinear(i, o, bias=True, latent_dim=lat, layers=3, seed=seed).to(dev, torch.bfloat16)
 
     class Block(torch.nn.Module):
@@ -998,7 +1028,7 @@ def run_gpt2(args) -> None:
 
     with torch.no_grad():
         idx = idx_host.to(dev)
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             forward(idx)
         torch.cuda.synchronize()
         # the whole forward (generation + dense compute) replays as one CUDA graph
@@ -1012,33 +1042,45 @@ def run_gpt2(args) -> None:
             logits = forward(idx)
             last_dev = logits[:, -1, :].argmax(-1)
         last = torch.empty_like(last_dev, device="cpu").pin_memory()
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             graph.replay()
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with ClockSampler(0) as clk:
+        with ClockSampler(dev.index) as clk:
             a.record()
-            for _ in range(args.steps):
+            for _ in range(steps):
                 idx.copy_(idx_host, non_blocking=True)  # token ids from pinned host memory
                 graph.replay()
                 last.copy_(last_dev, non_blocking=True)  # next-token ids read back every step
             b.record()
             torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / args.steps
+    ms = a.elapsed_time(b) / steps
     lin_flops = 2 * Bsz * T * n_layer * (d * 3 * d + d * d + 2 * d * 4 * d)
     line = {
         "metric": "GPT-2-small inference logits tokens/s, BlockFHT-generated linears (C4)",
-        "value": Bsz * T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "value": Bsz * T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": steps,
+        "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic token ids (uniform, seed 0), random-init weights",
-        "config": {"workload": f"C4 GPT-2-small inference, latent mode {args.latent_mode}", "batch": Bsz,
+        "config": {"workload": f"C4 GPT-2-small inference, latent mode {latent_mode}", "batch": Bsz,
                    "seq_len": T, "layers": n_layer, "d_model": d, "vocab_padded": vocab,
                    "e2e": "token ids copied from pinned host memory and next-token argmax read back each step",
                    "execution": "one CUDA graph per forward (grouped weight generation + dense compute)"},
         "linear_tflops": lin_flops / (ms * 1e-3) / 1e12,
         "clocks": clk.summary(),
     }
-    print(json.dumps(line), flush=True)
+    del graph, blocks, model, wte
+    torch.cuda.empty_cache()
+    return line
+
+
+def run_gpt2(args) -> None:
+    """C4 on its own line (see measure_gpt2), one GPU."""
+    import torch
+
+    from latent_weight_lab import _native
+
+    _native.load()
+    print(json.dumps(measure_gpt2(torch.device("cuda", 0), args.steps, args.warmup, args.latent_mode)), flush=True)
 
 
 def run_tp(args) -> None:
@@ -1173,6 +1215,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-mlp", action="store_true", help="skip the C3 MLP-pair keys of the default line")
+    ap.add_argument("--no-gpt", action="store_true", help="skip the C4 / C5 keys of the default line")
     ap.add_argument("--log-coords", type=int, default=28,
                     help="default workload: log2 of the generated coordinates per GPU (28 = the benchmark; "
                          "smaller values give the reduced cases that ncu captures run on)")

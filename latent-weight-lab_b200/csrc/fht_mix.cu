@@ -3,7 +3,8 @@
 // Reference: examples/nanogpt/model.py:182-218 (normalized_fht_last_dim + FixedFHTMix.forward).
 // The map is symmetric, so the same kernel computes the gradient.
 //
-// HBM-bound: one read and one write per element.  E = P / 32 values per lane
+// This kernel serves P <= 1024; larger P run on the tile kernel of
+// fht32_mix.cu.  HBM-bound: one read and one write per element.  E = P / 32 values per lane
 // (E <= 32, fp32 registers) in chunks of up to 16 bytes: lane l owns chunks
 // l, l + 32, ... of the row's 1024-element slice of its warp, so every warp
 // access is contiguous (P / 1024 warps per row when P > 1024).  Butterflies
@@ -232,8 +233,14 @@ int launch_t(const void* x, void* y, const float* signs, int64_t rows, int F, in
 
 }  // namespace mix
 
+bool fht_mix32_supported(int logP);
+int fht_mix32_launch(int dtype, const void* x, void* y, const float* signs, int64_t rows, int F, int logP,
+                     cudaStream_t st);
+
 int fht_mix_launch(int dtype, const void* x, void* y, const float* signs, int64_t rows, int F, int logP,
                    cudaStream_t st) {
+  // P = 2048 .. 8192: the register-resident tile kernel (fht32_mix.cu)
+  if (fht_mix32_supported(logP)) return fht_mix32_launch(dtype, x, y, signs, rows, F, logP, st);
   if (dtype == 0) return mix::launch_t<float>(x, y, signs, rows, F, logP, st);
   if (dtype == 1) return mix::launch_t<__nv_bfloat16>(x, y, signs, rows, F, logP, st);
   return mix::launch_t<__half>(x, y, signs, rows, F, logP, st);

@@ -41,7 +41,9 @@ __global__ void __launch_bounds__(kThreads, 1) fht15_forward_kernel(const __grid
   uint16_t* zbuf = reinterpret_cast<uint16_t*>(smem);   // scaled fp16 latent copy (64 KB)
   uint16_t* xbuf = zbuf + kB;                           // exchange buffers (64 KB each)
   uint16_t* ybuf = xbuf + kB;
-  uint32_t* sw = reinterpret_cast<uint32_t*>(ybuf + kB);  // sign words [layers+1][kWordsPad]
+  // two sign tables [layers+1][kWordsPad]: the next tile's words are written
+  // during this tile, before its staging barrier, so a tile starts without one
+  uint32_t* sw_buf = reinterpret_cast<uint32_t*>(ybuf + kB);
   __shared__ float red[kThreads / 32];
   __shared__ int k0_shared;
 
@@ -62,8 +64,29 @@ __global__ void __launch_bounds__(kThreads, 1) fht15_forward_kernel(const __grid
   const uint32_t yb = (uint32_t)__cvta_generic_to_shared(ybuf);
   Frags f;
   int cur = -1, k0 = 0;
+  // sign words of work item `it` (any descriptor) into dst
+  auto gen_signs = [&](int64_t it, uint32_t* dst) {
+    int dd = 0;
+    while (dd + 1 < G.count && G.d[dd + 1].tile_prefix <= it) ++dd;
+    const FwdDesc& E = G.d[dd];
+    const int en = E.n, eBm = (1 << en) - 1;
+    const int64_t eblk = E.first_tile + (it - E.tile_prefix);
+    for (int i = tid; i < (E.layers + 1) * kWords; i += kThreads) {
+      int l = i / kWords, wd = i - l * kWords;
+      const int p = 32 * wd;
+      dst[l * kWordsPad + spad(wd)] =
+          sign_word(block_layer_key(E.seed32, (eblk << (kLog - en)) + (p >> en), l), (p & eBm) >> 5);
+    }
+  };
+  if (blockIdx.x < G.total_tiles) gen_signs(blockIdx.x, sw_buf);
+  __syncthreads();
+  int parity = 0;
 
   for (int64_t item = blockIdx.x; item < G.total_tiles; item += gridDim.x) {
+    uint32_t* sw = sw_buf + (parity ? 4 * kWordsPad : 0);
+    uint32_t* sw_next = sw_buf + (parity ? 0 : 4 * kWordsPad);
+    parity ^= 1;
+    const bool has_next = item + gridDim.x < G.total_tiles;
     int di = 0;
     while (di + 1 < G.count && G.d[di + 1].tile_prefix <= item) ++di;
     const FwdDesc& D = G.d[di];
@@ -132,22 +155,20 @@ __global__ void __launch_bounds__(kThreads, 1) fht15_forward_kernel(const __grid
     T* out = reinterpret_cast<T*>(D.out);
     const bool vec_ok = ((D.start & 7) == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
     const int64_t blk = D.first_tile + (item - D.tile_prefix);
-    for (int i = tid; i < (layers + 1) * kWords; i += kThreads) {
-      int l = i / kWords, wd = i - l * kWords;
-      const int p = 32 * wd;
-      sw[l * kWordsPad + spad(wd)] =
-          sign_word(block_layer_key(D.seed32, (blk << (kLog - n)) + (p >> n), l), (p & Bm) >> 5);
-    }
-    __syncthreads();
+    // this tile's sign words were written before the previous tile's staging
+    // barrier (or before the loop); the next tile's are written below, before
+    // run_final's staging barrier, into the other table
     if (layers == 1) {
       run_first_tmem<1>(f, tz, xb, sw, w, lane, g, t);
       __syncthreads();
+      if (has_next) gen_signs(item + gridDim.x, sw_next);
       run_final<T>(f, xb, yb, ybuf, sw + 1 * kWordsPad, out_scale, out, blk, D.start, D.stop, vec_ok, w, lane, g, t);
     } else if (layers == 2) {
       run_first_tmem<0>(f, tz, yb, sw, w, lane, g, t);
       __syncthreads();
       run<1, true, false>(f, yb, xb, nullptr, sw + 1 * kWordsPad, w, lane, g, t);
       __syncthreads();
+      if (has_next) gen_signs(item + gridDim.x, sw_next);
       run_final<T>(f, xb, yb, ybuf, sw + 2 * kWordsPad, out_scale, out, blk, D.start, D.stop, vec_ok, w, lane, g, t);
     } else {
       run_first_tmem<1>(f, tz, xb, sw, w, lane, g, t);
@@ -156,6 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1) fht15_forward_kernel(const __grid
       __syncthreads();
       run<1, true, false>(f, yb, xb, nullptr, sw + 2 * kWordsPad, w, lane, g, t);
       __syncthreads();
+      if (has_next) gen_signs(item + gridDim.x, sw_next);
       run_final<T>(f, xb, yb, ybuf, sw + 3 * kWordsPad, out_scale, out, blk, D.start, D.stop, vec_ok, w, lane, g, t);
     }
   }
@@ -165,7 +187,8 @@ __global__ void __launch_bounds__(kThreads, 1) fht15_forward_kernel(const __grid
   if (w == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;\n" ::"r"(tmem_base_shared));
 }
 
-constexpr size_t kSmem = 3 * kB * 2 + 4 * kWordsPad * 4;
+constexpr size_t kSmem = 3 * kB * 2 + 2 * 4 * kWordsPad * 4;  // two sign tables
+static_assert(kSmem <= 232448, "shared memory per CTA");
 
 template <typename T>
 int launch_forward_t(const FwdGroup& G, cudaStream_t st) {
@@ -442,7 +465,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint16_t* xbuf = reinterpret_cast<uint16_t*>(smem);
   uint16_t* ybuf = xbuf + kB;
   uint16_t* stage = ybuf + kB;  // raw gradient of the next block (bulk copy target)
-  uint32_t* sw = reinterpret_cast<uint32_t*>(stage + kB);
+  // two sign tables: block i writes one while slower warps may still read
+  // block i-1's in its last run, so the loop needs no barrier at its top
+  uint32_t* sw_buf = reinterpret_cast<uint32_t*>(stage + kB);
   __shared__ float red[kThreads / 32];
   __shared__ __align__(8) uint64_t mbar;
   __shared__ int abort_flag;
@@ -508,10 +533,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     inflight = true;
   }
 
+  int parity = 0;
   for (int64_t bi = blockIdx.x; bi < nblocks; bi += gridDim.x) {
     const int64_t blk = first_block + bi;
     const int64_t bbase = blk * kB;
-    __syncthreads();
+    uint32_t* sw = sw_buf + (parity ? 4 * kWordsPad : 0);
+    parity ^= 1;
+    // 2 layers land the gradient in xbuf, which the previous block's last run
+    // still reads; 1 and 3 layers land it in ybuf, free since that run began
+    if (layers == 2) __syncthreads();
     for (int i = tid; i < (layers + 1) * kWords; i += kThreads) {
       int l = i / kWords, wd = i - l * kWords;
       const int p = 32 * wd;
@@ -680,6 +710,8 @@ __global__ void fht15_reduce_kernel(const float* __restrict__ partial, int rows,
 }
 
 constexpr size_t kSmemBwd = 3 * kB * 2 + 4 * kWordsPad * 4;
+constexpr size_t kSmemBwd1 = 3 * kB * 2 + 2 * 4 * kWordsPad * 4;  // single backward: two sign tables
+static_assert(kSmemBwd1 <= 232448, "shared memory per CTA");
 constexpr size_t kBwdHeader = 256;  // workspace: [error word | pad] then the partial rows
 
 
@@ -691,11 +723,11 @@ int launch_backward_t(const void* grad, int64_t L, int layers, int n, uint32_t s
   int* err = reinterpret_cast<int*>(workspace);
   float* partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kBwdHeader);
   if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess) return -1;
-  if (!set_max_smem((const void*)fht15_backward_kernel<T>, (int)kSmemBwd)) return -1;
+  if (!set_max_smem((const void*)fht15_backward_kernel<T>, (int)kSmemBwd1)) return -1;
   int sms = sm_count();
   int grid = (int)(nblocks < sms ? nblocks : sms);
   const float corr = (float)std::pow(layer_correction(n), layers);
-  fht15_backward_kernel<T><<<grid, kThreads, kSmemBwd, st>>>(reinterpret_cast<const T*>(grad), L, layers, n, seed32,
+  fht15_backward_kernel<T><<<grid, kThreads, kSmemBwd1, st>>>(reinterpret_cast<const T*>(grad), L, layers, n, seed32,
                                                              corr,
                                                              first_block, nblocks, start, stop, partial, err,
                                                              test_stall);

@@ -66,7 +66,8 @@ def test_gpu_forward_backward_match_reference(native_lib, dtype, tol):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("features", [1, 5, 31, 32, 33, 100, 1024, 1025, 2048, 4095, 8192])
+@pytest.mark.parametrize("features", [1, 5, 31, 32, 33, 100, 1024, 1025, 1600, 2048, 2049, 3072, 4095, 6400, 8191,
+                                      8192])
 def test_gpu_shapes_against_oracle(native_lib, features):
     """Every register/shuffle/exchange regime, ragged widths, leading dims, many rows."""
     from latent_weight_lab.fht_mix import FixedFHTMix
@@ -78,6 +79,22 @@ def test_gpu_shapes_against_oracle(native_lib, features):
     ref = orc.fixed_fht_mix(x.cpu().numpy(), mix.signs.cpu().numpy())
     assert rel_l2(y.cpu().numpy(), ref) < 1e-5
     assert torch.allclose(mix(mix(x)), x, atol=1e-4) or features & (features - 1)  # involution when P == F
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("features", [1600, 3072, 6400])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_gpu_wide_rows_half(native_lib, features, dtype):
+    """16-bit rows at the GPT widths (the tile kernel for P >= 2048): 1e-2 against fp32 math on the rounded input."""
+    from latent_weight_lab.fht_mix import FixedFHTMix
+
+    torch.manual_seed(features + 1)
+    mix = FixedFHTMix(features, 11).cuda()
+    x = torch.randn(257, features, device="cuda").to(dtype)
+    y = mix(x)
+    ref = orc.fixed_fht_mix(x.float().cpu().numpy(), mix.signs.cpu().numpy())
+    assert y.dtype == dtype
+    assert rel_l2(y.float().cpu().numpy(), ref) < 1e-2
 
 
 @pytest.mark.gpu

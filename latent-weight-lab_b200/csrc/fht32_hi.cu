@@ -1,0 +1,153 @@
+// fht32_hi.cu -- the high-bit pass of the two-pass layout for 16-bit blocks
+// of 2^18 .. 2^21 on the register-resident scheme of fht32.cuh.
+//
+// The two-pass layout (fht_engine.cu) transforms a block of B = 2^n as
+// H_B = H_hi (x) H_32768: the tensor-core low pass (fht_lo_kernel) takes the 15
+// low position bits, and this pass the h = n - 15 high bits, which are
+// strided by 2^15 in the block.  The generic tile engine ran the high pass
+// with eight 4-byte loads in flight per thread, latency-bound at about
+// 1.8 TB/s.  Here a CTA of 128 threads owns a tile of 2^13 elements: the
+// 2^h high positions (tile bits 13-h .. 12) times 2^(13-h) consecutive low
+// positions (tile bits 0 .. 12-h).  In set C of fht32.cuh (registers = tile
+// bits 7..12, lanes = bits 0..4) the high bits are register bits, so the whole
+// pass -- the optional pre-sign, the runs of butterflies and their signs --
+// is one residency with no exchange, and every warp load and store covers 32
+// consecutive positions.  Each thread holds 64 values in flight.
+//
+// Sources: the latent, the gradient slice or the fp32 workspace; sink: the
+// fp32 workspace (16-bit plans always end with a low pass).  Signs and the
+// 1/sqrt(B) of each post-sign follow the plan's slots exactly as the tile
+// engine applies them.
+#include <algorithm>
+
+#include "fht32.cuh"
+
+namespace lwl {
+namespace f32k {
+
+template <typename T, int H, int SRC>
+__global__ void __launch_bounds__(Tile<13>::kThreads, Tile<13>::kMinBlocks)
+    fht_hi_kernel(const __grid_constant__ TileParams p) {
+  using Tl = Tile<13>;
+  constexpr int LOW = 13 - H;                   // consecutive low positions per tile
+  constexpr int CHUNKS = 1 << (15 - LOW);       // tiles per block
+  constexpr int HIMASK = ((1 << H) - 1) << LOW;  // tile bits of the high positions
+  __shared__ uint32_t sw[kMaxSlots * Tl::kWords];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int base = base_of<13, SC>(lane, warp);
+  const int nsw = p.nslots;
+  float v[kRegs];
+  for (int64_t tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x) {
+    const int64_t b = p.first_block + tile / CHUNKS;  // block
+    const int j = (int)(tile % CHUNKS);              // low chunk of the block
+    const int64_t pos0 = (int64_t)j << LOW;          // position of tile element 0
+    __syncthreads();  // the previous tile is done with the sign table
+    // sign words of the tile: entry c covers high value c >> (8 - H), low word c & (2^(8-H) - 1)
+    for (int i = tid; i < nsw * Tl::kWords; i += Tl::kThreads) {
+      const int s = i / Tl::kWords, c = i - s * Tl::kWords;
+      const int64_t word = ((int64_t)(c >> (8 - H)) << 10) + (pos0 >> 5) + (c & ((1 << (8 - H)) - 1));
+      sw[i] = sign_word(block_layer_key(p.seed32, b, p.slot_layer[s]), word);
+    }
+    __syncthreads();
+    // element t = base | spread(r): position pos0 + (t & low mask) + (t >> LOW) << 15
+    const int lo_b = base & ((1 << LOW) - 1);
+    const int64_t rowoff = (b - p.first_block) * p.B;
+    if (SRC == SRC_WS) {
+      const float* s = reinterpret_cast<const float*>(p.src) + rowoff + pos0 + lo_b;
+#pragma unroll
+      for (int r = 0; r < kRegs; ++r) {
+        const int t = spread<13, SC>(r);
+        v[r] = s[(t & ((1 << LOW) - 1)) + ((int64_t)(t >> LOW) << 15)];
+      }
+    } else if (SRC == SRC_LATENT) {
+      const T* s = reinterpret_cast<const T*>(p.src);
+#pragma unroll
+      for (int r = 0; r < kRegs; ++r) {
+        const int t = spread<13, SC>(r);
+        const int64_t pos = pos0 + lo_b + (t & ((1 << LOW) - 1)) + ((int64_t)(t >> LOW) << 15);
+        v[r] = pos < p.L ? Cvt<T>::to_f(s[pos]) : 0.0f;
+      }
+    } else {
+      const T* s = reinterpret_cast<const T*>(p.src);
+      const int64_t g0 = b * p.B + pos0 + lo_b;
+#pragma unroll
+      for (int r = 0; r < kRegs; ++r) {
+        const int t = spread<13, SC>(r);
+        const int64_t g = g0 + (t & ((1 << LOW) - 1)) + ((int64_t)(t >> LOW) << 15);
+        v[r] = (g >= p.start && g < p.stop) ? Cvt<T>::to_f(s[g - p.start]) : 0.0f;
+      }
+    }
+    if (p.pre_slot >= 0) apply_sign<13, SC>(v, sw + p.pre_slot * Tl::kWords, base);
+    for (int ri = 0; ri < p.nruns; ++ri) {
+      const RunDesc& rd = p.runs[ri];
+      // the run's group: transform bits glo..glo+gr-1 of the engine's tile, whose
+      // column bits (cb = 3) precede them, i.e. high bits glo-3 .. glo-3+gr-1
+      const int mask = (((1 << rd.gr) - 1) << (rd.glo - 3 + LOW)) & HIMASK;
+      for (int f = 0; f < rd.nfht; ++f) {
+        xform<13, SC>(v, mask, 13);
+        const int sl = rd.slot[f];
+        if (sl >= 0) {
+          apply_sign<13, SC>(v, sw + sl * Tl::kWords, base);
+#pragma unroll
+          for (int r = 0; r < kRegs; ++r) v[r] *= p.scale;
+        }
+      }
+    }
+    float* d = reinterpret_cast<float*>(p.dst) + rowoff + pos0 + lo_b;
+#pragma unroll
+    for (int r = 0; r < kRegs; ++r) {
+      const int t = spread<13, SC>(r);
+      d[(t & ((1 << LOW) - 1)) + ((int64_t)(t >> LOW) << 15)] = v[r];
+    }
+  }
+}
+
+template <typename T, int SRC>
+const void* hi_kernel_h(int h) {
+  switch (h) {
+    case 3: return (const void*)fht_hi_kernel<T, 3, SRC>;
+    case 4: return (const void*)fht_hi_kernel<T, 4, SRC>;
+    case 5: return (const void*)fht_hi_kernel<T, 5, SRC>;
+    default: return (const void*)fht_hi_kernel<T, 6, SRC>;
+  }
+}
+
+template <typename T>
+const void* hi_kernel(int src, int h) {
+  if (src == SRC_WS) return hi_kernel_h<T, SRC_WS>(h);
+  if (src == SRC_LATENT) return hi_kernel_h<T, SRC_LATENT>(h);
+  return hi_kernel_h<T, SRC_SLICE>(h);
+}
+
+}  // namespace f32k
+
+// A planned tile-engine launch this pass can take: a 16-bit two-pass plan's
+// high-bit launch (column chunks of 8 below 15 low bits) of 3..6 high bits
+// into the fp32 workspace.
+bool fht_hi_eligible(int dtype, const TileParams& p) {
+  if (dtype != LWL_BF16 && dtype != LWL_F16) return false;
+  if (p.lo || p.tlo != 15 || p.cb != 3 || p.dst_kind != DST_WS) return false;
+  const int h = p.n - 15;
+  if (h < 3 || h > 6 || p.r != h || p.nslots > f32k::kMaxSlots) return false;
+  for (int i = 0; i < p.nruns; ++i)
+    if (p.runs[i].glo < 3 || p.runs[i].glo + p.runs[i].gr > 3 + h) return false;
+  return true;
+}
+
+int fht_hi_launch(int dtype, const TileParams& p_in, cudaStream_t st) {
+  using namespace f32k;
+  TileParams p = p_in;
+  const int h = p.n - 15;
+  p.ntiles = p.nblocks << (h + 2);  // 2^(15 - (13 - h)) tiles per block
+  const void* k = dtype == LWL_BF16 ? hi_kernel<__nv_bfloat16>(p.src_kind, h) : hi_kernel<__half>(p.src_kind, h);
+  int per_sm = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, Tile<13>::kThreads, 0) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  int dev = 0, nsm = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = (int)std::min<int64_t>(p.ntiles, (int64_t)nsm * per_sm);
+  void* args[] = {&p};
+  return cudaLaunchKernel(k, dim3(grid), dim3(Tile<13>::kThreads), args, 0, st) == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace lwl

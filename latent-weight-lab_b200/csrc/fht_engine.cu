@@ -300,6 +300,13 @@ int run_plan_t(const FhtArgs& a, FhtPlan& plan, cudaStream_t st) {
       }
       continue;
     }
+    if (fht_hi_eligible(a.dtype, p)) {
+      if (fht_hi_launch(a.dtype, p, st) != 0) {
+        set_error("high-bit pass launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return LWL_ERR_CUDA;
+      }
+      continue;
+    }
     tile_kernel_for<T>(p.src_kind, p.dst_kind)<<<l.grid, l.threads, l.smem, st>>>(p);
     LWL_CUDA_TRY(cudaGetLastError());
   }

@@ -50,6 +50,10 @@ int run_fht(const FhtArgs& a, FhtPlan& plan, cudaStream_t st);
 bool fht32_supported(int dtype, int64_t latent_size, bool backward, unsigned flags);
 size_t fht32_workspace_bytes(const FhtArgs& a);
 int fht32_launches(const FhtArgs& a);  // kernels one call enqueues
+
+// High-bit pass of 16-bit two-pass plans with 3..6 high bits (fht32_hi.cu).
+bool fht_hi_eligible(int dtype, const TileParams& p);
+int fht_hi_launch(int dtype, const TileParams& p, cudaStream_t st);
 int fht32_run(const FhtArgs& a, cudaStream_t st);
 
 }  // namespace lwl

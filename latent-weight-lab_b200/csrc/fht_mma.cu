@@ -1390,14 +1390,16 @@ __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_consta
       int sl = i / kWords, wd = i - sl * kWords;
       sw[sl * kWordsPad + spad(wd)] = sign_word(block_layer_key(p.seed32, b, p.slot_layer[sl]), j * kWords + wd);
     }
-    // tile's largest magnitude (first read), then scaled fp16 landing in the first run's layout (second read, from L2)
-    float mx = 0.0f;
-    for (int c = tid; c < kB / 8; c += kThreads) {
-      float v[8];
-      lo_load8<T>(p, b, tbase + 8 * c, v);
+    // the tile's 8 chunks of 8 per thread, all loads in flight at once, and
+    // their largest magnitude; the values stay in registers for the landing
+    float v[8][8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(v[e]));
-    }
+    for (int i = 0; i < 8; ++i) lo_load8<T>(p, b, tbase + 8 * (tid + kThreads * i), v[i]);
+    float mx = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(v[i][e]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if (lane == 0) red[w] = mx;
@@ -1412,12 +1414,12 @@ __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_consta
     const int k0 = k0_shared;
     const float in_scale = ldexpf(1.0f, -k0);
     uint16_t* land = nseg == 1 ? ybuf : xbuf;
-    for (int c = tid; c < kB / 8; c += kThreads) {
-      float v[8];
-      lo_load8<T>(p, b, tbase + 8 * c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int c = tid + kThreads * i;
       uint32_t hv[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) hv[e] = pack_h2(v[2 * e] * in_scale, v[2 * e + 1] * in_scale);
+      for (int e = 0; e < 4; ++e) hv[e] = pack_h2(v[i][2 * e] * in_scale, v[i][2 * e + 1] * in_scale);
       if (nseg == 1) {
         *reinterpret_cast<uint4*>(land + lay_ab(8 * c)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
       } else {
@@ -1479,8 +1481,19 @@ __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_consta
         }
       }
       __syncthreads();
+      // lay_f32 XORs each aligned group of 4 positions with one mask, so a group
+      // is one aligned 16-byte shared load, permuted back in registers
       float* dst = reinterpret_cast<float*>(p.dst) + (b - p.first_block) * p.B + tbase;
-      for (int q = tid; q < kB; q += kThreads) dst[q] = fstage[lay_f32(q)];
+#pragma unroll 4
+      for (int q = 4 * tid; q < kB; q += 4 * kThreads) {
+        const int m = lay_f32(q) ^ q;  // the group's XOR mask
+        const float4 a = *reinterpret_cast<const float4*>(fstage + (lay_f32(q) & ~3));
+        // element i of the group sits in word i ^ m of the loaded 16 bytes
+        const bool s0 = m & 1, s1 = m & 2;
+        const float lo0 = s0 ? a.y : a.x, lo1 = s0 ? a.x : a.y, hi0 = s0 ? a.w : a.z, hi1 = s0 ? a.z : a.w;
+        *reinterpret_cast<float4*>(dst + q) =
+            s1 ? make_float4(hi0, hi1, lo0, lo1) : make_float4(lo0, lo1, hi0, hi1);
+      }
     }
   }
 }

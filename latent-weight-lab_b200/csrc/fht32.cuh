@@ -290,20 +290,36 @@ __device__ __forceinline__ void store_out(const float (&v)[kRegs], const Params&
 }
 
 // Backward: the tile's per-block results (set B or C) summed over its blocks
-// into this CTA's partial row.  Thread i owns positions i, i + threads, ...
+// into this CTA's partial row.  Register bits that select blocks (tile bits at
+// or above n) are summed in registers first; the rest of the block bits are
+// summed through shared memory.  Thread i owns positions i, i + threads, ...
 // for the whole kernel, so each address sees its additions in tile order.
 template <int TB, int SET>
-__device__ __forceinline__ void accumulate(const float (&v)[kRegs], float* buf, const Params& p, int base, int tid) {
+__device__ __forceinline__ void accumulate(float (&v)[kRegs], float* buf, const Params& p, int base, int tid, int n) {
+  int regmask = 0;  // tile bits of the register bits summed here
+#pragma unroll
+  for (int j = 0; j < 6; ++j) {
+    const int tb = reg_bit<TB>(SET, j);
+    if (tb >= n) {
+      regmask |= 1 << tb;
+      const int h = 1 << j;
+#pragma unroll
+      for (int r = 0; r < kRegs; ++r)
+        if (!(r & h)) v[r] += v[r | h];
+    }
+  }
   __syncthreads();
   float* wb = buf + pad(base);
 #pragma unroll
-  for (int r = 0; r < kRegs; ++r) wb[pad(spread<TB, SET>(r))] = v[r];
+  for (int r = 0; r < kRegs; ++r)
+    if (!(spread<TB, SET>(r) & regmask)) wb[pad(spread<TB, SET>(r))] = v[r];
   __syncthreads();
   float* row = reinterpret_cast<float*>(p.dst) + (int64_t)(p.row0 + blockIdx.x) * p.L;
-  const int nb = 1 << (TB - p.n);
+  const int nb = 1 << (TB - n);
   for (int q = tid; q < p.L; q += Tile<TB>::kThreads) {
     float s = 0.0f;
-    for (int k = 0; k < nb; ++k) s += buf[pad((k << p.n) | q)];
+    for (int k = 0; k < nb; ++k)
+      if (!((k << n) & regmask)) s += buf[pad((k << n) | q)];
     atomicAdd(row + q, s * p.scale);  // one thread per address: program order, deterministic
   }
 }
@@ -358,7 +374,7 @@ __global__ void __launch_bounds__(Tile<TB>::kThreads, Tile<TB>::kMinBlocks)
         apply_sign<TB, SA>(v, s3, bA);
       }
       exchange<TB, SA, SB>(v, buf, lane, warp);
-      if (BWD) accumulate<TB, SB>(v, buf, p, bB, tid);
+      if (BWD) accumulate<TB, SB>(v, buf, p, bB, tid, n);
       else store_out<T, TB, SB, FULL>(v, p, tile, bB);
     } else if constexpr (KCLS == 2) {
       if (LAYERS == 2) {
@@ -390,7 +406,7 @@ __global__ void __launch_bounds__(Tile<TB>::kThreads, Tile<TB>::kMinBlocks)
           apply_sign<TB, SB>(v, s3, bB);
         }
       }
-      if (BWD) accumulate<TB, SB>(v, buf, p, bB, tid);
+      if (BWD) accumulate<TB, SB>(v, buf, p, bB, tid, n);
       else store_out<T, TB, SB, FULL>(v, p, tile, bB);
     } else {
       if (LAYERS == 2) {
@@ -432,7 +448,7 @@ __global__ void __launch_bounds__(Tile<TB>::kThreads, Tile<TB>::kMinBlocks)
           apply_sign<TB, SC>(v, s3, bC);
         }
       }
-      if (BWD) accumulate<TB, SC>(v, buf, p, bC, tid);
+      if (BWD) accumulate<TB, SC>(v, buf, p, bC, tid, n);
       else store_out<T, TB, SC, FULL>(v, p, tile, bC);
     }
   }

@@ -14,9 +14,10 @@
 // is one residency with no exchange, and every warp load and store covers 32
 // consecutive positions.  Each thread holds 64 values in flight.
 //
-// Sources: the latent or the fp32 workspace (the gradient-slice variant is
-// compiled but not dispatched); sink: the fp32 workspace (16-bit plans always
-// end with a low pass).  Signs and the
+// Sources: the latent, the gradient slice or the fp32 workspace; sink: the
+// fp32 workspace (16-bit plans always end with a low pass).  Blocks wholly
+// inside the gradient slice load without bounds tests: with a 64-bit range
+// test on every element this launch ran at half the speed of the tile engine.  Signs and the
 // 1/sqrt(B) of each post-sign follow the plan's slots exactly as the tile
 // engine applies them.
 #include <algorithm>
@@ -67,6 +68,14 @@ __global__ void __launch_bounds__(Tile<13>::kThreads, Tile<13>::kMinBlocks)
         const int t = spread<13, SC>(r);
         const int64_t pos = pos0 + lo_b + (t & ((1 << LOW) - 1)) + ((int64_t)(t >> LOW) << 15);
         v[r] = pos < p.L ? Cvt<T>::to_f(s[pos]) : 0.0f;
+      }
+    } else if (b * p.B >= p.start && (b + 1) * p.B <= p.stop) {
+      // the whole block lies inside the slice: unpredicated loads
+      const T* s = reinterpret_cast<const T*>(p.src) + (b * p.B - p.start) + pos0 + lo_b;
+#pragma unroll
+      for (int r = 0; r < kRegs; ++r) {
+        const int t = spread<13, SC>(r);
+        v[r] = Cvt<T>::to_f(s[(t & ((1 << LOW) - 1)) + ((int64_t)(t >> LOW) << 15)]);
       }
     } else {
       const T* s = reinterpret_cast<const T*>(p.src);
@@ -128,10 +137,6 @@ const void* hi_kernel(int src, int h) {
 bool fht_hi_eligible(int dtype, const TileParams& p) {
   if (dtype != LWL_BF16 && dtype != LWL_F16) return false;
   if (p.lo || p.tlo != 15 || p.cb != 3 || p.dst_kind != DST_WS) return false;
-  // a gradient-slice source (the backward's first launch) measured slower here
-  // than on the tile engine's vector path (1.6 vs 0.8 ms per 2^28 coordinates
-  // at 2^18), so that launch stays there
-  if (p.src_kind == SRC_SLICE) return false;
   const int h = p.n - 15;
   if (h < 3 || h > 6 || p.r != h || p.nslots > f32k::kMaxSlots) return false;
   for (int i = 0; i < p.nruns; ++i)

@@ -1,5 +1,5 @@
 // fht32_hi.cu -- the high-bit pass of the two-pass layout for 16-bit blocks
-// of 2^18 .. 2^21 on the register-resident scheme of fht32.cuh.
+// of 2^18 .. 2^23 on the register-resident scheme of fht32.cuh.
 //
 // The two-pass layout (fht_engine.cu) transforms a block of B = 2^n as
 // H_B = H_hi (x) H_32768: the tensor-core low pass (fht_lo_kernel) takes the 15
@@ -112,13 +112,120 @@ __global__ void __launch_bounds__(Tile<13>::kThreads, Tile<13>::kMinBlocks)
   }
 }
 
+// 7 or 8 high bits (blocks of 2^22 / 2^23): a tile of 2^(7+h) elements = the
+// 2^h high positions x 128 consecutive low positions (tile bits 0..6), so that
+// every run's group of high bits lies in the registers of set B (tile bits
+// 6..11) or set C (the top six); the runs execute in plan order and the tile
+// moves between B and C through shared memory when the next group needs it.
+template <typename T, int TB, int SET, int SRC>
+__device__ __forceinline__ void hi2_load(float (&v)[kRegs], const TileParams& p, int64_t b, int64_t pos0, int base) {
+  constexpr int LOW = 7;
+  auto off = [](int t) { return (int64_t)(t & ((1 << LOW) - 1)) + ((int64_t)(t >> LOW) << 15); };
+  if (SRC == SRC_WS) {
+    const float* s = reinterpret_cast<const float*>(p.src) + (b - p.first_block) * p.B + pos0 + off(base);
+#pragma unroll
+    for (int r = 0; r < kRegs; ++r) v[r] = s[off(spread<TB, SET>(r))];
+  } else if (SRC == SRC_LATENT) {
+    const T* s = reinterpret_cast<const T*>(p.src);
+#pragma unroll
+    for (int r = 0; r < kRegs; ++r) {
+      const int64_t pos = pos0 + off(base) + off(spread<TB, SET>(r));
+      v[r] = pos < p.L ? Cvt<T>::to_f(s[pos]) : 0.0f;
+    }
+  } else if (b * p.B >= p.start && (b + 1) * p.B <= p.stop) {
+    const T* s = reinterpret_cast<const T*>(p.src) + (b * p.B - p.start) + pos0 + off(base);
+#pragma unroll
+    for (int r = 0; r < kRegs; ++r) v[r] = Cvt<T>::to_f(s[off(spread<TB, SET>(r))]);
+  } else {
+    const T* s = reinterpret_cast<const T*>(p.src);
+    const int64_t g0 = b * p.B + pos0 + off(base);
+#pragma unroll
+    for (int r = 0; r < kRegs; ++r) {
+      const int64_t g = g0 + off(spread<TB, SET>(r));
+      v[r] = (g >= p.start && g < p.stop) ? Cvt<T>::to_f(s[g - p.start]) : 0.0f;
+    }
+  }
+}
+
+template <int TB, int SET>
+__device__ __forceinline__ void hi2_store(const float (&v)[kRegs], const TileParams& p, int64_t b, int64_t pos0,
+                                          int base) {
+  constexpr int LOW = 7;
+  auto off = [](int t) { return (int64_t)(t & ((1 << LOW) - 1)) + ((int64_t)(t >> LOW) << 15); };
+  float* d = reinterpret_cast<float*>(p.dst) + (b - p.first_block) * p.B + pos0 + off(base);
+#pragma unroll
+  for (int r = 0; r < kRegs; ++r) d[off(spread<TB, SET>(r))] = v[r];
+}
+
+template <typename T, int H, int SRC>
+__global__ void __launch_bounds__(Tile<7 + H>::kThreads, 1) fht_hi2_kernel(const __grid_constant__ TileParams p) {
+  constexpr int TB = 7 + H;
+  using Tl = Tile<TB>;
+  constexpr int LOW = 7;
+  constexpr int CHUNKS = 1 << (15 - LOW);  // tiles per block
+  constexpr int MASKC = Tl::kC;            // tile bits of set C's registers
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* buf = reinterpret_cast<float*>(smem);
+  uint32_t* sw = reinterpret_cast<uint32_t*>(buf + Tl::kBufWords);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int bB = base_of<TB, SB>(lane, warp), bC = base_of<TB, SC>(lane, warp);
+  // tile bits of run ri's group: high bits glo-3 .. glo-3+gr-1 (column bits cb = 3 precede them)
+  auto group_mask = [&](int ri) { return ((1 << p.runs[ri].gr) - 1) << (p.runs[ri].glo - 3 + LOW); };
+  float v[kRegs];
+  for (int64_t tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x) {
+    const int64_t b = p.first_block + tile / CHUNKS;
+    const int64_t pos0 = (int64_t)(tile % CHUNKS) << LOW;
+    __syncthreads();  // the previous tile is done with the sign table and the exchange buffer
+    for (int i = tid; i < p.nslots * Tl::kWords; i += Tl::kThreads) {
+      const int s = i / Tl::kWords, c = i - s * Tl::kWords;
+      const int64_t word = ((int64_t)(c >> (LOW - 5)) << 10) + (pos0 >> 5) + (c & ((1 << (LOW - 5)) - 1));
+      sw[i] = sign_word(block_layer_key(p.seed32, b, p.slot_layer[s]), word);
+    }
+    __syncthreads();
+    bool in_c = (group_mask(0) & ~MASKC) == 0;  // start in the set of the first run's group
+    if (in_c) hi2_load<T, TB, SC, SRC>(v, p, b, pos0, bC);
+    else hi2_load<T, TB, SB, SRC>(v, p, b, pos0, bB);
+    if (p.pre_slot >= 0) {
+      if (in_c) apply_sign<TB, SC>(v, sw + p.pre_slot * Tl::kWords, bC);
+      else apply_sign<TB, SB>(v, sw + p.pre_slot * Tl::kWords, bB);
+    }
+    for (int ri = 0; ri < p.nruns; ++ri) {
+      const int mask = group_mask(ri);
+      const bool want_c = (mask & ~MASKC) == 0;
+      if (want_c != in_c) {
+        if (want_c) exchange<TB, SB, SC>(v, buf, lane, warp);
+        else exchange<TB, SC, SB>(v, buf, lane, warp);
+        in_c = want_c;
+      }
+      for (int f = 0; f < p.runs[ri].nfht; ++f) {
+        const int sl = p.runs[ri].slot[f];
+        if (in_c) {
+          xform<TB, SC>(v, mask, TB);
+          if (sl >= 0) apply_sign<TB, SC>(v, sw + sl * Tl::kWords, bC);
+        } else {
+          xform<TB, SB>(v, mask, TB);
+          if (sl >= 0) apply_sign<TB, SB>(v, sw + sl * Tl::kWords, bB);
+        }
+        if (sl >= 0) {
+#pragma unroll
+          for (int r = 0; r < kRegs; ++r) v[r] *= p.scale;
+        }
+      }
+    }
+    if (in_c) hi2_store<TB, SC>(v, p, b, pos0, bC);
+    else hi2_store<TB, SB>(v, p, b, pos0, bB);
+  }
+}
+
 template <typename T, int SRC>
 const void* hi_kernel_h(int h) {
   switch (h) {
     case 3: return (const void*)fht_hi_kernel<T, 3, SRC>;
     case 4: return (const void*)fht_hi_kernel<T, 4, SRC>;
     case 5: return (const void*)fht_hi_kernel<T, 5, SRC>;
-    default: return (const void*)fht_hi_kernel<T, 6, SRC>;
+    case 6: return (const void*)fht_hi_kernel<T, 6, SRC>;
+    case 7: return (const void*)fht_hi2_kernel<T, 7, SRC>;
+    default: return (const void*)fht_hi2_kernel<T, 8, SRC>;
   }
 }
 
@@ -138,9 +245,17 @@ bool fht_hi_eligible(int dtype, const TileParams& p) {
   if (dtype != LWL_BF16 && dtype != LWL_F16) return false;
   if (p.lo || p.tlo != 15 || p.cb != 3 || p.dst_kind != DST_WS) return false;
   const int h = p.n - 15;
-  if (h < 3 || h > 6 || p.r != h || p.nslots > f32k::kMaxSlots) return false;
-  for (int i = 0; i < p.nruns; ++i)
-    if (p.runs[i].glo < 3 || p.runs[i].glo + p.runs[i].gr > 3 + h) return false;
+  if (h < 3 || h > 8 || p.r != h || p.nslots > f32k::kMaxSlots || p.nruns < 1) return false;
+  for (int i = 0; i < p.nruns; ++i) {
+    const RunDesc& rd = p.runs[i];
+    if (rd.glo < 3 || rd.glo + rd.gr > 3 + h) return false;
+    if (h > 6) {
+      // every group must lie in the registers of set B (tile bits 6..11) or of
+      // set C (the top six tile bits 1+h .. 6+h); high bit k is tile bit 7 + k
+      const int lo = rd.glo + 4, hi = rd.glo + 4 + rd.gr;  // tile bits [lo, hi)
+      if (!(lo >= 6 && hi <= 12) && !(lo >= 1 + h && hi <= 7 + h)) return false;
+    }
+  }
   return true;
 }
 
@@ -148,16 +263,21 @@ int fht_hi_launch(int dtype, const TileParams& p_in, cudaStream_t st) {
   using namespace f32k;
   TileParams p = p_in;
   const int h = p.n - 15;
-  p.ntiles = p.nblocks << (h + 2);  // 2^(15 - (13 - h)) tiles per block
+  // tiles of 2^13 (h <= 6: 2^(2+h) per block) or 2^(7+h) (h = 7, 8: 256 per block)
+  const int tb = h <= 6 ? 13 : 7 + h;
+  p.ntiles = p.nblocks << (h <= 6 ? h + 2 : 8);
+  const int threads = 1 << (tb - 6);
+  const size_t smem = h <= 6 ? 0 : (tb == 14 ? Tile<14>::kSmem : Tile<15>::kSmem);
   const void* k = dtype == LWL_BF16 ? hi_kernel<__nv_bfloat16>(p.src_kind, h) : hi_kernel<__half>(p.src_kind, h);
+  if (smem > 0 && !set_max_smem(k, (int)smem)) return -1;
   int per_sm = 1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, Tile<13>::kThreads, 0) != cudaSuccess || per_sm < 1)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, threads, smem) != cudaSuccess || per_sm < 1)
     per_sm = 1;
   int dev = 0, nsm = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   const int grid = (int)std::min<int64_t>(p.ntiles, (int64_t)nsm * per_sm);
   void* args[] = {&p};
-  return cudaLaunchKernel(k, dim3(grid), dim3(Tile<13>::kThreads), args, 0, st) == cudaSuccess ? 0 : -1;
+  return cudaLaunchKernel(k, dim3(grid), dim3(threads), args, smem, st) == cudaSuccess ? 0 : -1;
 }
 
 }  // namespace lwl

@@ -1,5 +1,6 @@
-// fht32_hi.cu -- the high-bit pass of the two-pass layout for 16-bit blocks
-// of 2^18 .. 2^23 on the register-resident scheme of fht32.cuh.
+// fht32_hi.cu -- the high-bit pass of the two-pass layout (blocks of
+// 2^16 .. 2^23 with a 15-bit low pass) on the register-resident scheme of
+// fht32.cuh.
 //
 // The two-pass layout (fht_engine.cu) transforms a block of B = 2^n as
 // H_B = H_hi (x) H_32768: the tensor-core low pass (fht_lo_kernel) takes the 15
@@ -220,6 +221,8 @@ __global__ void __launch_bounds__(Tile<7 + H>::kThreads, 1) fht_hi2_kernel(const
 template <typename T, int SRC>
 const void* hi_kernel_h(int h) {
   switch (h) {
+    case 1: return (const void*)fht_hi_kernel<T, 1, SRC>;
+    case 2: return (const void*)fht_hi_kernel<T, 2, SRC>;
     case 3: return (const void*)fht_hi_kernel<T, 3, SRC>;
     case 4: return (const void*)fht_hi_kernel<T, 4, SRC>;
     case 5: return (const void*)fht_hi_kernel<T, 5, SRC>;
@@ -238,14 +241,14 @@ const void* hi_kernel(int src, int h) {
 
 }  // namespace f32k
 
-// A planned tile-engine launch this pass can take: a 16-bit two-pass plan's
-// high-bit launch (column chunks of 8 below 15 low bits) of 3..6 high bits
-// into the fp32 workspace.
+// A planned tile-engine launch this pass can take: a two-pass plan's high-bit
+// launch (column chunks of 8 below 15 low bits) of 1..8 high bits into the
+// fp32 workspace, for any dtype (fp32 arithmetic throughout).
 bool fht_hi_eligible(int dtype, const TileParams& p) {
-  if (dtype != LWL_BF16 && dtype != LWL_F16) return false;
+  if (dtype != LWL_BF16 && dtype != LWL_F16 && dtype != LWL_F32) return false;
   if (p.lo || p.tlo != 15 || p.cb != 3 || p.dst_kind != DST_WS) return false;
   const int h = p.n - 15;
-  if (h < 3 || h > 8 || p.r != h || p.nslots > f32k::kMaxSlots || p.nruns < 1) return false;
+  if (h < 1 || h > 8 || p.r != h || p.nslots > f32k::kMaxSlots || p.nruns < 1) return false;
   for (int i = 0; i < p.nruns; ++i) {
     const RunDesc& rd = p.runs[i];
     if (rd.glo < 3 || rd.glo + rd.gr > 3 + h) return false;
@@ -268,7 +271,9 @@ int fht_hi_launch(int dtype, const TileParams& p_in, cudaStream_t st) {
   p.ntiles = p.nblocks << (h <= 6 ? h + 2 : 8);
   const int threads = 1 << (tb - 6);
   const size_t smem = h <= 6 ? 0 : (tb == 14 ? Tile<14>::kSmem : Tile<15>::kSmem);
-  const void* k = dtype == LWL_BF16 ? hi_kernel<__nv_bfloat16>(p.src_kind, h) : hi_kernel<__half>(p.src_kind, h);
+  const void* k = dtype == LWL_BF16 ? hi_kernel<__nv_bfloat16>(p.src_kind, h)
+                : dtype == LWL_F16  ? hi_kernel<__half>(p.src_kind, h)
+                                    : hi_kernel<float>(p.src_kind, h);
   if (smem > 0 && !set_max_smem(k, (int)smem)) return -1;
   int per_sm = 1;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, threads, smem) != cudaSuccess || per_sm < 1)

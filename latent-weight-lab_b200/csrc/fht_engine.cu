@@ -187,11 +187,14 @@ int plan_fht(const FhtArgs& a, FhtPlan& plan) {
     return 0;
   }
 
-  // two-pass layout.  For 16-bit dtypes the low pass is exactly 15 bits and
-  // runs on the tensor-core tile kernel (fht_lo_kernel); the high n-15 bits
-  // stay on the tile engine.
+  // two-pass layout.  The low pass is exactly 15 bits: on the tensor-core
+  // tile kernel for 16-bit dtypes (fht_lo_kernel), on the register-resident
+  // fp32 kernel for fp32 and the exact mode (fht32_lo_kernel); the high n-15
+  // bits run on fht_hi_kernel / fht_hi2_kernel where they qualify, else on
+  // the tile engine.
   const bool use_lo = mma_lo_supported(a.dtype, n, a.flags);
-  const int abits = use_lo ? 15 : (n + 1) / 2;
+  const bool use_lo32 = !use_lo && fht32_lo_supported(a.dtype, n, a.flags);
+  const int abits = (use_lo || use_lo32) ? 15 : (n + 1) / 2;
   const int hbits = n - abits;
   // execution order of (part, post-layer) steps; part 1 = P1 (low bits), 2 = P2
   int step_part[6], step_sign[6], nsteps = 0;
@@ -254,12 +257,12 @@ int plan_fht(const FhtArgs& a, FhtPlan& plan) {
     p.src_kind = is_first ? (bwd ? SRC_SLICE : SRC_LATENT) : SRC_WS;
     p.dst_kind = (is_last && !bwd) ? DST_SLICE : DST_WS;
     finish_launch(a.dtype, l);
-    if (use_lo && step_part[s] == 1 && nseg <= 2) {
-      p.lo = 1;
+    if ((use_lo || use_lo32) && step_part[s] == 1 && nseg <= 2) {
+      p.lo = use_lo ? 1 : 2;
       p.lo_nseg = nseg;
       p.lo_seg_slot[0] = seg_slot[0];
       p.lo_seg_slot[1] = nseg > 1 ? seg_slot[1] : -1;
-      l.grid = mma_lo_grid(p);
+      if (use_lo) l.grid = mma_lo_grid(p);
     }
     plan.nlaunch++;
     s = e_ + 1;
@@ -274,6 +277,7 @@ __global__ void reduce_rows_kernel(const float* __restrict__ src, int64_t rows, 
                                    int64_t L, T* __restrict__ out) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < L; i += (int64_t)gridDim.x * blockDim.x) {
     float s = 0.0f;
+#pragma unroll 8
     for (int64_t r = 0; r < rows; ++r) s += src[r * row_stride + i];
     out[i] = Cvt<T>::from_f(s);
   }
@@ -293,6 +297,13 @@ int run_plan_t(const FhtArgs& a, FhtPlan& plan, cudaStream_t st) {
     if (p.dst_kind == DST_SLICE) p.dst = a.out;
     else if (p.dst_kind == DST_WS) p.dst = a.workspace;
     else p.partial = reinterpret_cast<float*>(a.workspace);
+    if (p.lo == 2) {
+      if (fht32_lo_launch(a.dtype, p, st) != 0) {
+        set_error("fp32 low-pass launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return LWL_ERR_CUDA;
+      }
+      continue;
+    }
     if (p.lo) {
       if (mma_lo_launch(a.dtype, p, l.grid, st) != 0) {
         set_error("tensor-core low-pass launch failed: %s", cudaGetErrorString(cudaGetLastError()));

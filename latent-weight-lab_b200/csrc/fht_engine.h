@@ -51,7 +51,11 @@ bool fht32_supported(int dtype, int64_t latent_size, bool backward, unsigned fla
 size_t fht32_workspace_bytes(const FhtArgs& a);
 int fht32_launches(const FhtArgs& a);  // kernels one call enqueues
 
-// High-bit pass of 16-bit two-pass plans with 3..6 high bits (fht32_hi.cu).
+// fp32 low pass of two-pass plans (fp32 and the exact mode, 2^16..2^23; fht32_lo.cu).
+bool fht32_lo_supported(int dtype, int n, unsigned flags);
+int fht32_lo_launch(int dtype, const TileParams& p, cudaStream_t st);
+
+// High-bit pass of two-pass plans with 15 low bits and 1..8 high bits (fht32_hi.cu).
 bool fht_hi_eligible(int dtype, const TileParams& p);
 int fht_hi_launch(int dtype, const TileParams& p, cudaStream_t st);
 int fht32_run(const FhtArgs& a, cudaStream_t st);

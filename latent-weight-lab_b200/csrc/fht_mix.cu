@@ -3,7 +3,8 @@
 // Reference: examples/nanogpt/model.py:182-218 (normalized_fht_last_dim + FixedFHTMix.forward).
 // The map is symmetric, so the same kernel computes the gradient.
 //
-// This kernel serves P <= 1024; larger P run on the tile kernel of
+// This kernel serves full rows of P = 256 .. 1024 and rows that are not
+// 16-byte aligned up to P = 1024; the rest run on the tile kernels of
 // fht32_mix.cu.  HBM-bound: one read and one write per element.  E = P / 32 values per lane
 // (E <= 32, fp32 registers) in chunks of up to 16 bytes: lane l owns chunks
 // l, l + 32, ... of the row's 1024-element slice of its warp, so every warp
@@ -13,6 +14,8 @@
 // sign-bit flips from a per-CTA bit table.  For P < 32 one warp holds 32 / P rows.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+
+#include <cstdlib>
 
 #include "lwl_common.cuh"
 
@@ -237,10 +240,31 @@ bool fht_mix32_supported(int logP);
 int fht_mix32_launch(int dtype, const void* x, void* y, const float* signs, int64_t rows, int F, int logP,
                      cudaStream_t st);
 
+bool fht_mix32p_supported(int dtype, const void* x, const void* y, int F, int logP);
+int fht_mix32p_launch(int dtype, const void* x, void* y, const float* signs, int64_t rows, int F, int logP,
+                      cudaStream_t st);
+
+// Kernel choice (LWL_MIX_KERNEL overrides for measurement: 1 = warp-per-row,
+// 2 = tile, 3 = prefetching tile; each only where it applies).
+static int mix_choice() {
+  static const int v = [] {
+    const char* s = std::getenv("LWL_MIX_KERNEL");
+    return s ? std::atoi(s) : 0;
+  }();
+  return v;
+}
+
 int fht_mix_launch(int dtype, const void* x, void* y, const float* signs, int64_t rows, int F, int logP,
                    cudaStream_t st) {
-  // P = 2048 .. 8192: the register-resident tile kernel (fht32_mix.cu)
-  if (fht_mix32_supported(logP)) return fht_mix32_launch(dtype, x, y, signs, rows, F, logP, st);
+  const int c = mix_choice();
+  // aligned rows: the prefetching register-resident tile kernel (fht32_mix.cu),
+  // except for full rows of P = 256 .. 1024, where the warp-per-row kernel
+  // below measured 3-8% faster
+  const bool warp_rows = F == (1 << logP) && logP >= 8 && logP <= 10;
+  if ((c == 3 || (c == 0 && !warp_rows)) && fht_mix32p_supported(dtype, x, y, F, logP))
+    return fht_mix32p_launch(dtype, x, y, signs, rows, F, logP, st);
+  // other P = 2048 .. 8192: the tile kernel without prefetch
+  if (c != 1 && fht_mix32_supported(logP)) return fht_mix32_launch(dtype, x, y, signs, rows, F, logP, st);
   if (dtype == 0) return mix::launch_t<float>(x, y, signs, rows, F, logP, st);
   if (dtype == 1) return mix::launch_t<__nv_bfloat16>(x, y, signs, rows, F, logP, st);
   return mix::launch_t<__half>(x, y, signs, rows, F, logP, st);

@@ -57,7 +57,7 @@ struct TileParams {
   int64_t start, stop;
   float* partial;  // DST_ACC: [gridDim.x][L]
   // launches of the low-15-bit pass on the tensor-core kernel (16-bit dtypes, B > 2^15)
-  int lo;           // 1: run on fht_lo_kernel instead of fht_tile_kernel
+  int lo;           // 1: run on fht_lo_kernel (16-bit), 2: on fht32_lo_kernel (fp32 math), instead of fht_tile_kernel
   int lo_nseg;      // 1 or 2 applications of the 2^15 transform
   int lo_seg_slot[2];  // sign slot after each application, -1 = none
 };

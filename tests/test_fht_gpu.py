@@ -404,3 +404,29 @@ def test_fp32_whole_block_slices(nat, logb, layers):
                               (3 * E + 5, E - 9, E + 11), (5 * E, E // 5, 4 * E + 123)]:
         _check_forward(nat, L, size, layers, 1234 + logb, start, stop, torch.float32)
         _check_backward(nat, L, size, layers, 1234 + logb, start, stop, torch.float32)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("logb", [16, 17, 19, 21])
+@pytest.mark.parametrize("layers", [1, 2, 3])
+def test_fp32_two_pass_blocks(nat, logb, layers):
+    """fp32 blocks above 2^15: a 15-bit low pass in fp32 arithmetic (one or two
+    applications per launch) and the high pass, with slices that start and end
+    inside a 2^15 chunk, cover whole chunks, or lie inside one chunk."""
+    B = 1 << logb
+    C = 1 << 15
+    L = B - 77
+    size = 2 * B + 9
+    for start, stop in [(0, size), (C + 5, min(B + 3 * C - 7, size)), (B - C // 2, B - 10), (2 * B, size)]:
+        _check_forward(nat, L, size, layers, 77 + logb, start, stop, torch.float32)
+        _check_backward(nat, L, size, layers, 77 + logb, start, stop, torch.float32)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("logb", [16, 18, 20])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_exact_flag_large_blocks(nat, logb, dtype):
+    """The exact mode on 16-bit generators above 2^15 takes the fp32 two-pass path."""
+    B = 1 << logb
+    _check_forward(nat, B - 5, B + 100, 3, 4321, 0, B + 100, dtype, flags=nat.FLAG_EXACT)
+    _check_backward(nat, B - 5, B + 100, 3, 4321, 17, B + 50, dtype, flags=nat.FLAG_EXACT)

@@ -66,8 +66,8 @@ def test_gpu_forward_backward_match_reference(native_lib, dtype, tol):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("features", [1, 5, 31, 32, 33, 100, 1024, 1025, 1600, 2048, 2049, 3072, 4095, 6400, 8191,
-                                      8192])
+@pytest.mark.parametrize("features", [1, 5, 8, 16, 24, 31, 32, 33, 40, 64, 100, 128, 200, 520, 768, 1024, 1025, 1600,
+                                      2048, 2049, 3072, 4095, 6400, 8191, 8192])
 def test_gpu_shapes_against_oracle(native_lib, features):
     """Every register/shuffle/exchange regime, ragged widths, leading dims, many rows."""
     from latent_weight_lab.fht_mix import FixedFHTMix
@@ -82,10 +82,11 @@ def test_gpu_shapes_against_oracle(native_lib, features):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("features", [1600, 3072, 6400])
+@pytest.mark.parametrize("features", [8, 16, 24, 56, 136, 768, 1000, 1600, 3072, 6400])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_gpu_wide_rows_half(native_lib, features, dtype):
-    """16-bit rows at the GPT widths (the tile kernel for P >= 2048): 1e-2 against fp32 math on the rounded input."""
+    """16-bit rows at the GPT widths and at other 16-byte-aligned widths (the prefetching tile
+    kernel for P >= 128): 1e-2 against fp32 math on the rounded input."""
     from latent_weight_lab.fht_mix import FixedFHTMix
 
     torch.manual_seed(features + 1)

@@ -67,22 +67,42 @@ struct Tile {
   static constexpr int kBsub = ((1 << (TB - 6)) - 1) & ~0x3F;  // B bits below C
 };
 
-enum Set : int { SA = 0, SB = 1, SC = 2 };
+// Two more splits for TB = 15 (fht32_lo.cu) hold four consecutive tile
+// elements (t0, t1) per register group, so a thread stores 16 bytes at once
+// and a warp 512 (SD) or 2 x 256 (SD2) consecutive bytes:
+//   SD:  registers t0, t1, t11..t14; lanes t2..t6;      warps t7..t10
+//   SD2: registers t0, t1, t6..t9;   lanes t2..t5, t10; warps t11..t14
+enum Set : int { SA = 0, SB = 1, SC = 2, SD = 3, SD2 = 4 };
 
 template <int TB>
-__host__ __device__ constexpr int reg_bit(int set, int j) { return set == SA ? j : (set == SB ? 6 + j : TB - 6 + j); }
+__host__ __device__ constexpr int reg_bit(int set, int j) {
+  return set == SA ? j
+       : set == SB ? 6 + j
+       : set == SC ? TB - 6 + j
+       : j < 2     ? j
+       : set == SD ? TB - 6 + j
+                   : 4 + j;
+}
 
 // tile index of register rho of this thread = base | spread(rho) (disjoint bits)
 template <int TB, int SET>
 __device__ __forceinline__ int base_of(int lane, int warp) {
   if (SET == SA) return (lane << 6) | (warp << 11);
   if (SET == SB) return lane | ((warp & 1) << 5) | ((warp >> 1) << 12);
+  if (SET == SD) return (lane << 2) | (warp << 7);
+  if (SET == SD2) return ((lane & 15) << 2) | ((lane >> 4) << 10) | (warp << 11);
   return lane | (warp << 5);
 }
 template <int TB, int SET>
 __host__ __device__ constexpr int spread(int rho) {
-  return SET == SA ? rho : (SET == SB ? rho << 6 : rho << (TB - 6));
+  return SET == SA ? rho
+       : SET == SB ? rho << 6
+       : SET == SC ? rho << (TB - 6)
+       : SET == SD ? (rho & 3) | ((rho >> 2) << (TB - 4))
+                   : (rho & 3) | ((rho >> 2) << 6);
 }
+template <int SET>
+__host__ __device__ constexpr bool quads() { return SET == SA || SET == SD || SET == SD2; }
 
 // Shared-memory word address of tile element t: four pad words per 64.  For
 // every set the lanes of a warp then hit distinct banks (lanes on t6..t10
@@ -146,6 +166,15 @@ __device__ __forceinline__ void apply_sign(float (&v)[kRegs], const uint32_t* sw
       const uint32_t w = (r & 32) ? w1 : w0;
       v[r] = flip(v[r], (w << (31 - (r & 31))) & 0x80000000u);
     }
+  } else if (SET == SD || SET == SD2) {
+    // t0, t1 are register bits, t2..t4 lane bits: one word per group of four
+#pragma unroll
+    for (int q = 0; q < kRegs / 4; ++q) {
+      const int t = base + spread<TB, SET>(4 * q);
+      const uint32_t w = ~sw[t >> 5] >> (t & 31);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[4 * q + e] = flip(v[4 * q + e], (w << (31 - e)) & 0x80000000u);
+    }
   } else {
     // t0..t4 are the lane: one bit of a (warp-uniform) word per register;
     // (base >> 5) and (spread >> 5) have disjoint bits
@@ -158,10 +187,11 @@ __device__ __forceinline__ void apply_sign(float (&v)[kRegs], const uint32_t* sw
 
 template <int TB, int SET>
 __device__ __forceinline__ void smem_write(const float (&v)[kRegs], float* b) {
-  if (SET == SA) {
+  if (quads<SET>()) {
 #pragma unroll
     for (int q = 0; q < kRegs / 4; ++q)
-      *reinterpret_cast<float4*>(b + pad(4 * q)) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      *reinterpret_cast<float4*>(b + pad(spread<TB, SET>(4 * q))) =
+          make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
   } else {
 #pragma unroll
     for (int r = 0; r < kRegs; ++r) b[pad(spread<TB, SET>(r))] = v[r];
@@ -169,10 +199,10 @@ __device__ __forceinline__ void smem_write(const float (&v)[kRegs], float* b) {
 }
 template <int TB, int SET>
 __device__ __forceinline__ void smem_read(float (&v)[kRegs], const float* b) {
-  if (SET == SA) {
+  if (quads<SET>()) {
 #pragma unroll
     for (int q = 0; q < kRegs / 4; ++q) {
-      const float4 x = *reinterpret_cast<const float4*>(b + pad(4 * q));
+      const float4 x = *reinterpret_cast<const float4*>(b + pad(spread<TB, SET>(4 * q)));
       v[4 * q] = x.x, v[4 * q + 1] = x.y, v[4 * q + 2] = x.z, v[4 * q + 3] = x.w;
     }
   } else {
@@ -346,6 +376,12 @@ __global__ void __launch_bounds__(Tile<TB>::kThreads, Tile<TB>::kMinBlocks)
   float v[kRegs];
   for (int64_t it = blockIdx.x; it < p.ntiles; it += gridDim.x) {
     const int64_t tile = p.first_tile + it * p.tile_step;
+    if (BWD && TB > 13 && tid == 0 && it + gridDim.x < p.ntiles) {
+      // one CTA per SM at TB > 13: the next tile's gradient slice into L2 while this one runs
+      const int64_t g0 = ((p.first_tile + (it + gridDim.x) * p.tile_step) << TB) - p.start, ns = p.stop - p.start;
+      const int64_t lo = g0 > 0 ? g0 : 0, hi = g0 + (1 << TB) < ns ? g0 + (1 << TB) : ns;
+      if (hi > lo) prefetch_l2(p.src, lo * (int64_t)sizeof(T), hi * (int64_t)sizeof(T));
+    }
     __syncthreads();  // the previous tile is done with the sign table
     {
       const int wsh = n - 5;  // words per block = 2^(n-5)

@@ -5,11 +5,15 @@
 // H_B = H_hi (x) H_32768: this pass applies H_32768 to the 15 low position
 // bits of every 2^15 chunk of a block, once or twice, with the plan's signs,
 // and the high bits run in fht32_hi.cu.  A CTA of 512 threads owns one chunk
-// (TB = 15, 64 values per thread).  One application is sets A, B and C (two
+// (TB = 15, 64 values per thread).  One application is sets A, B and SD (three
 // exchanges); two applications share set C between them:
-//     one:  A: [pre-sign] T(t0..5) -> B: T(t6..11) -> C: T(t12..14) [sign]
-//     two:  A: [pre-sign] T(A) -> B: T(B) -> C: T(t12..14) [sign] T(t9..14)
-//           -> A: T(A) -> B: T(t6..8) [sign]
+//     one:  SD: [pre-sign] -> A: T(t0..5) -> B: T(t6..11) -> SD: T(t12..14) [sign]
+//     two:  SD: [pre-sign] -> A: T(A) -> B: T(B) -> C: T(t12..14) [sign] T(t9..14)
+//           -> A: T(A) -> SD2: T(t6..8) [sign]
+// The first and last residencies (SD / SD2) hold four consecutive elements per
+// register group, so the tile arrives and leaves with 16-byte accesses that
+// are contiguous across the warp (set A's 16-byte loads, one per lane at a
+// 256-byte stride, held the kernel on the L1 request queue).
 // A sign that ends a layer carries the layer's 1/sqrt(B), exactly as the
 // tile engine applies it; an application without one leaves the result
 // unnormalised (the high pass of the same layer normalises it).
@@ -21,22 +25,19 @@
 namespace lwl {
 namespace f32k {
 
-// Source values of chunk j of block b in set SET (zero outside the latent / slice).
-template <typename T, int SET, int SRC>
+// Source values of chunk j of block b in set SD (four consecutive elements per
+// register group, lanes on t2..t6: each warp load covers 512 consecutive bytes
+// of fp32), zero outside the latent / slice.
+template <typename T, int SRC>
 __device__ __forceinline__ void lo32_load(float (&v)[kRegs], const TileParams& p, int64_t b, int64_t pos0,
                                           int base) {
-  constexpr int TB = 15;
+  constexpr int TB = 15, SET = SD;
   if (SRC == SRC_WS) {
     const float* s = reinterpret_cast<const float*>(p.src) + (b - p.first_block) * p.B + pos0 + base;
-    if (SET == SA) {
 #pragma unroll
-      for (int q = 0; q < kRegs / 4; ++q) {
-        const float4 a = *reinterpret_cast<const float4*>(s + 4 * q);
-        v[4 * q] = a.x, v[4 * q + 1] = a.y, v[4 * q + 2] = a.z, v[4 * q + 3] = a.w;
-      }
-    } else {
-#pragma unroll
-      for (int r = 0; r < kRegs; ++r) v[r] = s[spread<TB, SET>(r)];
+    for (int q = 0; q < kRegs / 4; ++q) {
+      const float4 a = *reinterpret_cast<const float4*>(s + spread<TB, SET>(4 * q));
+      v[4 * q] = a.x, v[4 * q + 1] = a.y, v[4 * q + 2] = a.z, v[4 * q + 3] = a.w;
     }
     return;
   }
@@ -53,9 +54,21 @@ __device__ __forceinline__ void lo32_load(float (&v)[kRegs], const TileParams& p
     hi = p.stop - g;
   }
   const T* s = src + off;
-  if (lo <= 0 && hi >= (int64_t(1) << TB)) {
+  const bool vec = (reinterpret_cast<uintptr_t>(s) & (4 * sizeof(T) - 1)) == 0;
+  if (lo <= 0 && hi >= (int64_t(1) << TB) && vec) {
 #pragma unroll
-    for (int r = 0; r < kRegs; ++r) v[r] = Cvt<T>::to_f(s[spread<TB, SET>(r)]);
+    for (int q = 0; q < kRegs / 4; ++q) {
+      const T* e = s + spread<TB, SET>(4 * q);
+      if (sizeof(T) == 4) {
+        const float4 a = *reinterpret_cast<const float4*>(e);
+        v[4 * q] = a.x, v[4 * q + 1] = a.y, v[4 * q + 2] = a.z, v[4 * q + 3] = a.w;
+      } else {
+        const uint2 a = *reinterpret_cast<const uint2*>(e);
+        const T* h = reinterpret_cast<const T*>(&a);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[4 * q + i] = Cvt<T>::to_f(h[i]);
+      }
+    }
   } else {
 #pragma unroll
     for (int r = 0; r < kRegs; ++r) {
@@ -65,22 +78,40 @@ __device__ __forceinline__ void lo32_load(float (&v)[kRegs], const TileParams& p
   }
 }
 
+// Results of set SD / SD2 (four consecutive elements per register group): one
+// 16-byte (fp32) or 8-byte (16-bit) store per group where aligned.
 template <typename T, int SET, int DST>
 __device__ __forceinline__ void lo32_store(const float (&v)[kRegs], const TileParams& p, int64_t b, int64_t pos0,
                                            int base) {
   constexpr int TB = 15;
+  static_assert(SET == SD || SET == SD2, "stores leave from the quad sets");
   if (DST == DST_WS) {
     float* d = reinterpret_cast<float*>(p.dst) + (b - p.first_block) * p.B + pos0 + base;
 #pragma unroll
-    for (int r = 0; r < kRegs; ++r) d[spread<TB, SET>(r)] = v[r];
+    for (int q = 0; q < kRegs / 4; ++q)
+      *reinterpret_cast<float4*>(d + spread<TB, SET>(4 * q)) =
+          make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
     return;
   }
   const int64_t g = b * p.B + pos0 + base;
   T* d = reinterpret_cast<T*>(p.dst) + (g - p.start);
   const int64_t lo = p.start - g, hi = p.stop - g;
-  if (lo <= 0 && hi >= (int64_t(1) << TB)) {
+  const int64_t t0 = b * p.B + pos0;  // the tile's range [t0, t0 + 2^TB) inside the slice?
+  const bool full = t0 >= p.start && t0 + (int64_t(1) << TB) <= p.stop;
+  const bool vec = ((p.start & 3) == 0) && (reinterpret_cast<uintptr_t>(p.dst) & (4 * sizeof(T) - 1)) == 0;
+  if (full && vec) {
 #pragma unroll
-    for (int r = 0; r < kRegs; ++r) d[spread<TB, SET>(r)] = Cvt<T>::from_f(v[r]);
+    for (int q = 0; q < kRegs / 4; ++q) {
+      T* e = d + spread<TB, SET>(4 * q);
+      if (sizeof(T) == 4) {
+        *reinterpret_cast<float4*>(e) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      } else {
+        T h[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = Cvt<T>::from_f(v[4 * q + i]);
+        *reinterpret_cast<uint2*>(e) = *reinterpret_cast<const uint2*>(h);
+      }
+    }
   } else {
 #pragma unroll
     for (int r = 0; r < kRegs; ++r) {
@@ -106,6 +137,7 @@ __global__ void __launch_bounds__(Tile<15>::kThreads, 1) fht32_lo_kernel(const _
   uint32_t* sw = reinterpret_cast<uint32_t*>(buf + Tl::kBufWords);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int bA = base_of<TB, SA>(lane, warp), bB = base_of<TB, SB>(lane, warp), bC = base_of<TB, SC>(lane, warp);
+  const int bD = base_of<TB, SD>(lane, warp), bD2 = base_of<TB, SD2>(lane, warp);
   const int cpb = (int)(p.B >> TB);  // chunks per block
   const int64_t ntiles = p.nblocks * cpb;
   const int s1 = p.lo_seg_slot[0], s2 = NSEG == 2 ? p.lo_seg_slot[1] : -1;
@@ -114,30 +146,45 @@ __global__ void __launch_bounds__(Tile<15>::kThreads, 1) fht32_lo_kernel(const _
     const int64_t b = p.first_block + tile / cpb;
     const int j = (int)(tile % cpb);
     const int64_t pos0 = (int64_t)j << TB;
+    if (tid == 0 && tile + gridDim.x < ntiles) {  // the next tile's source into L2
+      const int64_t nt = tile + gridDim.x, nb = p.first_block + nt / cpb, np = (nt % cpb) << TB;
+      if (SRC == SRC_WS) {
+        const int64_t e0 = (nb - p.first_block) * p.B + np;
+        prefetch_l2(p.src, e0 * 4, (e0 + (1 << TB)) * 4);
+      } else if (SRC == SRC_SLICE) {
+        const int64_t g0 = nb * p.B + np - p.start, n = p.stop - p.start;
+        const int64_t lo = g0 > 0 ? g0 : 0, hi = g0 + (1 << TB) < n ? g0 + (1 << TB) : n;
+        if (hi > lo) prefetch_l2(p.src, lo * (int64_t)sizeof(T), hi * (int64_t)sizeof(T));
+      }
+    }
     __syncthreads();  // the previous tile is done with the sign table and the exchange buffer
     for (int i = tid; i < p.nslots * Tl::kWords; i += Tl::kThreads) {
       const int s = i / Tl::kWords, c = i - s * Tl::kWords;
       sw[i] = sign_word(block_layer_key(p.seed32, b, p.slot_layer[s]), ((int64_t)j << 10) + c);
     }
     __syncthreads();
-    lo32_load<T, SA, SRC>(v, p, b, pos0, bA);
-    if (p.pre_slot >= 0) apply_sign<TB, SA>(v, sw + p.pre_slot * Tl::kWords, bA);
+    lo32_load<T, SRC>(v, p, b, pos0, bD);
+    if (p.pre_slot >= 0) apply_sign<TB, SD>(v, sw + p.pre_slot * Tl::kWords, bD);
+    exchange<TB, SD, SA>(v, buf, lane, warp);
     xform<TB, SA>(v, Tl::kA, TB);
     exchange<TB, SA, SB>(v, buf, lane, warp);
     xform<TB, SB>(v, Tl::kB, TB);
-    exchange<TB, SB, SC>(v, buf, lane, warp);
-    xform<TB, SC>(v, Tl::kChi, TB);
-    if (s1 >= 0) sign_scaled<TB, SC>(v, sw + s1 * Tl::kWords, bC, p.scale);
     if (NSEG == 1) {
-      lo32_store<T, SC, DST>(v, p, b, pos0, bC);
+      exchange<TB, SB, SD>(v, buf, lane, warp);
+      xform<TB, SD>(v, Tl::kChi, TB);
+      if (s1 >= 0) sign_scaled<TB, SD>(v, sw + s1 * Tl::kWords, bD, p.scale);
+      lo32_store<T, SD, DST>(v, p, b, pos0, bD);
     } else {
+      exchange<TB, SB, SC>(v, buf, lane, warp);
+      xform<TB, SC>(v, Tl::kChi, TB);
+      if (s1 >= 0) sign_scaled<TB, SC>(v, sw + s1 * Tl::kWords, bC, p.scale);
       xform<TB, SC>(v, Tl::kC, TB);
       exchange<TB, SC, SA>(v, buf, lane, warp);
       xform<TB, SA>(v, Tl::kA, TB);
-      exchange<TB, SA, SB>(v, buf, lane, warp);
-      xform<TB, SB>(v, Tl::kBsub, TB);
-      if (s2 >= 0) sign_scaled<TB, SB>(v, sw + s2 * Tl::kWords, bB, p.scale);
-      lo32_store<T, SB, DST>(v, p, b, pos0, bB);
+      exchange<TB, SA, SD2>(v, buf, lane, warp);
+      xform<TB, SD2>(v, Tl::kBsub, TB);
+      if (s2 >= 0) sign_scaled<TB, SD2>(v, sw + s2 * Tl::kWords, bD2, p.scale);
+      lo32_store<T, SD2, DST>(v, p, b, pos0, bD2);
     }
   }
 }

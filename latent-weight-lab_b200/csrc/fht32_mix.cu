@@ -124,6 +124,29 @@ __global__ void __launch_bounds__(Tile<13>::kThreads, Tile<13>::kMinBlocks)
 // tile of loads in flight through its compute phase.  Stage layout: chunk c
 // (64 consecutive tile elements) at c * (64 * sizeof(T) + 16) bytes, so the
 // set-A reads (lanes one chunk apart, 16 bytes each) are bank-conflict free.
+// The fixed sign vector is the same for every tile, so each thread gathers the
+// 64 sign bits of its registers in a set once (bit r set = negate register r)
+// and a flip is two integer ops per element.
+template <int SET>
+__device__ __forceinline__ uint64_t sign_mask(const uint32_t* sw, int base) {
+  uint64_t m = 0;
+#pragma unroll
+  for (int r = 0; r < kRegs; ++r) {
+    const int t = base | spread<13, SET>(r);
+    m |= (uint64_t)((~sw[t >> 5] >> (t & 31)) & 1u) << r;
+  }
+  return m;
+}
+__device__ __forceinline__ void apply_mask(float (&v)[kRegs], uint64_t m) {
+  // opaque copies: otherwise the compiler hoists 64 per-register flip words
+  // out of the tile loop and runs out of registers
+  uint32_t lo, hi;
+  asm volatile("mov.b32 %0, %1;" : "=r"(lo) : "r"((uint32_t)m));
+  asm volatile("mov.b32 %0, %1;" : "=r"(hi) : "r"((uint32_t)(m >> 32)));
+#pragma unroll
+  for (int r = 0; r < kRegs; ++r) v[r] = flip(v[r], ((r < 32 ? lo : hi) << (31 - (r & 31))) & 0x80000000u);
+}
+
 template <typename T>
 struct Stage {
   static constexpr int kChunkBytes = 64 * (int)sizeof(T) + 16;
@@ -176,6 +199,8 @@ __global__ void __launch_bounds__(Tile<13>::kThreads)
     if (lane == 0) sw[c] = b;
   }
   const int bA = base_of<13, SA>(lane, warp), bB = base_of<13, SB>(lane, warp), bC = base_of<13, SC>(lane, warp);
+  __syncthreads();  // the sign table is complete
+  const uint64_t mA = sign_mask<SA>(sw, bA), mOut = N == 13 ? sign_mask<SC>(sw, bC) : sign_mask<SB>(sw, bB);
   float v[kRegs];
   int s = 0;
   for (int64_t tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, s ^= 1) {
@@ -201,17 +226,17 @@ __global__ void __launch_bounds__(Tile<13>::kThreads)
         v[q * PER + u] = f;
       }
     }
-    apply_sign<13, SA>(v, sw, bA);
+    apply_mask(v, mA);
     xform<13, SA>(v, Tl::kA, N);
     exchange<13, SA, SB>(v, buf, lane, warp);
     xform<13, SB>(v, Tl::kB, N);
     if constexpr (N == 13) {
       exchange<13, SB, SC>(v, buf, lane, warp);
       xform<13, SC>(v, Tl::kChi, N);
-      apply_sign<13, SC>(v, sw, bC);
+      apply_mask(v, mOut);
       mix_store<T, N, SC>(v, p, tile, bC);
     } else {
-      apply_sign<13, SB>(v, sw, bB);
+      apply_mask(v, mOut);
       mix_store<T, N, SB>(v, p, tile, bB);
     }
   }

@@ -1358,6 +1358,22 @@ __device__ __forceinline__ void lo_load8(const TileParams& p, int64_t b, int64_t
   }
 }
 
+// L2 prefetch of the source of work item `tile` (the CTA's next one): its
+// fp32 workspace tile or its part of the gradient slice (the latent is shared
+// by all tiles and stays in L2).
+template <typename T>
+__device__ __forceinline__ void lo_prefetch_next(const TileParams& p, int64_t tile, int tpb) {
+  const int64_t b = p.first_block + tile / tpb, pos0 = (tile % tpb) << kLog;
+  if (p.src_kind == SRC_WS) {
+    const int64_t e0 = (b - p.first_block) * p.B + pos0;
+    prefetch_l2(p.src, e0 * 4, (e0 + kB) * 4);
+  } else if (p.src_kind == SRC_SLICE) {
+    const int64_t g0 = b * p.B + pos0 - p.start;
+    const int64_t lo = g0 > 0 ? g0 : 0, hi = (g0 + kB < p.stop - p.start) ? g0 + kB : p.stop - p.start;
+    if (hi > lo) prefetch_l2(p.src, lo * (int64_t)sizeof(T), hi * (int64_t)sizeof(T));
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_constant__ TileParams p, float corr1) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -1385,6 +1401,7 @@ __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_consta
     const int64_t b = p.first_block + tile / tpb;
     const int j = (int)(tile % tpb);
     const int64_t tbase = (int64_t)j << kLog;  // first position of the tile in its block
+    if (tid == 0 && tile + gridDim.x < ntiles) lo_prefetch_next<T>(p, tile + gridDim.x, tpb);
     __syncthreads();
     for (int i = tid; i < p.nslots * kWords; i += kThreads) {
       int sl = i / kWords, wd = i - sl * kWords;

@@ -68,6 +68,20 @@ inline int64_t next_pow2(int64_t v) {
   return o;
 }
 
+// Asks L2 to fetch bytes [lo, hi) of `base` (rounded inward to 16-byte
+// boundaries, so nothing outside the range is touched), in 64 KB pieces.
+// Issued by one thread for a tile that is loaded later, it lets the HBM fetch
+// overlap the current tile's work; the later loads then hit L2.
+__device__ __forceinline__ void prefetch_l2(const void* base, int64_t lo, int64_t hi) {
+  uint64_t a = reinterpret_cast<uint64_t>(base) + (uint64_t)lo, e = reinterpret_cast<uint64_t>(base) + (uint64_t)hi;
+  a = (a + 15) & ~uint64_t(15);
+  e &= ~uint64_t(15);
+  for (; a < e; a += 65536) {
+    const uint32_t n = (uint32_t)((e - a) < 65536 ? (e - a) : 65536);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(a), "r"(n) : "memory");
+  }
+}
+
 inline size_t dtype_bytes(int dtype) { return dtype == LWL_F32 ? 4 : 2; }
 
 // Thread-local error text for lwl_last_error().

@@ -302,13 +302,42 @@ __device__ __forceinline__ void load_first(float (&v)[kRegs], const Params& p, i
 // (four consecutive elements per register group, lanes on t2..t6: each warp
 // load covers 512 contiguous bytes of fp32) and moves to set A through shared
 // memory; set A's own loads (one 16-byte load per lane at a 256-byte stride)
-// keep the L1 request queue full.  The forward reads the small, L2-resident
-// latent directly in set A.
+// keep the L1 request queue full.  The forward reads the latent the same way
+// (it is L2-resident, but the L1 request cost is the same), except for blocks
+// of <= 128, whose positions repeat across the lanes of a set-A load (the
+// SD path measured 3-5% slower at 128).
 template <typename T, int TB, bool BWD, bool FULL>
 __device__ __forceinline__ void load_first_a(float (&v)[kRegs], const Params& p, int64_t tile, int bA, float* buf,
-                                             int lane, int warp) {
-  if (!BWD) {
+                                             int lane, int warp, int n) {
+  if (!BWD && n <= 7) {  // blocks of <= 128: a warp's lanes read the same few latent lines
     load_first<T, TB, SA, BWD, FULL>(v, p, tile, bA);
+    return;
+  }
+  if (!BWD) {
+    // latent positions (t mod B) of set SD: four consecutive per register group
+    const int bD = base_of<TB, SD>(lane, warp);
+    const int Bm = (1 << n) - 1;
+    const T* src = reinterpret_cast<const T*>(p.src);
+    const bool vec = (reinterpret_cast<uintptr_t>(src) & (4 * sizeof(T) - 1)) == 0;
+#pragma unroll
+    for (int q = 0; q < kRegs / 4; ++q) {
+      const int pos = (bD | spread<TB, SD>(4 * q)) & Bm;
+      if (vec && pos + 4 <= p.L) {
+        if (sizeof(T) == 4) {
+          const float4 a = *reinterpret_cast<const float4*>(src + pos);
+          v[4 * q] = a.x, v[4 * q + 1] = a.y, v[4 * q + 2] = a.z, v[4 * q + 3] = a.w;
+        } else {
+          const uint2 a = *reinterpret_cast<const uint2*>(src + pos);
+          const T* h = reinterpret_cast<const T*>(&a);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) v[4 * q + i] = Cvt<T>::to_f(h[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[4 * q + i] = pos + i < p.L ? ld_elem(src + pos + i) : 0.0f;
+      }
+    }
+    exchange<TB, SD, SA>(v, buf, lane, warp);
     return;
   }
   const int bD = base_of<TB, SD>(lane, warp);
@@ -441,7 +470,7 @@ __global__ void __launch_bounds__(Tile<TB>::kThreads, Tile<TB>::kMinBlocks)
     const uint32_t* s2 = sw + 2 * Tl::kWords;
     const uint32_t* s3 = sw + 3 * Tl::kWords;
     if constexpr (KCLS == 1) {
-      load_first_a<T, TB, BWD, FULL>(v, p, tile, bA, buf, lane, warp);
+      load_first_a<T, TB, BWD, FULL>(v, p, tile, bA, buf, lane, warp, n);
       apply_sign<TB, SA>(v, s0, bA);
       xform<TB, SA>(v, Tl::kA, n);
       apply_sign<TB, SA>(v, s1, bA);
@@ -470,7 +499,7 @@ __global__ void __launch_bounds__(Tile<TB>::kThreads, Tile<TB>::kMinBlocks)
         xform<TB, SB>(v, Tl::kB, n);
         apply_sign<TB, SB>(v, s2, bB);
       } else {
-        load_first_a<T, TB, BWD, FULL>(v, p, tile, bA, buf, lane, warp);
+        load_first_a<T, TB, BWD, FULL>(v, p, tile, bA, buf, lane, warp, n);
         apply_sign<TB, SA>(v, s0, bA);
         xform<TB, SA>(v, Tl::kA, n);
         exchange<TB, SA, SB>(v, buf, lane, warp);
@@ -506,7 +535,7 @@ __global__ void __launch_bounds__(Tile<TB>::kThreads, Tile<TB>::kMinBlocks)
         xform<TB, SC>(v, Tl::kChi, n);
         apply_sign<TB, SC>(v, s2, bC);
       } else {
-        load_first_a<T, TB, BWD, FULL>(v, p, tile, bA, buf, lane, warp);
+        load_first_a<T, TB, BWD, FULL>(v, p, tile, bA, buf, lane, warp, n);
         apply_sign<TB, SA>(v, s0, bA);
         xform<TB, SA>(v, Tl::kA, n);
         exchange<TB, SA, SB>(v, buf, lane, warp);

@@ -639,6 +639,7 @@ def run_sweep(args) -> None:
     N = COORDS_PER_GPU
     stream = torch.cuda.current_stream(dev).cuda_stream
     kinds = (("bf16", torch.bfloat16, _native.LWL_BF16), ("fp32", torch.float32, _native.LWL_F32))
+    flags = args.sweep_flags
     for dt_name, dt, code in (k for k in kinds if k[0] in args.sweep_dtypes.split(",")):
         y = torch.empty(N, device=dev, dtype=dt)
         g = torch.randn(N, device=dev, dtype=dt)
@@ -647,17 +648,17 @@ def run_sweep(args) -> None:
                 B = 1 << k
                 z = torch.randn(B, device=dev, dtype=dt)
                 grad = torch.empty(B, device=dev, dtype=dt)
-                wsb = max(lib.lwl_fht_forward_workspace_bytes(code, B, N, layers, 0, N, 0),
-                          lib.lwl_fht_backward_workspace_bytes(code, B, N, layers, 0, N, 0), 1)
+                wsb = max(lib.lwl_fht_forward_workspace_bytes(code, B, N, layers, 0, N, flags),
+                          lib.lwl_fht_backward_workspace_bytes(code, B, N, layers, 0, N, flags), 1)
                 ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
 
                 def fwd():
                     assert lib.lwl_fht_forward(code, z.data_ptr(), B, N, layers, SEED, 0, N, y.data_ptr(),
-                                               ws.data_ptr(), wsb, 0, stream) == 0
+                                               ws.data_ptr(), wsb, flags, stream) == 0
 
                 def bwd():
                     assert lib.lwl_fht_backward(code, g.data_ptr(), B, N, layers, SEED, 0, N, grad.data_ptr(),
-                                                ws.data_ptr(), wsb, 0, stream) == 0
+                                                ws.data_ptr(), wsb, flags, stream) == 0
 
                 res = {}
                 for name, fn in (("forward", fwd), ("backward", bwd)):
@@ -672,7 +673,7 @@ def run_sweep(args) -> None:
                     torch.cuda.synchronize()
                     ms = a.elapsed_time(b) / reps
                     res[name] = N / (ms * 1e-3) / 1e9
-                print(json.dumps({"sweep": "C2", "dtype": dt_name, "layers": layers, "block_size": B,
+                print(json.dumps({"sweep": "C2", "dtype": dt_name, "flags": flags, "layers": layers, "block_size": B,
                                   "coords": N, "forward_gcoords_s": res["forward"],
                                   "backward_gcoords_s": res["backward"],
                                   "forward_hbm_frac": res["forward"] * 1e9 * y.element_size() / 1e9
@@ -1224,6 +1225,7 @@ def main() -> None:
     ap.add_argument("--min-log", type=int, default=5)
     ap.add_argument("--max-log", type=int, default=23)
     ap.add_argument("--sweep-dtypes", default="bf16,fp32", help="--workload sweep: comma-separated bf16,fp32")
+    ap.add_argument("--sweep-flags", type=int, default=0, help="--workload sweep: transform flags (1 = LWL_FLAG_EXACT)")
     ap.add_argument("--latent", type=int, default=32768, help="latent size for --workload mlp")
     ap.add_argument("--tokens", type=int, default=32768, help="tokens for --workload linear (mix: rows / 2)")
     ap.add_argument("--features", type=int, default=3072, help="features for --workload mix")

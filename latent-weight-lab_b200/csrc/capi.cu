@@ -89,6 +89,7 @@ static int fht_call(bool backward, int dtype, const void* in, void* out, int64_t
   a.workspace = ws;
   a.workspace_bytes = ws_bytes;
   a.flags = flags;
+  if (fhts_supported(dtype, L, backward, layers, flags)) return fhts_run(a, reinterpret_cast<cudaStream_t>(stream));
   if (!backward && mma_forward_supported(dtype, L, flags)) {
     if (mma_forward(dtype, in, L, layers, seed, start, stop, out, reinterpret_cast<cudaStream_t>(stream)) != 0) {
       set_error("tensor-core forward launch failed: %s", cudaGetErrorString(cudaGetLastError()));
@@ -142,6 +143,19 @@ static int fht_call(bool backward, int dtype, const void* in, void* out, int64_t
 static size_t fht_ws(bool backward, int dtype, int64_t L, int64_t size, int layers, int64_t start,
                      int64_t stop, unsigned flags) {
   if (validate_fht(dtype, L, size, layers, start, stop) != LWL_OK) return 0;
+  if (fhts_supported(dtype, L, backward, layers, flags)) {
+    FhtArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.dtype = dtype;
+    a.backward = backward;
+    a.latent_size = L;
+    a.size = size;
+    a.layers = layers;
+    a.start = start;
+    a.stop = stop;
+    a.flags = flags;
+    return fhts_workspace_bytes(a);
+  }
   if (!backward && mma_forward_supported(dtype, L, flags)) return 0;
   if (!backward && mma16_forward_supported(dtype, L, flags)) return 0;
   if (backward && mma_backward_supported(dtype, L, flags)) return mma_backward_workspace_bytes(L, start, stop);
@@ -301,7 +315,8 @@ int lwl_fht_backward_status(int dtype, int64_t latent_size, int64_t size, int la
   if (st) return st;
   // only the tensor-core backward waits on the device; it keeps its error word
   // at the start of a non-empty workspace
-  if (!lwl::mma_backward_supported(dtype, latent_size, flags) ||
+  if (lwl::fhts_supported(dtype, latent_size, true, layers, flags) ||
+      !lwl::mma_backward_supported(dtype, latent_size, flags) ||
       lwl::mma_backward_workspace_bytes(latent_size, start, stop) == 0)
     return LWL_OK;
   if (!workspace) {
@@ -339,14 +354,25 @@ int lwl_fht_forward_grouped(int dtype, int count, const lwl_fht_forward_desc* de
     if (!lwl::mma_forward_supported(dtype, q.latent_size, flags)) all_fast = false;
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (all_fast) {
-    if (lwl::mma_forward_grouped(dtype, count, descs, st) != 0) {
+  // Generators that a single call sends to the tensor-core tile kernel share
+  // one grouped launch; the rest (the small-block kernel's sizes included)
+  // run as single calls, so every output equals its single call bit for bit.
+  std::vector<lwl_fht_forward_desc> grouped;
+  std::vector<int> rest;
+  for (int i = 0; i < count; ++i) {
+    const lwl_fht_forward_desc& q = descs[i];
+    if (all_fast && !lwl::fhts_supported(dtype, q.latent_size, false, q.layers, flags))
+      grouped.push_back(q);
+    else
+      rest.push_back(i);
+  }
+  if (!grouped.empty()) {
+    if (lwl::mma_forward_grouped(dtype, (int)grouped.size(), grouped.data(), st) != 0) {
       lwl::set_error("grouped forward launch failed: %s", cudaGetErrorString(cudaGetLastError()));
       return LWL_ERR_CUDA;
     }
-    return LWL_OK;
   }
-  for (int i = 0; i < count; ++i) {
+  for (int i : rest) {
     const lwl_fht_forward_desc& q = descs[i];
     if (lwl::fht_ws(false, dtype, q.latent_size, q.size, q.layers, q.start, q.stop, flags) > 0) {
       lwl::set_error("descriptor %d needs a workspace; call lwl_fht_forward for it", i);
@@ -472,8 +498,11 @@ int lwl_linear_backward(int dtype, const void* x, const void* grad_y, int64_t to
   return LWL_OK;
 }
 
+// Generators that a single call sends to the tensor-core backward share the
+// grouped launch; the small-block kernel's sizes run as single calls.
 static bool grouped_bwd_fast(int dtype, const lwl_fht_backward_desc& q, unsigned flags) {
-  return lwl::mma_backward_supported(dtype, q.latent_size, flags);
+  return lwl::mma_backward_supported(dtype, q.latent_size, flags) &&
+         !lwl::fhts_supported(dtype, q.latent_size, true, q.layers, flags);
 }
 
 size_t lwl_fht_backward_grouped_workspace_bytes(int dtype, int count, const lwl_fht_backward_desc* descs,
@@ -630,6 +659,7 @@ int lwl_fht_launch_count(int dtype, int64_t latent_size, int64_t size, int layer
                          int backward, unsigned flags) {
   if (lwl::validate_fht(dtype, latent_size, size, layers, start, stop) != LWL_OK) return -1;
   if (stop == start) return 0;
+  if (lwl::fhts_supported(dtype, latent_size, backward != 0, layers, flags)) return backward ? 2 : 1;
   if (!backward && lwl::mma_forward_supported(dtype, latent_size, flags)) return 1;
   if (!backward && lwl::mma16_forward_supported(dtype, latent_size, flags)) return 1;
   if (backward && lwl::mma_backward_supported(dtype, latent_size, flags)) return 2;

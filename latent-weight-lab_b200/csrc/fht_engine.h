@@ -51,6 +51,13 @@ bool fht32_supported(int dtype, int64_t latent_size, bool backward, unsigned fla
 size_t fht32_workspace_bytes(const FhtArgs& a);
 int fht32_launches(const FhtArgs& a);  // kernels one call enqueues
 
+// Small-block kernel (fhts.cu): padded block 2^5 .. 2^10, every dtype, fp32
+// arithmetic, forward and backward.
+bool fhts_supported(int dtype, int64_t latent_size, bool backward, int layers, unsigned flags);
+size_t fhts_workspace_bytes(const FhtArgs& a);
+int fhts_launches(const FhtArgs& a);
+int fhts_run(const FhtArgs& a, cudaStream_t st);
+
 // fp32 low pass of two-pass plans (fp32 and the exact mode, 2^16..2^23; fht32_lo.cu).
 bool fht32_lo_supported(int dtype, int n, unsigned flags);
 int fht32_lo_launch(int dtype, const TileParams& p, cudaStream_t st);

@@ -1,0 +1,415 @@
+// fhts.cu -- small blocks (padded block size B = 2^5 .. 2^10), every dtype,
+// fp32 arithmetic, forward and backward.
+//
+// The work unit is a warp tile of 1024 consecutive coordinates (2^(10-n)
+// whole blocks).  Lane l holds the 32 coordinates 32 l .. 32 l + 31 of the
+// tile in fp32 registers, so
+//   * position bits 0..4 are register bits: those butterflies are register
+//     arithmetic (one add per value per bit);
+//   * position bits 5..n-1 are the low lane bits: one shfl.bfly + one FMA per
+//     value per bit;
+//   * the lane's 32 positions are exactly one sign word of the stateless hash
+//     (latent_weight_lab/block_fht.py:46-81): one hash per lane per layer,
+//     and the flip is a shift + XOR on the fp32 sign bit.
+// The chain is the reference's (block_fht.py:84-109): y_b = S_L H .. S_1 H S_0
+// pad(z) with the layers' 1/sqrt(B) applied once at the end (the backward is
+// the transposed chain, S_0 last, summed over blocks).
+//
+// Global memory moves in whole 16-byte chunks through a per-warp shared
+// buffer: lane l owns chunks 4l..4l+3 (16-bit) or 8l..8l+7 (fp32) of the tile,
+// the warp's global accesses are chunks l, l + 32, ... (512 contiguous bytes
+// per instruction).  swz() XORs the chunk index with bits 3..5 so both the
+// owner's and the streaming side's accesses are bank-conflict free.  Tiles
+// that straddle the slice's ends, or slices not aligned to a chunk, go element
+// by element (still lane-contiguous) with bounds tests.
+//
+// The forward's input is the same padded latent for every block, so each lane
+// loads its 32 latent values once per launch.  The backward keeps the lane's
+// 32 partial sums of the latent gradient in registers across its tiles; at
+// the end lanes and warps holding the same positions are summed in a fixed
+// order and each CTA writes one [L] row, which fhts_reduce_kernel adds up in a
+// fixed order (deterministic, like every backward in this library).
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+
+#include "fht_engine.h"
+#include "lwl_common.cuh"
+
+namespace lwl {
+namespace smallk {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = 32 * kWarps;
+constexpr int kTileLog = 10;
+constexpr int kMinLog = 5, kMaxLog = 10;
+constexpr int kBufBytes = 32 * 32 * 4;  // one warp tile in fp32 (16-bit tiles use half)
+
+struct SParams {
+  const void* src;  // forward: latent [L]; backward: gradient slice [stop - start]
+  void* dst;        // forward: output slice [stop - start]; backward: fp32 rows [gridDim.x][L]
+  int64_t L, start, stop;
+  int64_t t_first, ntiles;  // warp tiles (1024 coordinates) touched by [start, stop)
+  int layers;
+  uint32_t seed32;
+  float scale;  // B^(-layers/2)
+  int vec_ok;   // data pointer and slice start aligned to a 16-byte chunk
+};
+
+__device__ __forceinline__ int swz(int c) { return c ^ ((c >> 3) & 7); }
+
+// Sign layer: bit r of w set -> +1, clear -> -1 (block_fht.py:55-81).
+__device__ __forceinline__ void apply_sign(float (&v)[32], uint32_t w) {
+  const uint32_t nw = ~w;
+#pragma unroll
+  for (int r = 0; r < 32; ++r) v[r] = __int_as_float(__float_as_int(v[r]) ^ ((nw << (31 - r)) & 0x80000000u));
+}
+
+// Unnormalised H_32 over the register bits.
+__device__ __forceinline__ void fht_regs(float (&v)[32]) {
+#pragma unroll
+  for (int h = 1; h < 32; h <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (!(i & h)) {
+        const float a = v[i], b = v[i + h];
+        v[i] = a + b;
+        v[i + h] = a - b;
+      }
+    }
+  }
+}
+
+// Unnormalised butterflies over lane bits 0 .. N-6 (position bits 5 .. N-1):
+// the lane with the bit clear keeps a + b, the other b' = a - b.
+template <int N>
+__device__ __forceinline__ void fht_lanes(float (&v)[32], int lane) {
+#pragma unroll
+  for (int j = 0; j < N - 5; ++j) {
+    const int m = 1 << j;
+    const float s = (lane & m) ? -1.0f : 1.0f;
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      const float o = __shfl_xor_sync(0xffffffffu, v[r], m);
+      v[r] = fmaf(s, v[r], o);
+    }
+  }
+}
+
+template <typename T> struct Chunk;
+template <> struct Chunk<float> {
+  static constexpr int E = 4;  // elements per 16-byte chunk
+  static __device__ __forceinline__ uint4 pack(const float* v, float s) {
+    return make_uint4(__float_as_uint(v[0] * s), __float_as_uint(v[1] * s), __float_as_uint(v[2] * s),
+                      __float_as_uint(v[3] * s));
+  }
+  static __device__ __forceinline__ void unpack(uint4 c, float* v) {
+    v[0] = __uint_as_float(c.x);
+    v[1] = __uint_as_float(c.y);
+    v[2] = __uint_as_float(c.z);
+    v[3] = __uint_as_float(c.w);
+  }
+};
+template <typename H> struct Pair;
+template <> struct Pair<__nv_bfloat16> {
+  static __device__ __forceinline__ uint32_t pack(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  static __device__ __forceinline__ float2 unpack(uint32_t w) {
+    return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w));
+  }
+};
+template <> struct Pair<__half> {
+  static __device__ __forceinline__ uint32_t pack(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  static __device__ __forceinline__ float2 unpack(uint32_t w) { return __half22float2(*reinterpret_cast<__half2*>(&w)); }
+};
+template <typename H> struct Chunk16 {
+  static constexpr int E = 8;
+  static __device__ __forceinline__ uint4 pack(const float* v, float s) {
+    return make_uint4(Pair<H>::pack(v[0] * s, v[1] * s), Pair<H>::pack(v[2] * s, v[3] * s),
+                      Pair<H>::pack(v[4] * s, v[5] * s), Pair<H>::pack(v[6] * s, v[7] * s));
+  }
+  static __device__ __forceinline__ void unpack(uint4 c, float* v) {
+    const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = Pair<H>::unpack(w[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+};
+template <> struct Chunk<__nv_bfloat16> : Chunk16<__nv_bfloat16> {};
+template <> struct Chunk<__half> : Chunk16<__half> {};
+
+template <typename T, int N>
+__global__ void __launch_bounds__(kThreads) fhts_forward_kernel(const __grid_constant__ SParams P) {
+  __shared__ __align__(16) unsigned char sbuf[kWarps][kBufBytes];
+  constexpr int E = Chunk<T>::E, CPT = 32 / E;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lp = lane & ((1 << (N - 5)) - 1);  // position bits 5 .. N-1
+  unsigned char* wb = sbuf[warp];
+  float zin[32];
+  {
+    const T* z = reinterpret_cast<const T*>(P.src);
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      const int p = 32 * lp + r;
+      zin[r] = p < P.L ? Cvt<T>::to_f(z[p]) : 0.0f;
+    }
+  }
+  T* out = reinterpret_cast<T*>(P.dst);
+  const int64_t nw = (int64_t)gridDim.x * kWarps;
+  for (int64_t t = (int64_t)blockIdx.x * kWarps + warp; t < P.ntiles; t += nw) {
+    const int64_t base = (P.t_first + t) << kTileLog;
+    const int64_t blk = (base + 32 * lane) >> N;
+    float v[32];
+#pragma unroll
+    for (int r = 0; r < 32; ++r) v[r] = zin[r];
+    apply_sign(v, sign_word(block_layer_key(P.seed32, blk, 0), lp));
+    for (int l = 1; l <= P.layers; ++l) {
+      fht_regs(v);
+      fht_lanes<N>(v, lane);
+      apply_sign(v, sign_word(block_layer_key(P.seed32, blk, l), lp));
+    }
+    __syncwarp();  // the previous tile's reads of the buffer are done
+#pragma unroll
+    for (int q = 0; q < CPT; ++q)
+      *reinterpret_cast<uint4*>(wb + 16 * swz(CPT * lane + q)) = Chunk<T>::pack(v + E * q, P.scale);
+    __syncwarp();
+    if (P.vec_ok && base >= P.start && base + (1 << kTileLog) <= P.stop) {
+      uint4* dst = reinterpret_cast<uint4*>(out + (base - P.start));
+#pragma unroll
+      for (int k = 0; k < CPT; ++k) {
+        const int c = lane + 32 * k;
+        dst[c] = *reinterpret_cast<const uint4*>(wb + 16 * swz(c));
+      }
+    } else {
+      const T* tb = reinterpret_cast<const T*>(wb);
+      for (int k = 0; k < 32; ++k) {
+        const int e = lane + 32 * k;
+        const int64_t gi = base + e;
+        if (gi >= P.start && gi < P.stop) out[gi - P.start] = tb[E * swz(e / E) + (e % E)];
+      }
+    }
+  }
+}
+
+template <typename T, int N>
+__global__ void __launch_bounds__(kThreads) fhts_backward_kernel(const __grid_constant__ SParams P) {
+  constexpr int B = 1 << N;
+  constexpr int kRedBytes = kWarps * B * 4;
+  __shared__ __align__(16) unsigned char sbuf[kWarps * kBufBytes > kRedBytes ? kWarps * kBufBytes : kRedBytes];
+  constexpr int E = Chunk<T>::E, CPT = 32 / E;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lp = lane & ((1 << (N - 5)) - 1);
+  unsigned char* wb = sbuf + warp * kBufBytes;
+  const T* g = reinterpret_cast<const T*>(P.src);
+  float acc[32];
+#pragma unroll
+  for (int r = 0; r < 32; ++r) acc[r] = 0.0f;
+  const int64_t nw = (int64_t)gridDim.x * kWarps;
+  for (int64_t t = (int64_t)blockIdx.x * kWarps + warp; t < P.ntiles; t += nw) {
+    const int64_t base = (P.t_first + t) << kTileLog;
+    const int64_t blk = (base + 32 * lane) >> N;
+    __syncwarp();  // the previous tile's reads of the buffer are done
+    if (P.vec_ok && base >= P.start && base + (1 << kTileLog) <= P.stop) {
+      const uint4* src = reinterpret_cast<const uint4*>(g + (base - P.start));
+      uint4 c[CPT];
+#pragma unroll
+      for (int k = 0; k < CPT; ++k) c[k] = __ldcs(src + lane + 32 * k);
+#pragma unroll
+      for (int k = 0; k < CPT; ++k) *reinterpret_cast<uint4*>(wb + 16 * swz(lane + 32 * k)) = c[k];
+    } else {
+      T* tb = reinterpret_cast<T*>(wb);
+      for (int k = 0; k < 32; ++k) {
+        const int e = lane + 32 * k;
+        const int64_t gi = base + e;
+        tb[E * swz(e / E) + (e % E)] = (gi >= P.start && gi < P.stop) ? g[gi - P.start] : Cvt<T>::from_f(0.0f);
+      }
+    }
+    __syncwarp();
+    float v[32];
+#pragma unroll
+    for (int q = 0; q < CPT; ++q)
+      Chunk<T>::unpack(*reinterpret_cast<const uint4*>(wb + 16 * swz(CPT * lane + q)), v + E * q);
+    apply_sign(v, sign_word(block_layer_key(P.seed32, blk, P.layers), lp));
+    for (int l = P.layers - 1; l >= 0; --l) {
+      fht_regs(v);
+      fht_lanes<N>(v, lane);
+      apply_sign(v, sign_word(block_layer_key(P.seed32, blk, l), lp));
+    }
+#pragma unroll
+    for (int r = 0; r < 32; ++r) acc[r] += v[r];
+  }
+  // lanes that differ only in the block-select bits hold the same positions
+#pragma unroll
+  for (int m = 1 << (N - 5); m < 32; m <<= 1) {
+#pragma unroll
+    for (int r = 0; r < 32; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], m);
+  }
+  __syncthreads();
+  float* red = reinterpret_cast<float*>(sbuf);  // [kWarps][B]
+  if (lane < (B >> 5)) {
+#pragma unroll
+    for (int r = 0; r < 32; ++r) red[warp * B + 32 * lane + r] = acc[r];
+  }
+  __syncthreads();
+  float* row = reinterpret_cast<float*>(P.dst) + (int64_t)blockIdx.x * P.L;
+  for (int p = threadIdx.x; p < P.L; p += kThreads) {
+    float s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) s += red[w * B + p];
+    row[p] = s * P.scale;
+  }
+}
+
+template <typename T>
+__global__ void fhts_reduce_kernel(const float* __restrict__ rows, int nrows, int64_t L, T* __restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < L; i += (int64_t)gridDim.x * blockDim.x) {
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // four loads in flight, fixed summation order
+    int r = 0;
+    for (; r + 4 <= nrows; r += 4) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc[u] += rows[(int64_t)(r + u) * L + i];
+    }
+    for (; r < nrows; ++r) acc[0] += rows[(int64_t)r * L + i];
+    out[i] = Cvt<T>::from_f((acc[0] + acc[1]) + (acc[2] + acc[3]));
+  }
+}
+
+template <typename T, bool BWD, int N>
+const void* kernel_n() {
+  return BWD ? (const void*)fhts_backward_kernel<T, N> : (const void*)fhts_forward_kernel<T, N>;
+}
+template <typename T, bool BWD>
+const void* kernel_t(int n) {
+  switch (n) {
+    case 5: return kernel_n<T, BWD, 5>();
+    case 6: return kernel_n<T, BWD, 6>();
+    case 7: return kernel_n<T, BWD, 7>();
+    case 8: return kernel_n<T, BWD, 8>();
+    case 9: return kernel_n<T, BWD, 9>();
+    default: return kernel_n<T, BWD, 10>();
+  }
+}
+const void* kernel_of(int dtype, bool bwd, int n) {
+  if (dtype == LWL_F32) return bwd ? kernel_t<float, true>(n) : kernel_t<float, false>(n);
+  if (dtype == LWL_BF16) return bwd ? kernel_t<__nv_bfloat16, true>(n) : kernel_t<__nv_bfloat16, false>(n);
+  return bwd ? kernel_t<__half, true>(n) : kernel_t<__half, false>(n);
+}
+
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+// Persistent grid: every SM holds as many CTAs as fit, capped by the tiles.
+int grid_of(const void* k, int64_t ntiles) {
+  int per_sm = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, 0) != cudaSuccess || per_sm < 1) per_sm = 1;
+  const int64_t need = (ntiles + kWarps - 1) / kWarps;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(need, (int64_t)sm_count() * per_sm));
+}
+
+void make_params(const FhtArgs& a, SParams& p) {
+  std::memset(&p, 0, sizeof(p));
+  const int n = ilog2(next_pow2(a.latent_size));
+  p.src = a.in;
+  p.dst = a.out;
+  p.L = a.latent_size;
+  p.start = a.start;
+  p.stop = a.stop;
+  p.t_first = a.start >> kTileLog;
+  p.ntiles = a.stop > a.start ? ((a.stop - 1) >> kTileLog) - p.t_first + 1 : 0;
+  p.layers = a.layers;
+  p.seed32 = fold_seed(a.seed);
+  p.scale = (float)std::pow((double)(int64_t(1) << n), -0.5 * a.layers);
+  const int64_t E = 16 / (int64_t)dtype_bytes(a.dtype);
+  const void* data = a.backward ? a.in : a.out;
+  p.vec_ok = (a.start % E == 0) && ((reinterpret_cast<uintptr_t>(data) & 15) == 0);
+}
+
+}  // namespace smallk
+
+bool fhts_supported(int dtype, int64_t L, bool backward, int layers, unsigned flags) {
+  // fp32 arithmetic throughout, so LWL_FLAG_EXACT is honoured as well.
+  // LWL_SMALL_KERNEL=0 / =1 turns the kernel off / on for every size it
+  // handles (measurement only).
+  static const int mode = [] {
+    const char* e = std::getenv("LWL_SMALL_KERNEL");
+    return e ? std::atoi(e) : -1;
+  }();
+  if (mode == 0) return false;
+  const int n = ilog2(next_pow2(L));
+  if (n < smallk::kMinLog || n > smallk::kMaxLog) return false;
+  if (mode == 1) return true;
+  // fp32 (and the exact mode): faster than the fp32 whole-block kernel at every
+  // size here.  16-bit: faster than the tensor-core tile kernel while the
+  // lane-bit shuffles stay few (measured per size and layer count on B200).
+  if (dtype == LWL_F32 || (flags & LWL_FLAG_EXACT)) return true;
+  const int maxn = layers == 1 ? (backward ? 10 : 9) : 8;
+  return n <= maxn;
+}
+
+size_t fhts_workspace_bytes(const FhtArgs& a) {
+  if (!a.backward || a.stop <= a.start) return 0;
+  smallk::SParams p;
+  smallk::make_params(a, p);
+  const int n = ilog2(next_pow2(a.latent_size));
+  const int grid = smallk::grid_of(smallk::kernel_of(a.dtype, true, n), p.ntiles);
+  return size_t(grid) * size_t(a.latent_size) * 4;
+}
+
+int fhts_launches(const FhtArgs& a) {
+  if (a.stop <= a.start) return 0;
+  return a.backward ? 2 : 1;
+}
+
+int fhts_run(const FhtArgs& a, cudaStream_t st) {
+  using namespace smallk;
+  if (a.stop <= a.start) {
+    if (a.backward) LWL_CUDA_TRY(cudaMemsetAsync(a.out, 0, size_t(a.latent_size) * dtype_bytes(a.dtype), st));
+    return LWL_OK;
+  }
+  SParams p;
+  make_params(a, p);
+  const int n = ilog2(next_pow2(a.latent_size));
+  const void* k = kernel_of(a.dtype, a.backward, n);
+  const int grid = grid_of(k, p.ntiles);
+  if (a.backward) {
+    const size_t need = size_t(grid) * size_t(a.latent_size) * 4;
+    if (!a.workspace || a.workspace_bytes < need) {
+      set_error("workspace of %zu bytes required, %zu given", need, a.workspace ? a.workspace_bytes : (size_t)0);
+      return LWL_ERR_WORKSPACE;
+    }
+    p.dst = a.workspace;
+  }
+  void* args[] = {&p};
+  if (cudaLaunchKernel(k, dim3(grid), dim3(kThreads), args, 0, st) != cudaSuccess) {
+    set_error("small-block transform launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    return LWL_ERR_CUDA;
+  }
+  if (a.backward) {
+    const int threads = 256;
+    const int blocks = (int)std::min<int64_t>((a.latent_size + threads - 1) / threads, 1024);
+    const float* rows = reinterpret_cast<const float*>(a.workspace);
+    if (a.dtype == LWL_BF16)
+      fhts_reduce_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>(rows, grid, a.latent_size,
+                                                                     reinterpret_cast<__nv_bfloat16*>(a.out));
+    else if (a.dtype == LWL_F16)
+      fhts_reduce_kernel<__half><<<blocks, threads, 0, st>>>(rows, grid, a.latent_size, reinterpret_cast<__half*>(a.out));
+    else
+      fhts_reduce_kernel<float><<<blocks, threads, 0, st>>>(rows, grid, a.latent_size, reinterpret_cast<float*>(a.out));
+    LWL_CUDA_TRY(cudaGetLastError());
+  }
+  return LWL_OK;
+}
+
+}  // namespace lwl

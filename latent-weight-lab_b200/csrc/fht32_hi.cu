@@ -15,8 +15,9 @@
 // is one residency with no exchange, and every warp load and store covers 32
 // consecutive positions.  Each thread holds 64 values in flight.
 //
-// Sources: the latent, the gradient slice or the fp32 workspace; sink: the
-// fp32 workspace (16-bit plans always end with a low pass).  Blocks wholly
+// Sources: the latent, the gradient slice or the workspace; sink: the
+// workspace (16-bit plans always end with a low pass).  The workspace is fp32,
+// or bf16 in the forward plans that keep a bf16 workspace (fht_engine.cu).  Blocks wholly
 // inside the gradient slice load without bounds tests: with a 64-bit range
 // test on every element this launch ran at half the speed of the tile engine.  Signs and the
 // 1/sqrt(B) of each post-sign follow the plan's slots exactly as the tile
@@ -28,7 +29,7 @@
 namespace lwl {
 namespace f32k {
 
-template <typename T, int H, int SRC>
+template <typename T, int H, int SRC, typename W>
 __global__ void __launch_bounds__(Tile<13>::kThreads, Tile<13>::kMinBlocks)
     fht_hi_kernel(const __grid_constant__ TileParams p) {
   using Tl = Tile<13>;
@@ -56,11 +57,11 @@ __global__ void __launch_bounds__(Tile<13>::kThreads, Tile<13>::kMinBlocks)
     const int lo_b = base & ((1 << LOW) - 1);
     const int64_t rowoff = (b - p.first_block) * p.B;
     if (SRC == SRC_WS) {
-      const float* s = reinterpret_cast<const float*>(p.src) + rowoff + pos0 + lo_b;
+      const W* s = reinterpret_cast<const W*>(p.src) + rowoff + pos0 + lo_b;
 #pragma unroll
       for (int r = 0; r < kRegs; ++r) {
         const int t = spread<13, SC>(r);
-        v[r] = s[(t & ((1 << LOW) - 1)) + ((int64_t)(t >> LOW) << 15)];
+        v[r] = Cvt<W>::to_f(s[(t & ((1 << LOW) - 1)) + ((int64_t)(t >> LOW) << 15)]);
       }
     } else if (SRC == SRC_LATENT) {
       const T* s = reinterpret_cast<const T*>(p.src);
@@ -104,11 +105,11 @@ __global__ void __launch_bounds__(Tile<13>::kThreads, Tile<13>::kMinBlocks)
         }
       }
     }
-    float* d = reinterpret_cast<float*>(p.dst) + rowoff + pos0 + lo_b;
+    W* d = reinterpret_cast<W*>(p.dst) + rowoff + pos0 + lo_b;
 #pragma unroll
     for (int r = 0; r < kRegs; ++r) {
       const int t = spread<13, SC>(r);
-      d[(t & ((1 << LOW) - 1)) + ((int64_t)(t >> LOW) << 15)] = v[r];
+      d[(t & ((1 << LOW) - 1)) + ((int64_t)(t >> LOW) << 15)] = Cvt<W>::from_f(v[r]);
     }
   }
 }
@@ -118,14 +119,14 @@ __global__ void __launch_bounds__(Tile<13>::kThreads, Tile<13>::kMinBlocks)
 // every run's group of high bits lies in the registers of set B (tile bits
 // 6..11) or set C (the top six); the runs execute in plan order and the tile
 // moves between B and C through shared memory when the next group needs it.
-template <typename T, int TB, int SET, int SRC>
+template <typename T, int TB, int SET, int SRC, typename W>
 __device__ __forceinline__ void hi2_load(float (&v)[kRegs], const TileParams& p, int64_t b, int64_t pos0, int base) {
   constexpr int LOW = 7;
   auto off = [](int t) { return (int64_t)(t & ((1 << LOW) - 1)) + ((int64_t)(t >> LOW) << 15); };
   if (SRC == SRC_WS) {
-    const float* s = reinterpret_cast<const float*>(p.src) + (b - p.first_block) * p.B + pos0 + off(base);
+    const W* s = reinterpret_cast<const W*>(p.src) + (b - p.first_block) * p.B + pos0 + off(base);
 #pragma unroll
-    for (int r = 0; r < kRegs; ++r) v[r] = s[off(spread<TB, SET>(r))];
+    for (int r = 0; r < kRegs; ++r) v[r] = Cvt<W>::to_f(s[off(spread<TB, SET>(r))]);
   } else if (SRC == SRC_LATENT) {
     const T* s = reinterpret_cast<const T*>(p.src);
 #pragma unroll
@@ -148,17 +149,17 @@ __device__ __forceinline__ void hi2_load(float (&v)[kRegs], const TileParams& p,
   }
 }
 
-template <int TB, int SET>
+template <int TB, int SET, typename W>
 __device__ __forceinline__ void hi2_store(const float (&v)[kRegs], const TileParams& p, int64_t b, int64_t pos0,
                                           int base) {
   constexpr int LOW = 7;
   auto off = [](int t) { return (int64_t)(t & ((1 << LOW) - 1)) + ((int64_t)(t >> LOW) << 15); };
-  float* d = reinterpret_cast<float*>(p.dst) + (b - p.first_block) * p.B + pos0 + off(base);
+  W* d = reinterpret_cast<W*>(p.dst) + (b - p.first_block) * p.B + pos0 + off(base);
 #pragma unroll
-  for (int r = 0; r < kRegs; ++r) d[off(spread<TB, SET>(r))] = v[r];
+  for (int r = 0; r < kRegs; ++r) d[off(spread<TB, SET>(r))] = Cvt<W>::from_f(v[r]);
 }
 
-template <typename T, int H, int SRC>
+template <typename T, int H, int SRC, typename W>
 __global__ void __launch_bounds__(Tile<7 + H>::kThreads, 1) fht_hi2_kernel(const __grid_constant__ TileParams p) {
   constexpr int TB = 7 + H;
   using Tl = Tile<TB>;
@@ -184,8 +185,8 @@ __global__ void __launch_bounds__(Tile<7 + H>::kThreads, 1) fht_hi2_kernel(const
     }
     __syncthreads();
     bool in_c = (group_mask(0) & ~MASKC) == 0;  // start in the set of the first run's group
-    if (in_c) hi2_load<T, TB, SC, SRC>(v, p, b, pos0, bC);
-    else hi2_load<T, TB, SB, SRC>(v, p, b, pos0, bB);
+    if (in_c) hi2_load<T, TB, SC, SRC, W>(v, p, b, pos0, bC);
+    else hi2_load<T, TB, SB, SRC, W>(v, p, b, pos0, bB);
     if (p.pre_slot >= 0) {
       if (in_c) apply_sign<TB, SC>(v, sw + p.pre_slot * Tl::kWords, bC);
       else apply_sign<TB, SB>(v, sw + p.pre_slot * Tl::kWords, bB);
@@ -213,30 +214,33 @@ __global__ void __launch_bounds__(Tile<7 + H>::kThreads, 1) fht_hi2_kernel(const
         }
       }
     }
-    if (in_c) hi2_store<TB, SC>(v, p, b, pos0, bC);
-    else hi2_store<TB, SB>(v, p, b, pos0, bB);
+    if (in_c) hi2_store<TB, SC, W>(v, p, b, pos0, bC);
+    else hi2_store<TB, SB, W>(v, p, b, pos0, bB);
   }
 }
 
-template <typename T, int SRC>
+template <typename T, int SRC, typename W>
 const void* hi_kernel_h(int h) {
   switch (h) {
-    case 1: return (const void*)fht_hi_kernel<T, 1, SRC>;
-    case 2: return (const void*)fht_hi_kernel<T, 2, SRC>;
-    case 3: return (const void*)fht_hi_kernel<T, 3, SRC>;
-    case 4: return (const void*)fht_hi_kernel<T, 4, SRC>;
-    case 5: return (const void*)fht_hi_kernel<T, 5, SRC>;
-    case 6: return (const void*)fht_hi_kernel<T, 6, SRC>;
-    case 7: return (const void*)fht_hi2_kernel<T, 7, SRC>;
-    default: return (const void*)fht_hi2_kernel<T, 8, SRC>;
+    case 1: return (const void*)fht_hi_kernel<T, 1, SRC, W>;
+    case 2: return (const void*)fht_hi_kernel<T, 2, SRC, W>;
+    case 3: return (const void*)fht_hi_kernel<T, 3, SRC, W>;
+    case 4: return (const void*)fht_hi_kernel<T, 4, SRC, W>;
+    case 5: return (const void*)fht_hi_kernel<T, 5, SRC, W>;
+    case 6: return (const void*)fht_hi_kernel<T, 6, SRC, W>;
+    case 7: return (const void*)fht_hi2_kernel<T, 7, SRC, W>;
+    default: return (const void*)fht_hi2_kernel<T, 8, SRC, W>;
   }
 }
 
+// W: the workspace element (fp32, or bf16 for the forward plans that keep a
+// bf16 workspace; those read the latent or the workspace, never a slice).
 template <typename T>
-const void* hi_kernel(int src, int h) {
-  if (src == SRC_WS) return hi_kernel_h<T, SRC_WS>(h);
-  if (src == SRC_LATENT) return hi_kernel_h<T, SRC_LATENT>(h);
-  return hi_kernel_h<T, SRC_SLICE>(h);
+const void* hi_kernel(int src, int h, bool ws16) {
+  if (ws16) return src == SRC_WS ? hi_kernel_h<T, SRC_WS, __nv_bfloat16>(h) : hi_kernel_h<T, SRC_LATENT, __nv_bfloat16>(h);
+  if (src == SRC_WS) return hi_kernel_h<T, SRC_WS, float>(h);
+  if (src == SRC_LATENT) return hi_kernel_h<T, SRC_LATENT, float>(h);
+  return hi_kernel_h<T, SRC_SLICE, float>(h);
 }
 
 }  // namespace f32k
@@ -271,9 +275,10 @@ int fht_hi_launch(int dtype, const TileParams& p_in, cudaStream_t st) {
   p.ntiles = p.nblocks << (h <= 6 ? h + 2 : 8);
   const int threads = 1 << (tb - 6);
   const size_t smem = h <= 6 ? 0 : (tb == 14 ? Tile<14>::kSmem : Tile<15>::kSmem);
-  const void* k = dtype == LWL_BF16 ? hi_kernel<__nv_bfloat16>(p.src_kind, h)
-                : dtype == LWL_F16  ? hi_kernel<__half>(p.src_kind, h)
-                                    : hi_kernel<float>(p.src_kind, h);
+  const bool ws16 = p.ws16 != 0 && dtype != LWL_F32;
+  const void* k = dtype == LWL_BF16 ? hi_kernel<__nv_bfloat16>(p.src_kind, h, ws16)
+                : dtype == LWL_F16  ? hi_kernel<__half>(p.src_kind, h, ws16)
+                                    : hi_kernel<float>(p.src_kind, h, false);
   if (smem > 0 && !set_max_smem(k, (int)smem)) return -1;
   int per_sm = 1;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, threads, smem) != cudaSuccess || per_sm < 1)

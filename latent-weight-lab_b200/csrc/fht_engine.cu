@@ -11,6 +11,7 @@
 //    pass: layers+1 launches over an fp32 workspace of #blocks * B.
 // The backward runs the transposed chain (reversed sign layers) and reduces
 // the per-block results over blocks deterministically (reduce_rows_kernel).
+#include <cstdlib>
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
@@ -269,6 +270,23 @@ int plan_fht(const FhtArgs& a, FhtPlan& plan) {
   }
   plan.ws_bytes = size_t(nblk) * size_t(B) * 4;
   if (bwd) plan.partial_rows = nblk;
+  // bf16 workspace: bf16 forward plans whose every launch is a tensor-core
+  // low pass or a register-resident high pass (both read and write it).  The
+  // backward keeps fp32 for its block sums, and fp16 keeps fp32 because its
+  // unnormalised intermediates can leave the fp16 range.  One more bf16
+  // rounding per launch: rel-L2 3.4e-3 at 2^23 against 1.8e-3.  LWL_WS16=0 keeps
+  // fp32 (measurement only).
+  static const bool ws16_env = [] {
+    const char* e = std::getenv("LWL_WS16");
+    return !(e && e[0] == '0');
+  }();
+  bool ws16 = ws16_env && !bwd && use_lo && a.dtype == LWL_BF16;
+  for (int i = 0; ws16 && i < plan.nlaunch; ++i)
+    if (!plan.launches[i].p.lo && !fht_hi_eligible(a.dtype, plan.launches[i].p)) ws16 = false;
+  if (ws16) {
+    for (int i = 0; i < plan.nlaunch; ++i) plan.launches[i].p.ws16 = 1;
+    plan.ws_bytes = size_t(nblk) * size_t(B) * 2;
+  }
   return 0;
 }
 
@@ -289,6 +307,10 @@ int run_plan_t(const FhtArgs& a, FhtPlan& plan, cudaStream_t st) {
   if (plan.nblocks <= 0) {
     if (a.backward) LWL_CUDA_TRY(cudaMemsetAsync(a.out, 0, size_t(a.latent_size) * sizeof(T), st));
     return LWL_OK;
+  }
+  if (plan.launches[0].p.ws16 && (reinterpret_cast<uintptr_t>(a.workspace) & 15) != 0) {
+    set_error("the workspace of this call must be 16-byte aligned");
+    return LWL_ERR_INVALID;
   }
   for (int i = 0; i < plan.nlaunch; ++i) {
     TileLaunch& l = plan.launches[i];

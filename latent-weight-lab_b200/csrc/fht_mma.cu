@@ -1374,6 +1374,11 @@ __device__ __forceinline__ void lo_prefetch_next(const TileParams& p, int64_t ti
   }
 }
 
+constexpr size_t kSmemLo = 2 * kB * 2 + 4 * kWordsPad * 4;
+constexpr size_t kSmemLo16 = kSmemLo + kB * 2;  // with the bulk-copy stage
+static_assert(kSmemLo16 <= 232448, "shared memory per CTA");
+static_assert(kSmemLo % 16 == 0, "bulk-copy stage alignment");
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_constant__ TileParams p, float corr1) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -1397,11 +1402,46 @@ __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_consta
   const int mid = nseg == 2 ? p.lo_seg_slot[0] : -1;
   (void)corr1;  // the 2^-0.5 per application is folded into the exact 2^7 below
 
+  // bf16 workspace source: each tile (64 KB, contiguous) arrives by one bulk
+  // copy into `stage`, issued one tile ahead by thread 0; the waits are
+  // bounded, and a wait that gives up turns every later tile of the CTA into
+  // NaN (so the failure shows in the result) with no copy issued after it.
+  const bool bulk = p.ws16 && p.src_kind == SRC_WS;
+  uint16_t* stage16 = reinterpret_cast<uint16_t*>(smem + kSmemLo);
+  __shared__ __align__(8) uint64_t lo_mbar;
+  __shared__ int lo_abort;
+  const uint32_t mbar_s = (uint32_t)__cvta_generic_to_shared(&lo_mbar);
+  const uint32_t stage_s = (uint32_t)__cvta_generic_to_shared(stage16);
+  auto issue = [&](int64_t tl) {
+    const int64_t bb = p.first_block + tl / tpb;
+    const __nv_bfloat16* src =
+        reinterpret_cast<const __nv_bfloat16*>(p.src) + (bb - p.first_block) * p.B + ((tl % tpb) << kLog);
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(mbar_s), "r"((uint32_t)(kB * 2)));
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(stage_s),
+        "l"(src), "r"((uint32_t)(kB * 2)), "r"(mbar_s)
+        : "memory");
+  };
+  if (tid == 0) {
+    lo_abort = 0;
+    if (bulk) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(mbar_s));
+      asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+  }
+  __syncthreads();
+  bool inflight = false;  // thread 0: a bulk copy was issued and not yet waited for
+  uint32_t phase = 0;
+  if (bulk && tid == 0 && blockIdx.x < ntiles) {
+    issue(blockIdx.x);
+    inflight = true;
+  }
+
   for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const int64_t b = p.first_block + tile / tpb;
     const int j = (int)(tile % tpb);
     const int64_t tbase = (int64_t)j << kLog;  // first position of the tile in its block
-    if (tid == 0 && tile + gridDim.x < ntiles) lo_prefetch_next<T>(p, tile + gridDim.x, tpb);
+    if (!bulk && tid == 0 && tile + gridDim.x < ntiles) lo_prefetch_next<T>(p, tile + gridDim.x, tpb);
     __syncthreads();
     for (int i = tid; i < p.nslots * kWords; i += kThreads) {
       int sl = i / kWords, wd = i - sl * kWords;
@@ -1410,8 +1450,39 @@ __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_consta
     // the tile's 8 chunks of 8 per thread, all loads in flight at once, and
     // their largest magnitude; the values stay in registers for the landing
     float v[8][8];
+    if (bulk) {
+      uint32_t done = 0;
+      if (!lo_abort) {
+        for (int it = 0; it < (1 << 22) && !done; ++it) {
+          asm volatile(
+              "{\n .reg .pred q;\n mbarrier.try_wait.parity.shared::cta.b64 q, [%1], %2;\n selp.u32 %0, 1, 0, q;\n}\n"
+              : "=r"(done)
+              : "r"(mbar_s), "r"(phase)
+              : "memory");
+        }
+        if (!done) {
+          lo_abort = 1;  // the copy of parity `phase` may still land: waited for at the end
+        } else {
+          if (tid == 0) inflight = false;
+          phase ^= 1u;
+        }
+      }
+      const float bad = __int_as_float(0x7fc00000);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) lo_load8<T>(p, b, tbase + 8 * (tid + kThreads * i), v[i]);
+      for (int i = 0; i < 8; ++i) {
+        const uint4 raw = reinterpret_cast<const uint4*>(stage16)[tid + kThreads * i];
+        const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv[e]));
+          v[i][2 * e] = done ? f2.x : bad;
+          v[i][2 * e + 1] = done ? f2.y : bad;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) lo_load8<T>(p, b, tbase + 8 * (tid + kThreads * i), v[i]);
+    }
     float mx = 0.0f;
 #pragma unroll
     for (int i = 0; i < 8; ++i)
@@ -1421,6 +1492,12 @@ __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_consta
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if (lane == 0) red[w] = mx;
     __syncthreads();
+    // the stage is consumed: fetch the CTA's next tile while this one runs
+    if (bulk && tid == 0 && !lo_abort && tile + gridDim.x < ntiles) {
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      issue(tile + gridDim.x);
+      inflight = true;
+    }
     if (tid == 0) {
       float s = 0.0f;
       for (int i = 0; i < kThreads / 32; ++i) s = fmaxf(s, red[i]);
@@ -1464,7 +1541,13 @@ __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_consta
     float scale = ldexpf(1.0f, k0 + 7 * nseg);
     for (int sg = 0; sg < nseg; ++sg)
       if (p.lo_seg_slot[sg] >= 0) scale *= p.scale;
-    if (p.dst_kind == DST_SLICE) {
+    if (p.dst_kind == DST_WS && p.ws16) {
+      // bf16 workspace: the staged copy-out of the slice path, into the tile's
+      // 64 KB of the workspace (tile index counted from the plan's first block)
+      run_final<__nv_bfloat16>(f, xb, yb, ybuf, post >= 0 ? sw + post * kWordsPad : nullptr, scale,
+                               reinterpret_cast<__nv_bfloat16*>(p.dst), (b - p.first_block) * tpb + j, 0,
+                               p.nblocks * p.B, true, w, lane, g, t);
+    } else if (p.dst_kind == DST_SLICE) {
       // the post sign is always present on the final launch of a forward
       run_final<T>(f, xb, yb, ybuf, sw + post * kWordsPad, scale, reinterpret_cast<T*>(p.dst), b * (p.B >> kLog) + j,
                    p.start, p.stop, ((p.start & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.dst) & 15) == 0), w,
@@ -1513,9 +1596,19 @@ __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_consta
       }
     }
   }
+  if (bulk && tid == 0 && inflight) {
+    // after a wait gave up: let the outstanding copy land before the CTA exits (bounded)
+    uint32_t done = 0;
+    for (int it = 0; it < (1 << 22) && !done; ++it) {
+      asm volatile(
+          "{\n .reg .pred q;\n mbarrier.try_wait.parity.shared::cta.b64 q, [%1], %2;\n selp.u32 %0, 1, 0, q;\n}\n"
+          : "=r"(done)
+          : "r"(mbar_s), "r"(phase)
+          : "memory");
+    }
+  }
 }
 
-constexpr size_t kSmemLo = 2 * kB * 2 + 4 * kWordsPad * 4;
 
 }  // namespace fmma
 
@@ -1694,12 +1787,14 @@ int mma_lo_grid(const TileParams& p) {
 
 int mma_lo_launch(int dtype, const TileParams& p, int grid, cudaStream_t st) {
   const float corr1 = (float)fmma::layer_correction(fmma::kLog);
+  // + the bulk-copy stage when the bf16 workspace is the source
+  const size_t smem = fmma::kSmemLo + ((p.ws16 && p.src_kind == SRC_WS) ? size_t(fmma::kB) * 2 : 0);
   if (dtype == LWL_BF16) {
-    if (!set_max_smem((const void*)fmma::fht_lo_kernel<__nv_bfloat16>, (int)fmma::kSmemLo)) return -1;
-    fmma::fht_lo_kernel<__nv_bfloat16><<<grid, fmma::kThreads, fmma::kSmemLo, st>>>(p, corr1);
+    if (!set_max_smem((const void*)fmma::fht_lo_kernel<__nv_bfloat16>, (int)fmma::kSmemLo16)) return -1;
+    fmma::fht_lo_kernel<__nv_bfloat16><<<grid, fmma::kThreads, smem, st>>>(p, corr1);
   } else {
-    if (!set_max_smem((const void*)fmma::fht_lo_kernel<__half>, (int)fmma::kSmemLo)) return -1;
-    fmma::fht_lo_kernel<__half><<<grid, fmma::kThreads, fmma::kSmemLo, st>>>(p, corr1);
+    if (!set_max_smem((const void*)fmma::fht_lo_kernel<__half>, (int)fmma::kSmemLo16)) return -1;
+    fmma::fht_lo_kernel<__half><<<grid, fmma::kThreads, smem, st>>>(p, corr1);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }

@@ -410,7 +410,7 @@ __device__ __forceinline__ void run_final(const Frags& f, uint32_t in_base, uint
     o[k][1] = pack_out<T>(c[2] * scale, c[3] * scale);
     o[k][2] = pack_out<T>(c[4] * scale, c[5] * scale);
     o[k][3] = pack_out<T>(c[6] * scale, c[7] * scale);
-    sign_acc<0>(o[k], sw, w, k, g, t);
+    if (sw) sign_acc<0>(o[k], sw, w, k, g, t);  // sw == nullptr: no sign layer here
   }
 #pragma unroll
   for (int j = 0; j < 4; ++j) {

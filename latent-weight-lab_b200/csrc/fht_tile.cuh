@@ -60,6 +60,10 @@ struct TileParams {
   int lo;           // 1: run on fht_lo_kernel (16-bit), 2: on fht32_lo_kernel (fp32 math), instead of fht_tile_kernel
   int lo_nseg;      // 1 or 2 applications of the 2^15 transform
   int lo_seg_slot[2];  // sign slot after each application, -1 = none
+  // bf16 forward plans whose launches all run on fht_lo_kernel / fht_hi_kernel:
+  // the workspace holds bf16 instead of fp32 (2 bytes per coordinate each way)
+  // and the low pass streams its workspace tiles by bulk copy, one tile ahead.
+  int ws16;
 };
 
 __device__ __forceinline__ int pad_idx(int t) { return t + (t >> 5); }

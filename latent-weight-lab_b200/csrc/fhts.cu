@@ -24,7 +24,9 @@
 // by element (still lane-contiguous) with bounds tests.
 //
 // The forward's input is the same padded latent for every block, so each lane
-// loads its 32 latent values once per launch.  The backward keeps the lane's
+// loads its 32 latent values once per launch (with the layers' 1/sqrt(B)
+// folded in).  The backward streams its gradient tiles into two buffers per
+// warp by cp.async, one tile ahead of the transform, and keeps the lane's
 // 32 partial sums of the latent gradient in registers across its tiles; at
 // the end lanes and warps holding the same positions are summed in a fixed
 // order and each CTA writes one [L] row, which fhts_reduce_kernel adds up in a
@@ -53,7 +55,7 @@ struct SParams {
   int64_t t_first, ntiles;  // warp tiles (1024 coordinates) touched by [start, stop)
   int layers;
   uint32_t seed32;
-  float scale;  // B^(-layers/2)
+  float scale;  // B^(-layers/2): the forward multiplies the latent by it, the backward its sums
   int vec_ok;   // data pointer and slice start aligned to a 16-byte chunk
 };
 
@@ -100,9 +102,8 @@ __device__ __forceinline__ void fht_lanes(float (&v)[32], int lane) {
 template <typename T> struct Chunk;
 template <> struct Chunk<float> {
   static constexpr int E = 4;  // elements per 16-byte chunk
-  static __device__ __forceinline__ uint4 pack(const float* v, float s) {
-    return make_uint4(__float_as_uint(v[0] * s), __float_as_uint(v[1] * s), __float_as_uint(v[2] * s),
-                      __float_as_uint(v[3] * s));
+  static __device__ __forceinline__ uint4 pack(const float* v) {
+    return make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3]));
   }
   static __device__ __forceinline__ void unpack(uint4 c, float* v) {
     v[0] = __uint_as_float(c.x);
@@ -130,9 +131,9 @@ template <> struct Pair<__half> {
 };
 template <typename H> struct Chunk16 {
   static constexpr int E = 8;
-  static __device__ __forceinline__ uint4 pack(const float* v, float s) {
-    return make_uint4(Pair<H>::pack(v[0] * s, v[1] * s), Pair<H>::pack(v[2] * s, v[3] * s),
-                      Pair<H>::pack(v[4] * s, v[5] * s), Pair<H>::pack(v[6] * s, v[7] * s));
+  static __device__ __forceinline__ uint4 pack(const float* v) {
+    return make_uint4(Pair<H>::pack(v[0], v[1]), Pair<H>::pack(v[2], v[3]), Pair<H>::pack(v[4], v[5]),
+                      Pair<H>::pack(v[6], v[7]));
   }
   static __device__ __forceinline__ void unpack(uint4 c, float* v) {
     const uint32_t w[4] = {c.x, c.y, c.z, c.w};
@@ -160,7 +161,7 @@ __global__ void __launch_bounds__(kThreads) fhts_forward_kernel(const __grid_con
 #pragma unroll
     for (int r = 0; r < 32; ++r) {
       const int p = 32 * lp + r;
-      zin[r] = p < P.L ? Cvt<T>::to_f(z[p]) : 0.0f;
+      zin[r] = p < P.L ? Cvt<T>::to_f(z[p]) * P.scale : 0.0f;  // the layers' 1/sqrt(B), once
     }
   }
   T* out = reinterpret_cast<T*>(P.dst);
@@ -180,7 +181,7 @@ __global__ void __launch_bounds__(kThreads) fhts_forward_kernel(const __grid_con
     __syncwarp();  // the previous tile's reads of the buffer are done
 #pragma unroll
     for (int q = 0; q < CPT; ++q)
-      *reinterpret_cast<uint4*>(wb + 16 * swz(CPT * lane + q)) = Chunk<T>::pack(v + E * q, P.scale);
+      *reinterpret_cast<uint4*>(wb + 16 * swz(CPT * lane + q)) = Chunk<T>::pack(v + E * q);
     __syncwarp();
     if (P.vec_ok && base >= P.start && base + (1 << kTileLog) <= P.stop) {
       uint4* dst = reinterpret_cast<uint4*>(out + (base - P.start));
@@ -200,32 +201,58 @@ __global__ void __launch_bounds__(kThreads) fhts_forward_kernel(const __grid_con
   }
 }
 
+// Shared memory of the backward: two tile buffers per warp (the next tile's
+// chunks arrive by cp.async while the current one is transformed); the same
+// bytes serve the final cross-warp sums.
+template <typename T, int N>
+constexpr int bwd_smem() {
+  return 2 * kWarps * 32 * 32 * (int)sizeof(T) > kWarps * (1 << N) * 4 ? 2 * kWarps * 32 * 32 * (int)sizeof(T)
+                                                                        : kWarps * (1 << N) * 4;
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+               "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
+
 template <typename T, int N>
 __global__ void __launch_bounds__(kThreads) fhts_backward_kernel(const __grid_constant__ SParams P) {
   constexpr int B = 1 << N;
-  constexpr int kRedBytes = kWarps * B * 4;
-  __shared__ __align__(16) unsigned char sbuf[kWarps * kBufBytes > kRedBytes ? kWarps * kBufBytes : kRedBytes];
+  constexpr int TileBytes = 32 * 32 * (int)sizeof(T);
+  extern __shared__ __align__(16) unsigned char sbuf[];
   constexpr int E = Chunk<T>::E, CPT = 32 / E;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int lp = lane & ((1 << (N - 5)) - 1);
-  unsigned char* wb = sbuf + warp * kBufBytes;
+  unsigned char* wb0 = sbuf + warp * 2 * TileBytes;
   const T* g = reinterpret_cast<const T*>(P.src);
+  auto fast = [&](int64_t base) { return P.vec_ok && base >= P.start && base + (1 << kTileLog) <= P.stop; };
+  // whole tiles inside the slice: 16-byte chunks straight into the buffer
+  auto issue = [&](int64_t t, unsigned char* wb) {
+    const int64_t base = (P.t_first + t) << kTileLog;
+    if (t < P.ntiles && fast(base)) {
+      const uint4* src = reinterpret_cast<const uint4*>(g + (base - P.start));
+#pragma unroll
+      for (int k = 0; k < CPT; ++k) cp_async16(wb + 16 * swz(lane + 32 * k), src + lane + 32 * k);
+    }
+    cp_async_commit();
+  };
   float acc[32];
 #pragma unroll
   for (int r = 0; r < 32; ++r) acc[r] = 0.0f;
   const int64_t nw = (int64_t)gridDim.x * kWarps;
-  for (int64_t t = (int64_t)blockIdx.x * kWarps + warp; t < P.ntiles; t += nw) {
+  int buf = 0;
+  const int64_t t0 = (int64_t)blockIdx.x * kWarps + warp;
+  issue(t0, wb0);
+  for (int64_t t = t0; t < P.ntiles; t += nw, buf ^= 1) {
     const int64_t base = (P.t_first + t) << kTileLog;
     const int64_t blk = (base + 32 * lane) >> N;
-    __syncwarp();  // the previous tile's reads of the buffer are done
-    if (P.vec_ok && base >= P.start && base + (1 << kTileLog) <= P.stop) {
-      const uint4* src = reinterpret_cast<const uint4*>(g + (base - P.start));
-      uint4 c[CPT];
-#pragma unroll
-      for (int k = 0; k < CPT; ++k) c[k] = __ldcs(src + lane + 32 * k);
-#pragma unroll
-      for (int k = 0; k < CPT; ++k) *reinterpret_cast<uint4*>(wb + 16 * swz(lane + 32 * k)) = c[k];
-    } else {
+    unsigned char* wb = wb0 + buf * TileBytes;
+    issue(t + nw, wb0 + (buf ^ 1) * TileBytes);  // the other buffer was released at the end of the last tile
+    cp_async_wait1();                            // this tile's chunks have landed
+    if (!fast(base)) {
       T* tb = reinterpret_cast<T*>(wb);
       for (int k = 0; k < 32; ++k) {
         const int e = lane + 32 * k;
@@ -238,6 +265,7 @@ __global__ void __launch_bounds__(kThreads) fhts_backward_kernel(const __grid_co
 #pragma unroll
     for (int q = 0; q < CPT; ++q)
       Chunk<T>::unpack(*reinterpret_cast<const uint4*>(wb + 16 * swz(CPT * lane + q)), v + E * q);
+    __syncwarp();  // every lane is done with this buffer
     apply_sign(v, sign_word(block_layer_key(P.seed32, blk, P.layers), lp));
     for (int l = P.layers - 1; l >= 0; --l) {
       fht_regs(v);
@@ -247,6 +275,7 @@ __global__ void __launch_bounds__(kThreads) fhts_backward_kernel(const __grid_co
 #pragma unroll
     for (int r = 0; r < 32; ++r) acc[r] += v[r];
   }
+  asm volatile("cp.async.wait_all;\n" ::: "memory");  // nothing of this CTA may still be landing
   // lanes that differ only in the block-select bits hold the same positions
 #pragma unroll
   for (int m = 1 << (N - 5); m < 32; m <<= 1) {
@@ -287,6 +316,21 @@ template <typename T, bool BWD, int N>
 const void* kernel_n() {
   return BWD ? (const void*)fhts_backward_kernel<T, N> : (const void*)fhts_forward_kernel<T, N>;
 }
+template <typename T>
+int bwd_smem_t(int n) {
+  switch (n) {
+    case 5: return bwd_smem<T, 5>();
+    case 6: return bwd_smem<T, 6>();
+    case 7: return bwd_smem<T, 7>();
+    case 8: return bwd_smem<T, 8>();
+    case 9: return bwd_smem<T, 9>();
+    default: return bwd_smem<T, 10>();
+  }
+}
+int smem_of(int dtype, bool bwd, int n) {
+  if (!bwd) return 0;
+  return dtype == LWL_F32 ? bwd_smem_t<float>(n) : bwd_smem_t<__half>(n);
+}
 template <typename T, bool BWD>
 const void* kernel_t(int n) {
   switch (n) {
@@ -311,9 +355,11 @@ int sm_count() {
 }
 
 // Persistent grid: every SM holds as many CTAs as fit, capped by the tiles.
-int grid_of(const void* k, int64_t ntiles) {
+int grid_of(const void* k, int smem, int64_t ntiles) {
   int per_sm = 1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, 0) != cudaSuccess || per_sm < 1) per_sm = 1;
+  if (smem > 0 && !set_max_smem(k, smem)) return -1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
   const int64_t need = (ntiles + kWarps - 1) / kWarps;
   return (int)std::max<int64_t>(1, std::min<int64_t>(need, (int64_t)sm_count() * per_sm));
 }
@@ -363,8 +409,8 @@ size_t fhts_workspace_bytes(const FhtArgs& a) {
   smallk::SParams p;
   smallk::make_params(a, p);
   const int n = ilog2(next_pow2(a.latent_size));
-  const int grid = smallk::grid_of(smallk::kernel_of(a.dtype, true, n), p.ntiles);
-  return size_t(grid) * size_t(a.latent_size) * 4;
+  const int grid = smallk::grid_of(smallk::kernel_of(a.dtype, true, n), smallk::smem_of(a.dtype, true, n), p.ntiles);
+  return grid > 0 ? size_t(grid) * size_t(a.latent_size) * 4 : 0;
 }
 
 int fhts_launches(const FhtArgs& a) {
@@ -382,7 +428,12 @@ int fhts_run(const FhtArgs& a, cudaStream_t st) {
   make_params(a, p);
   const int n = ilog2(next_pow2(a.latent_size));
   const void* k = kernel_of(a.dtype, a.backward, n);
-  const int grid = grid_of(k, p.ntiles);
+  const int smem = smem_of(a.dtype, a.backward, n);
+  const int grid = grid_of(k, smem, p.ntiles);
+  if (grid < 0) {
+    set_error("small-block transform: kernel setup failed: %s", cudaGetErrorString(cudaGetLastError()));
+    return LWL_ERR_CUDA;
+  }
   if (a.backward) {
     const size_t need = size_t(grid) * size_t(a.latent_size) * 4;
     if (!a.workspace || a.workspace_bytes < need) {
@@ -392,7 +443,7 @@ int fhts_run(const FhtArgs& a, cudaStream_t st) {
     p.dst = a.workspace;
   }
   void* args[] = {&p};
-  if (cudaLaunchKernel(k, dim3(grid), dim3(kThreads), args, 0, st) != cudaSuccess) {
+  if (cudaLaunchKernel(k, dim3(grid), dim3(kThreads), args, (size_t)smem, st) != cudaSuccess) {
     set_error("small-block transform launch failed: %s", cudaGetErrorString(cudaGetLastError()));
     return LWL_ERR_CUDA;
   }

@@ -162,6 +162,18 @@ def block_fht_linear_forward(input: torch.Tensor, latent: torch.Tensor, out_feat
     return out.reshape(*input.shape[:-1], int(out_features))
 
 
+_SIDE_STREAMS: dict = {}
+
+
+def _side_stream(device: torch.device) -> "torch.cuda.Stream":
+    """One extra CUDA stream per device for work that overlaps the caller's stream."""
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    st = _SIDE_STREAMS.get(key)
+    if st is None:
+        st = _SIDE_STREAMS[key] = torch.cuda.Stream(device=key)
+    return st
+
+
 class _BlockFHTLinearFn(torch.autograd.Function):
     """Linear layer whose weight is regenerated from the latent (block_fht.py:291-356)."""
 
@@ -193,16 +205,35 @@ class _BlockFHTLinearFn(torch.autograd.Function):
         grad_input = grad_latent = grad_bias = None
         g2 = grad_output.reshape(-1, out_features)
         x2 = input.reshape(-1, in_features)
-        if ctx.needs_input_grad[0]:
-            grad_input = g2.matmul(weight.to(dtype=grad_output.dtype)).reshape_as(input)
+
+        def project(grad_weight):
+            gl = _native.fht_backward(grad_weight.reshape(-1), latent.numel(), size, layers, seed, 0, size,
+                                      flags=ctx.flags)
+            if ctx.weight_scale != 1.0:
+                gl = gl * ctx.weight_scale
+            if ctx.modulation_alpha != 0.0:
+                gl = gl + 2.0 * ctx.modulation_alpha * latent * grad_weight.sum()
+            return gl
+
         if ctx.needs_input_grad[1]:
             grad_weight = g2.transpose(0, 1).to(dtype=latent.dtype).matmul(x2.to(dtype=latent.dtype))
-            grad_latent = _native.fht_backward(grad_weight.reshape(-1), latent.numel(), size, layers, seed, 0, size,
-                                               flags=ctx.flags)
-            if ctx.weight_scale != 1.0:
-                grad_latent = grad_latent * ctx.weight_scale
-            if ctx.modulation_alpha != 0.0:
-                grad_latent = grad_latent + 2.0 * ctx.modulation_alpha * latent * grad_weight.sum()
+            if ctx.needs_input_grad[0]:
+                # The latent projection (a few dozen CTAs at GPT widths) and the
+                # grad_input GEMM are independent: the projection runs on a side
+                # stream, forked after grad_W and joined before returning.
+                main = torch.cuda.current_stream(grad_weight.device)
+                side = _side_stream(grad_weight.device)
+                side.wait_stream(main)
+                with torch.cuda.stream(side):
+                    grad_latent = project(grad_weight)
+                grad_weight.record_stream(side)
+                grad_input = g2.matmul(weight.to(dtype=grad_output.dtype)).reshape_as(input)
+                main.wait_stream(side)
+                grad_latent.record_stream(main)
+            else:
+                grad_latent = project(grad_weight)
+        elif ctx.needs_input_grad[0]:
+            grad_input = g2.matmul(weight.to(dtype=grad_output.dtype)).reshape_as(input)
         if ctx.has_bias and ctx.needs_input_grad[2]:
             grad_bias = g2.sum(dim=0).to(dtype=grad_output.dtype)
         return grad_input, grad_latent, grad_bias, None, None, None, None, None, None, None

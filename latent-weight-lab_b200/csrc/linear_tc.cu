@@ -58,6 +58,7 @@ struct LinParams {
   const __nv_bfloat16* bias;      // [N] or null
   const __nv_bfloat16* out_gain;  // [N] or null
   const __nv_bfloat16* in_gain;   // [K] or null
+  const float* w_add;             // scalar added to every weight element (modulation), or null
   int64_t L;
   int n, layers;
   uint32_t seed32;
@@ -265,6 +266,15 @@ __global__ void __launch_bounds__(kLinThreads, 1)
               const uint4 s4 = src[u];
               v[4 * u] = s4.x, v[4 * u + 1] = s4.y, v[4 * u + 2] = s4.z, v[4 * u + 3] = s4.w;
             }
+            if (P.w_add) {  // the modulation offset, added to every element (block_fht.py:448-449)
+              const float c = __ldg(P.w_add);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const __nv_bfloat162 r = __floats2bfloat162_rn(__uint_as_float(v[j] << 16) + c,
+                                                               __uint_as_float(v[j] & 0xffff0000u) + c);
+                v[j] = (uint32_t)__bfloat16_as_ushort(r.x) | ((uint32_t)__bfloat16_as_ushort(r.y) << 16);
+              }
+            }
             if (P.in_gain) {  // W[:, k] * in_gain[k]: columns 64*c64 .. +63 of this row
               const uint32_t* ig = reinterpret_cast<const uint32_t*>(P.in_gain + 64 * c64);
 #pragma unroll
@@ -457,6 +467,7 @@ int tc_linear_launch(bool gen, const void* x, int T, int K, int N, const void* l
     P.bias = reinterpret_cast<const __nv_bfloat16*>(extras->bias);
     P.out_gain = reinterpret_cast<const __nv_bfloat16*>(extras->out_gain);
     P.in_gain = reinterpret_cast<const __nv_bfloat16*>(extras->in_gain);
+    P.w_add = extras->weight_offset;
   }
   P.L = L;
   P.n = gen ? ilog2(next_pow2(L)) : 15;

@@ -57,7 +57,7 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.lwl_linear_forward.argtypes = [ci, vp, i64, i64, vp, i64, i64, ci, u64, ctypes.c_float, vp, vp, sz, vp]
     lib.lwl_linear_forward_ex.restype = ci
     lib.lwl_linear_forward_ex.argtypes = [ci, vp, i64, i64, vp, i64, i64, ci, u64, ctypes.c_float, vp, vp, vp, vp, vp,
-                                          sz, vp]
+                                          vp, sz, vp]
     lib.lwl_linear_backward_workspace_bytes.restype = sz
     lib.lwl_linear_backward_workspace_bytes.argtypes = [ci, i64, i64, i64, i64, ci, cu]
     lib.lwl_linear_backward.restype = ci
@@ -283,10 +283,12 @@ def fht_backward_grouped(items, flags: int = 0) -> list[torch.Tensor]:
 
 def linear_forward(x2d: torch.Tensor, latent: torch.Tensor, out_features: int, layers: int, seed: int,
                    weight_scale: float = 1.0, return_status: bool = False, bias: torch.Tensor | None = None,
-                   output_gain: torch.Tensor | None = None, input_gain: torch.Tensor | None = None):
+                   output_gain: torch.Tensor | None = None, input_gain: torch.Tensor | None = None,
+                   weight_offset: torch.Tensor | None = None):
     """Fused tcgen05 forward y = x @ (scale * W)^T with W generated on chip;
-    optional bf16 bias / output_gain ([out]) and input_gain ([in]) are folded
-    into the kernel (lwl_linear_forward_ex).
+    optional bf16 bias / output_gain ([out]) and input_gain ([in]), and a
+    scalar weight_offset added to every weight element (the modulation term),
+    are folded into the kernel (lwl_linear_forward_ex).
 
     Returns None when the shape is outside the fused kernel (the caller then
     generates W and uses a library GEMM).  With return_status the device error
@@ -301,6 +303,8 @@ def linear_forward(x2d: torch.Tensor, latent: torch.Tensor, out_features: int, l
     ws = torch.empty(lib.lwl_linear_forward_workspace_bytes(), dtype=torch.uint8, device=x2d.device)
     extras = [None if v is None else v.detach().to(device=x2d.device, dtype=torch.bfloat16).contiguous()
               for v in (bias, output_gain, input_gain)]
+    extras.append(None if weight_offset is None else
+                  weight_offset.detach().to(device=x2d.device, dtype=torch.float32).reshape(1).contiguous())
     with torch.cuda.device(x2d.device):
         if any(v is not None for v in extras):
             st = lib.lwl_linear_forward_ex(dtype_code(x2d.dtype), x2d.data_ptr(), T, K, latent.data_ptr(),

@@ -375,8 +375,10 @@ class BlockFHTLinear(nn.Module):
 
     def _forward_fused_gains(self, input: torch.Tensor, weight_scale: float) -> torch.Tensor | None:
         # like the reference's materialised path (F.linear with self.weight),
-        # the call's weight_scale argument does not enter when gains are set
-        del weight_scale
+        # the call's weight_scale argument does not enter when gains are set;
+        # without gains it scales the generated part, as in block_fht.py:487-494
+        gains = self.output_gain is not None or self.input_gain is not None
+        scale = self.weight_scale if gains else weight_scale * self.weight_scale
         lat = self.generator.latent
         if not (input.is_cuda and input.dtype == torch.bfloat16 and lat.dtype == torch.bfloat16) or _flags():
             return None
@@ -384,30 +386,30 @@ class BlockFHTLinear(nn.Module):
         if flat.shape[0] == 0:
             return None
         with torch.no_grad():
+            # the modulation term (alpha * offset added to every weight element,
+            # block_fht.py:448-449) stays on the device as an fp32 scalar and is
+            # added to the generated panel on chip, under the gains like the
+            # reference's weight property
+            offset = (self.modulation_alpha * self._modulation_offset().float()
+                      if self.modulation_alpha != 0.0 else None)
             out = _native.linear_forward(flat, lat, self.out_features, self.generator.layers, self.generator.seed,
-                                         self.weight_scale, bias=self.bias,
-                                         output_gain=self.output_gain, input_gain=self.input_gain)
+                                         scale, bias=self.bias,
+                                         output_gain=self.output_gain, input_gain=self.input_gain,
+                                         weight_offset=offset)
             if out is None:
                 return None
-            if self.modulation_alpha != 0.0:
-                xg = flat if self.input_gain is None else flat * self.input_gain.to(dtype=flat.dtype)
-                mod = (self.modulation_alpha * self._modulation_offset()).to(dtype=out.dtype) * \
-                    xg.sum(dim=-1, keepdim=True)
-                if self.output_gain is not None:
-                    mod = mod * self.output_gain.to(dtype=out.dtype)
-                out = out + mod
         return out.reshape(*input.shape[:-1], self.out_features)
 
     def forward_fused(self, input: torch.Tensor, weight_scale: float = 1.0) -> torch.Tensor:
         """Inference forward without autograd (block_fht.py:482-501).
 
         With output/input gains the reference multiplies a materialised
-        weight; here, for bf16 layers the fused kernel takes, the gains and
-        the bias are folded into the on-chip panel and the epilogue instead
-        (the modulation term is added afterwards, scaled by the same gains).
+        weight; here, for bf16 layers the fused kernel takes, the gains, the
+        modulation offset and the bias are folded into the on-chip panel and
+        the epilogue instead.
         """
-        if (self.output_gain is not None or self.input_gain is not None) and self.spectral_core is None \
-                and self.residual_base_weight is None:
+        if (self.output_gain is not None or self.input_gain is not None or self.modulation_alpha != 0.0) \
+                and self.spectral_core is None and self.residual_base_weight is None:
             out = self._forward_fused_gains(input, weight_scale)
             if out is not None:
                 return out

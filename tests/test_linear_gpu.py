@@ -171,6 +171,36 @@ def test_forward_fused_with_gains_matches_materialised(native_lib, gains, alpha)
     assert rel_l2(y.float().cpu().numpy(), ref.cpu().numpy()) < 1e-2
 
 
+@pytest.mark.parametrize("centered", [False, True])
+def test_forward_fused_modulation_on_chip(native_lib, centered):
+    """The modulation term (alpha * offset added to every weight element,
+    block_fht.py:448-449) is added to the generated panel inside the fused
+    kernel; without gains the call's weight_scale scales the generated part
+    only, as in the reference's forward_fused (block_fht.py:482-501)."""
+    from latent_weight_lab import BlockFHTLinear, _native
+
+    torch.manual_seed(12)
+    layer = BlockFHTLinear(768, 3072, bias=True, latent_dim=32768, layers=3, seed=6, weight_scale=0.7,
+                           modulation_alpha=0.02, modulation_centered=centered).cuda().bfloat16()
+    with torch.no_grad():
+        layer.bias.copy_(torch.randn(3072) * 0.1)
+    x = torch.randn(2, 300, 768, device="cuda", dtype=torch.bfloat16)
+    calls = []
+    orig = _native.linear_forward
+    _native.linear_forward = lambda *a, **k: calls.append(k.get("weight_offset")) or orig(*a, **k)
+    try:
+        y = layer.forward_fused(x, weight_scale=0.5)
+    finally:
+        _native.linear_forward = orig
+    assert calls and calls[0] is not None, "the modulation offset did not reach the fused kernel"
+    with torch.no_grad():
+        gen = layer.generator().float().view(3072, 768)
+        c = (layer.modulation_alpha * layer._modulation_offset()).float()
+        w = 0.5 * 0.7 * gen + c
+        ref = torch.nn.functional.linear(x.float(), w, layer.bias.float())
+    assert rel_l2(y.float().cpu().numpy(), ref.cpu().numpy()) < 1e-2
+
+
 def test_mlp_step_replays_as_cuda_graph(native_lib):
     """Forward + backward through BlockFHTLinear (generation, GEMMs, latent
     projections) captured in one CUDA graph gives the eager gradients."""

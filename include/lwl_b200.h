@@ -201,18 +201,22 @@ int lwl_fixed_fht_mix(int dtype, const void* x, int64_t rows, int64_t features, 
 
 /* lwl_linear_forward with the module's extra terms folded in (bias, out_gain,
  * in_gain: bf16 device vectors or NULL; weight_offset: one fp32 device
- * scalar or NULL):
- *   y[:, n] = out_gain[n] * (x @ ((weight_scale * W + offset) * in_gain[None, :])^T)[:, n] + bias[n].
- * The offset (the modulation term alpha * sum(z^2) [- expected]) is added
- * to and the input gain scales the generated panel on chip, the output gain
- * and bias are applied in the epilogue.  Same shape limits as
- * lwl_linear_forward; in_gain and weight_offset 4-byte aligned.  Replaces:
- * the materialised weight (block_fht.py:444-462) and the torch modulation
- * and gain terms of BlockFHTLinear.forward_fused (block_fht.py:482-501). */
+ * scalar or NULL; base: a dense bf16 [out_features, in_features] residual
+ * base weight or NULL, with its factor base_scale):
+ *   V = weight_scale * W + offset;  V = base + base_scale * V if base;
+ *   y[:, n] = out_gain[n] * (x @ (V * in_gain[None, :])^T)[:, n] + bias[n].
+ * The offset (the modulation term alpha * sum(z^2) [- expected]), the base
+ * and the input gain are applied to the generated panel on chip, the output
+ * gain and bias in the epilogue: one GEMM where the reference runs two.
+ * Same shape limits as lwl_linear_forward; in_gain and weight_offset 4-byte
+ * aligned, base 16-byte aligned.  Replaces: the materialised weight
+ * (block_fht.py:444-462) and the torch modulation, residual-base and gain
+ * terms of BlockFHTLinear.forward_fused (block_fht.py:482-501). */
 int lwl_linear_forward_ex(int dtype, const void* x, int64_t tokens, int64_t in_features, const void* latent,
                           int64_t latent_size, int64_t out_features, int layers, uint64_t seed, float weight_scale,
                           const void* bias, const void* out_gain, const void* in_gain, const float* weight_offset,
-                          void* y, void* workspace, size_t workspace_bytes, void* stream);
+                          const void* base, float base_scale, void* y, void* workspace, size_t workspace_bytes,
+                          void* stream);
 
 /* Dense-weight variant of the same tcgen05 pipeline: y = x @ w^T with a given
  * bf16 w[out_features, in_features] (same shape limits).  No reference

@@ -612,19 +612,22 @@ int lwl_linear_forward(int dtype, const void* x, int64_t tokens, int64_t in_feat
 int lwl_linear_forward_ex(int dtype, const void* x, int64_t tokens, int64_t in_features, const void* latent,
                           int64_t latent_size, int64_t out_features, int layers, uint64_t seed, float weight_scale,
                           const void* bias, const void* out_gain, const void* in_gain, const float* weight_offset,
-                          void* y, void* workspace, size_t workspace_bytes, void* stream) {
+                          const void* base, float base_scale, void* y, void* workspace, size_t workspace_bytes,
+                          void* stream) {
   lwl::g_err[0] = 0;
   int st = linear_common(true, dtype, x, tokens, in_features, out_features, latent, latent_size, layers, y, workspace,
                          workspace_bytes);
   if (st) return st;
   if ((reinterpret_cast<uintptr_t>(in_gain) & 3) || (reinterpret_cast<uintptr_t>(out_gain) & 1) ||
-      (reinterpret_cast<uintptr_t>(bias) & 1) || (reinterpret_cast<uintptr_t>(weight_offset) & 3)) {
-    lwl::set_error("gain and bias vectors must be aligned bf16 arrays (in_gain: 4 bytes), weight_offset an fp32");
+      (reinterpret_cast<uintptr_t>(bias) & 1) || (reinterpret_cast<uintptr_t>(weight_offset) & 3) ||
+      (reinterpret_cast<uintptr_t>(base) & 15)) {
+    lwl::set_error("gain and bias vectors must be aligned bf16 arrays (in_gain: 4 bytes), weight_offset an fp32, "
+                   "base 16-byte aligned");
     return LWL_ERR_UNSUPPORTED;
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   LWL_CUDA_TRY(cudaMemsetAsync(workspace, 0, 16, s));
-  const lwl::LinExtras ex{bias, out_gain, in_gain, weight_offset};
+  const lwl::LinExtras ex{bias, out_gain, in_gain, weight_offset, base, base ? base_scale : 1.0f};
   int rc = lwl::tc_linear_launch(true, x, (int)tokens, (int)in_features, (int)out_features, latent, latent_size,
                                  layers, seed, weight_scale, nullptr, y, reinterpret_cast<int*>(workspace), s, &ex);
   if (rc) {

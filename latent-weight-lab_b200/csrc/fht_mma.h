@@ -43,12 +43,16 @@ int mma_lo_launch(int dtype, const TileParams& p, int grid, cudaStream_t st);
 // tcgen05 BlockFHTLinear forward (linear_tc.cu).
 bool tc_linear_supported(int K, int N, int T);
 // Optional terms of the fused linear (bf16 device vectors, an fp32 device
-// scalar, or null): y[:, n] = out_gain[n] * (x ((W + offset) * in_gain)^T)[:, n] + bias[n].
+// scalar, a dense bf16 [N, K] base weight, or null):
+//   y[:, n] = out_gain[n] * (x ((base + base_scale (W + offset)) * in_gain)^T)[:, n] + bias[n]
+// (without base: base_scale = 1 and no base term).
 struct LinExtras {
   const void* bias;
   const void* out_gain;
   const void* in_gain;
   const float* weight_offset;
+  const void* base;
+  float base_scale;
 };
 int tc_linear_launch(bool gen, const void* x, int T, int K, int N, const void* latent, int64_t L, int layers,
                      uint64_t seed, float wscale, const void* wdense, void* y, int* err, cudaStream_t st,

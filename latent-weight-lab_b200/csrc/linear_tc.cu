@@ -59,6 +59,8 @@ struct LinParams {
   const __nv_bfloat16* out_gain;  // [N] or null
   const __nv_bfloat16* in_gain;   // [K] or null
   const float* w_add;             // scalar added to every weight element (modulation), or null
+  const __nv_bfloat16* base;      // dense residual base weight [N, K], or null
+  float base_scale;               // the generated part's factor when base is set
   int64_t L;
   int n, layers;
   uint32_t seed32;
@@ -275,6 +277,22 @@ __global__ void __launch_bounds__(kLinThreads, 1)
                 v[j] = (uint32_t)__bfloat16_as_ushort(r.x) | ((uint32_t)__bfloat16_as_ushort(r.y) << 16);
               }
             }
+            if (P.base) {  // residual base: base + base_scale * W (block_fht.py:451-452)
+              const uint4* bsrc = reinterpret_cast<const uint4*>(P.base + (size_t)(n0 + m) * K + 64 * c64);
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                const uint4 b4 = __ldg(bsrc + u);
+                const uint32_t bw[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const uint32_t vv = v[4 * u + e];
+                  const __nv_bfloat162 r = __floats2bfloat162_rn(
+                      __uint_as_float(bw[e] << 16) + P.base_scale * __uint_as_float(vv << 16),
+                      __uint_as_float(bw[e] & 0xffff0000u) + P.base_scale * __uint_as_float(vv & 0xffff0000u));
+                  v[4 * u + e] = (uint32_t)__bfloat16_as_ushort(r.x) | ((uint32_t)__bfloat16_as_ushort(r.y) << 16);
+                }
+              }
+            }
             if (P.in_gain) {  // W[:, k] * in_gain[k]: columns 64*c64 .. +63 of this row
               const uint32_t* ig = reinterpret_cast<const uint32_t*>(P.in_gain + 64 * c64);
 #pragma unroll
@@ -468,6 +486,8 @@ int tc_linear_launch(bool gen, const void* x, int T, int K, int N, const void* l
     P.out_gain = reinterpret_cast<const __nv_bfloat16*>(extras->out_gain);
     P.in_gain = reinterpret_cast<const __nv_bfloat16*>(extras->in_gain);
     P.w_add = extras->weight_offset;
+    P.base = reinterpret_cast<const __nv_bfloat16*>(extras->base);
+    P.base_scale = extras->base_scale;
   }
   P.L = L;
   P.n = gen ? ilog2(next_pow2(L)) : 15;

@@ -57,7 +57,7 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.lwl_linear_forward.argtypes = [ci, vp, i64, i64, vp, i64, i64, ci, u64, ctypes.c_float, vp, vp, sz, vp]
     lib.lwl_linear_forward_ex.restype = ci
     lib.lwl_linear_forward_ex.argtypes = [ci, vp, i64, i64, vp, i64, i64, ci, u64, ctypes.c_float, vp, vp, vp, vp, vp,
-                                          vp, sz, vp]
+                                          ctypes.c_float, vp, vp, sz, vp]
     lib.lwl_linear_backward_workspace_bytes.restype = sz
     lib.lwl_linear_backward_workspace_bytes.argtypes = [ci, i64, i64, i64, i64, ci, cu]
     lib.lwl_linear_backward.restype = ci
@@ -284,11 +284,13 @@ def fht_backward_grouped(items, flags: int = 0) -> list[torch.Tensor]:
 def linear_forward(x2d: torch.Tensor, latent: torch.Tensor, out_features: int, layers: int, seed: int,
                    weight_scale: float = 1.0, return_status: bool = False, bias: torch.Tensor | None = None,
                    output_gain: torch.Tensor | None = None, input_gain: torch.Tensor | None = None,
-                   weight_offset: torch.Tensor | None = None):
+                   weight_offset: torch.Tensor | None = None, base: torch.Tensor | None = None,
+                   base_scale: float = 1.0):
     """Fused tcgen05 forward y = x @ (scale * W)^T with W generated on chip;
     optional bf16 bias / output_gain ([out]) and input_gain ([in]), and a
     scalar weight_offset added to every weight element (the modulation term),
-    are folded into the kernel (lwl_linear_forward_ex).
+    and a dense residual base weight ([out, in], the generated part scaled
+    by base_scale) are folded into the kernel (lwl_linear_forward_ex).
 
     Returns None when the shape is outside the fused kernel (the caller then
     generates W and uses a library GEMM).  With return_status the device error
@@ -305,13 +307,15 @@ def linear_forward(x2d: torch.Tensor, latent: torch.Tensor, out_features: int, l
               for v in (bias, output_gain, input_gain)]
     extras.append(None if weight_offset is None else
                   weight_offset.detach().to(device=x2d.device, dtype=torch.float32).reshape(1).contiguous())
+    extras.append(None if base is None else base.detach().to(device=x2d.device, dtype=torch.bfloat16).contiguous())
     with torch.cuda.device(x2d.device):
         if any(v is not None for v in extras):
             st = lib.lwl_linear_forward_ex(dtype_code(x2d.dtype), x2d.data_ptr(), T, K, latent.data_ptr(),
                                            latent.numel(), int(out_features), int(layers), _seed_u64(seed),
                                            float(weight_scale),
                                            *[v.data_ptr() if v is not None else None for v in extras],
-                                           y.data_ptr(), ws.data_ptr(), ws.numel(), _stream_ptr(x2d.device))
+                                           float(base_scale), y.data_ptr(), ws.data_ptr(), ws.numel(),
+                                           _stream_ptr(x2d.device))
         else:
             st = lib.lwl_linear_forward(dtype_code(x2d.dtype), x2d.data_ptr(), T, K, latent.data_ptr(),
                                         latent.numel(), int(out_features), int(layers), _seed_u64(seed),

@@ -373,7 +373,7 @@ class BlockFHTLinear(nn.Module):
                                        self.generator.size, self.generator.layers, self.generator.seed,
                                        self.weight_scale, self.modulation_alpha)
 
-    def _forward_fused_gains(self, input: torch.Tensor, weight_scale: float) -> torch.Tensor | None:
+    def _forward_fused_ex(self, input: torch.Tensor, weight_scale: float) -> torch.Tensor | None:
         # like the reference's materialised path (F.linear with self.weight),
         # the call's weight_scale argument does not enter when gains are set;
         # without gains it scales the generated part, as in block_fht.py:487-494
@@ -392,10 +392,12 @@ class BlockFHTLinear(nn.Module):
             # reference's weight property
             offset = (self.modulation_alpha * self._modulation_offset().float()
                       if self.modulation_alpha != 0.0 else None)
+            base = self.residual_base_weight
             out = _native.linear_forward(flat, lat, self.out_features, self.generator.layers, self.generator.seed,
                                          scale, bias=self.bias,
                                          output_gain=self.output_gain, input_gain=self.input_gain,
-                                         weight_offset=offset)
+                                         weight_offset=offset, base=base,
+                                         base_scale=self.residual_base_scale if base is not None else 1.0)
             if out is None:
                 return None
         return out.reshape(*input.shape[:-1], self.out_features)
@@ -404,13 +406,14 @@ class BlockFHTLinear(nn.Module):
         """Inference forward without autograd (block_fht.py:482-501).
 
         With output/input gains the reference multiplies a materialised
-        weight; here, for bf16 layers the fused kernel takes, the gains, the
-        modulation offset and the bias are folded into the on-chip panel and
-        the epilogue instead.
+        weight, and with a residual base it runs a second GEMM; here, for
+        bf16 layers the fused kernel takes, the gains, the modulation offset,
+        the residual base and the bias are folded into the on-chip panel and
+        the epilogue instead (one GEMM).
         """
-        if (self.output_gain is not None or self.input_gain is not None or self.modulation_alpha != 0.0) \
-                and self.spectral_core is None and self.residual_base_weight is None:
-            out = self._forward_fused_gains(input, weight_scale)
+        if (self.output_gain is not None or self.input_gain is not None or self.modulation_alpha != 0.0
+                or self.residual_base_weight is not None) and self.spectral_core is None:
+            out = self._forward_fused_ex(input, weight_scale)
             if out is not None:
                 return out
         if self.output_gain is not None or self.input_gain is not None or self.spectral_core is not None:

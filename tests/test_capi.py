@@ -90,8 +90,8 @@ def test_linear_backward_validation_without_gpu(native_lib):
 
 
 def test_linear_forward_ex_rejects_non_bf16(native_lib):
-    st = native_lib.lwl_linear_forward_ex(0, None, 4, 64, None, 100, 128, 3, 1, 1.0, None, None, None, None, None, None, 0,
-                                          None)
+    st = native_lib.lwl_linear_forward_ex(0, None, 4, 64, None, 100, 128, 3, 1, 1.0, None, None, None, None, None, 1.0,
+                                          None, None, 0, None)
     assert st == 2
     assert b"bf16" in native_lib.lwl_last_error()
 

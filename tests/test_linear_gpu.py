@@ -201,6 +201,43 @@ def test_forward_fused_modulation_on_chip(native_lib, centered):
     assert rel_l2(y.float().cpu().numpy(), ref.cpu().numpy()) < 1e-2
 
 
+@pytest.mark.parametrize("gains, alpha, ws", [(False, 0.0, 0.5), (False, 0.02, 1.0), (True, 0.02, 3.0)])
+def test_forward_fused_residual_base_one_gemm(native_lib, gains, alpha, ws):
+    """A residual-base layer (base + s * generated, block_fht.py:451-452) runs as
+    one fused GEMM: the base panel is added to the generated panel on chip.
+    Checked against the materialised weight (with gains the call's
+    weight_scale is ignored, as in the reference)."""
+    from latent_weight_lab import BlockFHTLinear, _native
+
+    torch.manual_seed(13)
+    layer = BlockFHTLinear(768, 1024, bias=True, latent_dim=32768, layers=3, seed=8, weight_scale=0.7,
+                           modulation_alpha=alpha, residual_base_scale=0.3, output_gain=gains,
+                           input_gain=gains).cuda().bfloat16()
+    with torch.no_grad():
+        layer.bias.copy_(torch.randn(1024) * 0.1)
+        if gains:
+            layer.output_gain.copy_(torch.rand(1024) + 0.5)
+            layer.input_gain.copy_(torch.rand(768) + 0.5)
+    x = torch.randn(500, 768, device="cuda", dtype=torch.bfloat16)
+    calls = []
+    orig = _native.linear_forward
+    _native.linear_forward = lambda *a, **k: calls.append(k.get("base")) or orig(*a, **k)
+    try:
+        y = layer.forward_fused(x, weight_scale=ws)
+    finally:
+        _native.linear_forward = orig
+    assert calls and calls[0] is not None, "the residual base did not reach the fused kernel"
+    with torch.no_grad():
+        if gains:
+            w = layer.weight.float()
+        else:
+            gen = layer.generator().float().view(1024, 768)
+            c = (alpha * layer._modulation_offset()).float() if alpha else 0.0
+            w = layer.residual_base_weight.float() + 0.3 * (ws * 0.7 * gen + c)
+        ref = torch.nn.functional.linear(x.float(), w, layer.bias.float())
+    assert rel_l2(y.float().cpu().numpy(), ref.cpu().numpy()) < 1e-2
+
+
 def test_mlp_step_replays_as_cuda_graph(native_lib):
     """Forward + backward through BlockFHTLinear (generation, GEMMs, latent
     projections) captured in one CUDA graph gives the eager gradients."""

@@ -46,7 +46,9 @@ constexpr int kWarps = 8;
 constexpr int kThreads = 32 * kWarps;
 constexpr int kTileLog = 10;
 constexpr int kMinLog = 5, kMaxLog = 10;
-constexpr int kBufBytes = 32 * 32 * 4;  // one warp tile in fp32 (16-bit tiles use half)
+constexpr int kXp = 10;                  // blocks of 2^10: lane bits by shared-memory transpose
+constexpr int kBufBytes = 32 * 33 * 4;   // per warp: one tile in fp32 (16-bit tiles use less), or the
+                                         // padded 32 x 33 transpose buffer
 
 struct SParams {
   const void* src;  // forward: latent [L]; backward: gradient slice [stop - start]
@@ -69,10 +71,11 @@ __device__ __forceinline__ void apply_sign(float (&v)[32], uint32_t w) {
   for (int r = 0; r < 32; ++r) v[r] = (w & (1u << r)) ? v[r] : -v[r];
 }
 
-// Unnormalised H_32 over the register bits.
+// Unnormalised H over register bits 0 .. NB-1.
+template <int NB = 5>
 __device__ __forceinline__ void fht_regs(float (&v)[32]) {
 #pragma unroll
-  for (int h = 1; h < 32; h <<= 1) {
+  for (int h = 1; h < (1 << NB); h <<= 1) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       if (!(i & h)) {
@@ -98,6 +101,54 @@ __device__ __forceinline__ void fht_lanes(float (&v)[32], int lane) {
       v[r] = fmaf(s, v[r], o);
     }
   }
+}
+
+// Blocks of 2^10 hold position bits 5..9 on all 5 lane bits, where a shuffle
+// per value per bit costs more than moving the tile once per layer (measured:
+// +8-17% at 2^10, and no gain at 2^9, whose 4 lane bits the shuffles keep):
+// the warp's 32 x 32 tile M (row = lane, 32 consecutive positions per row:
+// "orientation A") is transposed through a padded shared buffer, so that
+// lane b holds column b ("orientation B": v[r] = M[r][b], register bits =
+// position bits 5..9).  Both accesses of the buffer are bank-conflict free
+// ((lane + r) mod 32 distinct).  The transpose is its own inverse.
+__device__ __forceinline__ void xpose(float (&v)[32], float* tb, int lane) {
+  __syncwarp();
+#pragma unroll
+  for (int r = 0; r < 32; ++r) tb[lane * 33 + r] = v[r];
+  __syncwarp();
+#pragma unroll
+  for (int r = 0; r < 32; ++r) v[r] = tb[r * 33 + lane];
+}
+
+// 32 x 32 bit-matrix transpose across the warp: lane a holds word w_a on
+// entry; on exit lane b holds the word whose bit a is bit b of w_a (the sign
+// bits of column b in orientation B).  Recursive block swap, five shuffles.
+__device__ __forceinline__ uint32_t bit_xpose(uint32_t x, int lane) {
+  constexpr uint32_t lo[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
+#pragma unroll
+  for (int s = 0; s < 5; ++s) {
+    const int j = 16 >> s;
+    const uint32_t y = __shfl_xor_sync(0xffffffffu, x, j);
+    x = (lane & j) ? ((x & ~lo[s]) | ((y & ~lo[s]) >> j)) : ((x & lo[s]) | ((y & lo[s]) << j));
+  }
+  return x;
+}
+
+// One unnormalised H_B of a block of 2^N in the transpose scheme: the
+// register bits of the current orientation, the transpose, the register bits
+// of the other; returns the new orientation.
+template <int N>
+__device__ __forceinline__ int fht_xp(float (&v)[32], float* tb, int lane, int ori) {
+  if (ori == 0) {
+    fht_regs<5>(v);
+    xpose(v, tb, lane);
+    fht_regs<N - 5>(v);
+  } else {
+    fht_regs<N - 5>(v);
+    xpose(v, tb, lane);
+    fht_regs<5>(v);
+  }
+  return ori ^ 1;
 }
 
 template <typename T> struct Chunk;
@@ -156,12 +207,16 @@ __global__ void __launch_bounds__(kThreads) fhts_forward_kernel(const __grid_con
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int lp = lane & ((1 << (N - 5)) - 1);  // position bits 5 .. N-1
   unsigned char* wb = sbuf[warp];
+  constexpr bool XP = N >= kXp;
+  // transpose scheme: start in orientation B for odd layer counts, so that the
+  // last layer ends in A, whose rows of 32 consecutive positions are stored
+  const int ori0 = XP ? (P.layers & 1) : 0;
   float zin[32];
   {
     const T* z = reinterpret_cast<const T*>(P.src);
 #pragma unroll
     for (int r = 0; r < 32; ++r) {
-      const int p = 32 * lp + r;
+      const int p = ori0 ? ((32 * r + lane) & ((1 << N) - 1)) : 32 * lp + r;
       zin[r] = p < P.L ? Cvt<T>::to_f(z[p]) * P.scale : 0.0f;  // the layers' 1/sqrt(B), once
     }
   }
@@ -173,11 +228,23 @@ __global__ void __launch_bounds__(kThreads) fhts_forward_kernel(const __grid_con
     float v[32];
 #pragma unroll
     for (int r = 0; r < 32; ++r) v[r] = zin[r];
-    apply_sign(v, sign_word(block_layer_key(P.seed32, blk, 0), lp));
-    for (int l = 1; l <= P.layers; ++l) {
-      fht_regs(v);
-      fht_lanes<N>(v, lane);
-      apply_sign(v, sign_word(block_layer_key(P.seed32, blk, l), lp));
+    if (XP) {
+      float* tb = reinterpret_cast<float*>(wb);
+      int ori = ori0;
+      uint32_t w = sign_word(block_layer_key(P.seed32, blk, 0), lp);  // row `lane`'s word
+      apply_sign(v, ori ? bit_xpose(w, lane) : w);
+      for (int l = 1; l <= P.layers; ++l) {
+        ori = fht_xp<N>(v, tb, lane, ori);
+        w = sign_word(block_layer_key(P.seed32, blk, l), lp);
+        apply_sign(v, ori ? bit_xpose(w, lane) : w);
+      }
+    } else {
+      apply_sign(v, sign_word(block_layer_key(P.seed32, blk, 0), lp));
+      for (int l = 1; l <= P.layers; ++l) {
+        fht_regs(v);
+        fht_lanes<N>(v, lane);
+        apply_sign(v, sign_word(block_layer_key(P.seed32, blk, l), lp));
+      }
     }
     __syncwarp();  // the previous tile's reads of the buffer are done
 #pragma unroll
@@ -206,9 +273,13 @@ __global__ void __launch_bounds__(kThreads) fhts_forward_kernel(const __grid_con
 // chunks arrive by cp.async while the current one is transformed); the same
 // bytes serve the final cross-warp sums.
 template <typename T, int N>
+constexpr int bwd_tile_bytes() {  // one per-warp buffer: a tile, or the transpose buffer
+  return N >= kXp && kBufBytes > 32 * 32 * (int)sizeof(T) ? kBufBytes : 32 * 32 * (int)sizeof(T);
+}
+template <typename T, int N>
 constexpr int bwd_smem() {
-  return 2 * kWarps * 32 * 32 * (int)sizeof(T) > kWarps * (1 << N) * 4 ? 2 * kWarps * 32 * 32 * (int)sizeof(T)
-                                                                        : kWarps * (1 << N) * 4;
+  return 2 * kWarps * bwd_tile_bytes<T, N>() > kWarps * (1 << N) * 4 ? 2 * kWarps * bwd_tile_bytes<T, N>()
+                                                                     : kWarps * (1 << N) * 4;
 }
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -222,7 +293,8 @@ __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_g
 template <typename T, int N>
 __global__ void __launch_bounds__(kThreads) fhts_backward_kernel(const __grid_constant__ SParams P) {
   constexpr int B = 1 << N;
-  constexpr int TileBytes = 32 * 32 * (int)sizeof(T);
+  constexpr int TileBytes = bwd_tile_bytes<T, N>();  // a multiple of 16
+  constexpr bool XP = N >= kXp;
   extern __shared__ __align__(16) unsigned char sbuf[];
   constexpr int E = Chunk<T>::E, CPT = 32 / E;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -267,27 +339,53 @@ __global__ void __launch_bounds__(kThreads) fhts_backward_kernel(const __grid_co
     for (int q = 0; q < CPT; ++q)
       Chunk<T>::unpack(*reinterpret_cast<const uint4*>(wb + 16 * swz(CPT * lane + q)), v + E * q);
     __syncwarp();  // every lane is done with this buffer
-    apply_sign(v, sign_word(block_layer_key(P.seed32, blk, P.layers), lp));
-    for (int l = P.layers - 1; l >= 0; --l) {
-      fht_regs(v);
-      fht_lanes<N>(v, lane);
-      apply_sign(v, sign_word(block_layer_key(P.seed32, blk, l), lp));
+    if (XP) {
+      // the buffer is free until the next tile's issue: it serves the transposes
+      float* tb = reinterpret_cast<float*>(wb);
+      int ori = 0;
+      apply_sign(v, sign_word(block_layer_key(P.seed32, blk, P.layers), lp));
+      for (int l = P.layers - 1; l >= 0; --l) {
+        ori = fht_xp<N>(v, tb, lane, ori);
+        const uint32_t w = sign_word(block_layer_key(P.seed32, blk, l), lp);
+        apply_sign(v, ori ? bit_xpose(w, lane) : w);
+      }
+    } else {
+      apply_sign(v, sign_word(block_layer_key(P.seed32, blk, P.layers), lp));
+      for (int l = P.layers - 1; l >= 0; --l) {
+        fht_regs(v);
+        fht_lanes<N>(v, lane);
+        apply_sign(v, sign_word(block_layer_key(P.seed32, blk, l), lp));
+      }
     }
 #pragma unroll
     for (int r = 0; r < 32; ++r) acc[r] += v[r];
   }
   asm volatile("cp.async.wait_all;\n" ::: "memory");  // nothing of this CTA may still be landing
-  // lanes that differ only in the block-select bits hold the same positions
-#pragma unroll
-  for (int m = 1 << (N - 5); m < 32; m <<= 1) {
-#pragma unroll
-    for (int r = 0; r < 32; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], m);
-  }
-  __syncthreads();
   float* red = reinterpret_cast<float*>(sbuf);  // [kWarps][B]
-  if (lane < (B >> 5)) {
+  if (XP && (P.layers & 1)) {
+    // odd layer counts end in orientation B: lane b, register r holds position
+    // 32 (r mod B/32) + b; registers that differ in block-select bits are summed
 #pragma unroll
-    for (int r = 0; r < 32; ++r) red[warp * B + 32 * lane + r] = acc[r];
+    for (int m = B >> 5; m < 32; m <<= 1) {
+#pragma unroll
+      for (int r = 0; r < 32; ++r)
+        if (!(r & m)) acc[r] += acc[r | m];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < (B >> 5); ++r) red[warp * B + 32 * r + lane] = acc[r];
+  } else {
+    // lanes that differ only in the block-select bits hold the same positions
+#pragma unroll
+    for (int m = 1 << (N - 5); m < 32; m <<= 1) {
+#pragma unroll
+      for (int r = 0; r < 32; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], m);
+    }
+    __syncthreads();
+    if (lane < (B >> 5)) {
+#pragma unroll
+      for (int r = 0; r < 32; ++r) red[warp * B + 32 * lane + r] = acc[r];
+    }
   }
   __syncthreads();
   float* row = reinterpret_cast<float*>(P.dst) + (int64_t)blockIdx.x * P.L;
@@ -401,7 +499,7 @@ bool fhts_supported(int dtype, int64_t L, bool backward, int layers, unsigned fl
   // size here.  16-bit: faster than the tensor-core tile kernel while the
   // lane-bit shuffles stay few (measured per size and layer count on B200).
   if (dtype == LWL_F32 || (flags & LWL_FLAG_EXACT)) return true;
-  const int maxn = layers == 1 ? (backward ? 10 : 9) : 8;
+  const int maxn = layers == 1 ? 10 : 8;
   return n <= maxn;
 }
 

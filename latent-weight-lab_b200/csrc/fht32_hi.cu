@@ -281,11 +281,15 @@ const void* hi_kernel_h(int h) {
   }
 }
 
-// W: the workspace element (fp32, or bf16 for the forward plans that keep a
-// bf16 workspace; those read the latent or the workspace, never a slice).
+// W: the workspace element (fp32, or bf16 for the plans that keep a bf16
+// workspace).
 template <typename T>
 const void* hi_kernel(int src, int h, bool ws16) {
-  if (ws16) return src == SRC_WS ? hi_kernel_h<T, SRC_WS, __nv_bfloat16>(h) : hi_kernel_h<T, SRC_LATENT, __nv_bfloat16>(h);
+  if (ws16) {
+    if (src == SRC_WS) return hi_kernel_h<T, SRC_WS, __nv_bfloat16>(h);
+    if (src == SRC_LATENT) return hi_kernel_h<T, SRC_LATENT, __nv_bfloat16>(h);
+    return hi_kernel_h<T, SRC_SLICE, __nv_bfloat16>(h);
+  }
   if (src == SRC_WS) return hi_kernel_h<T, SRC_WS, float>(h);
   if (src == SRC_LATENT) return hi_kernel_h<T, SRC_LATENT, float>(h);
   return hi_kernel_h<T, SRC_SLICE, float>(h);

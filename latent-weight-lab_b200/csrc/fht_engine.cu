@@ -270,22 +270,28 @@ int plan_fht(const FhtArgs& a, FhtPlan& plan) {
   }
   plan.ws_bytes = size_t(nblk) * size_t(B) * 4;
   if (bwd) plan.partial_rows = nblk;
-  // bf16 workspace: bf16 forward plans whose every launch is a tensor-core
-  // low pass or a register-resident high pass (both read and write it).  The
-  // backward keeps fp32 for its block sums, and fp16 keeps fp32 because its
-  // unnormalised intermediates can leave the fp16 range.  One more bf16
-  // rounding per launch: rel-L2 3.4e-3 at 2^23 against 1.8e-3.  LWL_WS16=0 keeps
-  // fp32 (measurement only).
+  // bf16 workspace: bf16 plans whose every launch is a tensor-core low pass or
+  // a register-resident high pass (both read and write it).  The backward's
+  // last launch (a low pass) writes fp32 into a second region, which the
+  // block sum reads; fp16 keeps fp32 because its unnormalised intermediates
+  // can leave the fp16 range.  One more bf16 rounding per launch: rel-L2
+  // 3.4e-3 at 2^23 against 1.8e-3.  LWL_WS16=0 keeps fp32 (measurement only).
   static const bool ws16_env = [] {
     const char* e = std::getenv("LWL_WS16");
     return !(e && e[0] == '0');
   }();
-  bool ws16 = ws16_env && !bwd && use_lo && a.dtype == LWL_BF16;
+  bool ws16 = ws16_env && use_lo && a.dtype == LWL_BF16 && (!bwd || plan.launches[plan.nlaunch - 1].p.lo == 1);
   for (int i = 0; ws16 && i < plan.nlaunch; ++i)
     if (!plan.launches[i].p.lo && !fht_hi_eligible(a.dtype, plan.launches[i].p)) ws16 = false;
   if (ws16) {
     for (int i = 0; i < plan.nlaunch; ++i) plan.launches[i].p.ws16 = 1;
-    plan.ws_bytes = size_t(nblk) * size_t(B) * 2;
+    const size_t h = (size_t(nblk) * size_t(B) * 2 + 255) & ~size_t(255);
+    plan.ws_bytes = h;
+    if (bwd) {
+      plan.launches[plan.nlaunch - 1].p.ws_out32 = 1;
+      plan.f32_off = h;
+      plan.ws_bytes = h + size_t(nblk) * size_t(B) * 4;
+    }
   }
   return 0;
 }
@@ -317,7 +323,7 @@ int run_plan_t(const FhtArgs& a, FhtPlan& plan, cudaStream_t st) {
     TileParams& p = l.p;
     p.src = (p.src_kind == SRC_WS) ? a.workspace : a.in;
     if (p.dst_kind == DST_SLICE) p.dst = a.out;
-    else if (p.dst_kind == DST_WS) p.dst = a.workspace;
+    else if (p.dst_kind == DST_WS) p.dst = static_cast<char*>(a.workspace) + (p.ws_out32 ? plan.f32_off : 0);
     else p.partial = reinterpret_cast<float*>(a.workspace);
     if (p.lo == 2) {
       if (fht32_lo_launch(a.dtype, p, st) != 0) {
@@ -347,7 +353,8 @@ int run_plan_t(const FhtArgs& a, FhtPlan& plan, cudaStream_t st) {
     int64_t stride = plan.launches[0].p.dst_kind == DST_ACC ? a.latent_size : plan.B;
     int threads = 256;
     int64_t blocks = std::min<int64_t>((a.latent_size + threads - 1) / threads, 65535);
-    reduce_rows_kernel<T><<<(int)blocks, threads, 0, st>>>(reinterpret_cast<const float*>(a.workspace),
+    reduce_rows_kernel<T><<<(int)blocks, threads, 0, st>>>(
+        reinterpret_cast<const float*>(static_cast<const char*>(a.workspace) + plan.f32_off),
                                                             plan.partial_rows, stride, a.latent_size,
                                                             reinterpret_cast<T*>(a.out));
     LWL_CUDA_TRY(cudaGetLastError());

@@ -39,6 +39,7 @@ struct FhtPlan {
   TileLaunch launches[4];
   int64_t nblocks, B;
   int64_t partial_rows;  // backward: rows reduced into grad_latent
+  size_t f32_off;        // bf16 backward plans: byte offset of the fp32 region the last launch writes
   size_t ws_bytes;
 };
 

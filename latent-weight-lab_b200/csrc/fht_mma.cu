@@ -1541,7 +1541,7 @@ __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_consta
     float scale = ldexpf(1.0f, k0 + 7 * nseg);
     for (int sg = 0; sg < nseg; ++sg)
       if (p.lo_seg_slot[sg] >= 0) scale *= p.scale;
-    if (p.dst_kind == DST_WS && p.ws16) {
+    if (p.dst_kind == DST_WS && p.ws16 && !p.ws_out32) {
       // bf16 workspace: the staged copy-out of the slice path, into the tile's
       // 64 KB of the workspace (tile index counted from the plan's first block)
       run_final<__nv_bfloat16>(f, xb, yb, ybuf, post >= 0 ? sw + post * kWordsPad : nullptr, scale,

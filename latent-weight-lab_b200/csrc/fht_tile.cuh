@@ -64,6 +64,7 @@ struct TileParams {
   // the workspace holds bf16 instead of fp32 (2 bytes per coordinate each way)
   // and the low pass streams its workspace tiles by bulk copy, one tile ahead.
   int ws16;
+  int ws_out32;  // bf16 backward plans: this (last) launch writes its workspace output in fp32
 };
 
 __device__ __forceinline__ int pad_idx(int t) { return t + (t >> 5); }

@@ -266,9 +266,9 @@ def test_single_spike_bf16(nat, logb):
 # fp32 oracle math on the same rounded inputs, layers 3; 2^28-coordinate runs
 # have the same per-block error).  Measured on a B200: bf16 1.80e-3 / 1.80e-3
 # (fwd / bwd) at 2^15, 1.86e-3 / 1.85e-3 at 2^17, 1.81e-3 / 1.81e-3 at 2^23;
-# fp16 7.2e-4 / 7.1e-4, 9.1e-4 / 9.1e-4, 7.5e-4 / 7.5e-4.  The bf16 forward
-# of blocks above 2^17 keeps its workspace in bf16 (one more rounding per
-# launch): 3.39e-3 at 2^23.  bf16 is dominated
+# fp16 7.2e-4 / 7.1e-4, 9.1e-4 / 9.1e-4, 7.5e-4 / 7.5e-4.  bf16 blocks above
+# 2^17 keep their workspace in bf16 (one more rounding per launch): 3.39e-3
+# forward and backward at 2^23.  bf16 is dominated
 # by the final rounding to bf16 (relative RMS ~2^-9 / sqrt(3)).  The bounds
 # are regression guards at about 1.5x those values; the gate stays 1e-2.
 MARGIN_CASES = [
@@ -277,7 +277,7 @@ MARGIN_CASES = [
     (15, 16, torch.float16, 1.1e-3, 1.1e-3),
     (17, 4, torch.bfloat16, 2.8e-3, 2.8e-3),
     (17, 4, torch.float16, 1.4e-3, 1.4e-3),
-    (23, 1, torch.bfloat16, 4.5e-3, 2.7e-3),
+    (23, 1, torch.bfloat16, 4.5e-3, 4.5e-3),
     (23, 1, torch.float16, 1.2e-3, 1.2e-3),
 ]
 

@@ -5,7 +5,7 @@
  * stream (cudaStream_t passed as void*; NULL = legacy default stream).  The
  * library never allocates device memory: callers size scratch space with the
  * *_workspace_bytes queries and pass it in, 16-byte aligned (every cudaMalloc
- * or torch allocation is; some large-block forward plans require it).  Calls are stateless and
+ * or torch allocation is; the bf16 large-block plans require it).  Calls are stateless and
  * re-entrant; work is enqueued on the given stream and nothing synchronises
  * the host.  Every call returns an lwl_status; lwl_last_error() gives the
  * calling thread's message for the most recent failure.

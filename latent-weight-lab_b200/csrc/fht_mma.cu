@@ -1387,7 +1387,6 @@ __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_consta
   uint32_t* sw = reinterpret_cast<uint32_t*>(ybuf + kB);  // [slot][kWordsPad]
   float* fstage = reinterpret_cast<float*>(smem);          // X+Y as 32768 fp32 (final fp32 output)
   __shared__ float red[kThreads / 32];
-  __shared__ int k0_shared;
 
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
   Frags f;
@@ -1498,14 +1497,15 @@ __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_consta
       issue(tile + gridDim.x);
       inflight = true;
     }
-    if (tid == 0) {
+    // every thread forms the prescale exponent from the warp maxima (same
+    // order everywhere, so all agree; no second barrier).  red is rewritten
+    // only after the next tile's loop-top barrier.
+    int k0;
+    {
       float s = 0.0f;
       for (int i = 0; i < kThreads / 32; ++i) s = fmaxf(s, red[i]);
-      int e = prescale_exponent(s, kLog);
-      k0_shared = e;
+      k0 = prescale_exponent(s, kLog);
     }
-    __syncthreads();
-    const int k0 = k0_shared;
     const float in_scale = ldexpf(1.0f, -k0);
     uint16_t* land = nseg == 1 ? ybuf : xbuf;
 #pragma unroll

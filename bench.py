@@ -471,6 +471,35 @@ def measure_mlp_pair(dev, world: int, steps: int, warmup: int) -> dict:
             h.copy_(d, non_blocking=True)
 
     ms_e2e = timed(e2e_step, max(3, steps // 2))
+
+    # the same step on the reference's training path (block_fht.py:560-569):
+    # both weights generated by one grouped launch, both latent projections by
+    # one grouped launch (prepare_ / flush_block_fht_weight_cache), one CUDA graph
+    from latent_weight_lab import flush_block_fht_weight_cache, prepare_block_fht_weight_cache
+
+    pair = torch.nn.ModuleList([up, down])
+
+    def cache_step():
+        prepare_block_fht_weight_cache(pair)
+        down(torch.nn.functional.gelu(up(x))).backward(gy)
+        flush_block_fht_weight_cache(pair)
+
+    for _ in range(warmup):
+        up.generator.latent.grad = down.generator.latent.grad = x.grad = None
+        cache_step()
+    torch.cuda.synchronize()
+    up.generator.latent.grad = down.generator.latent.grad = x.grad = None
+    graph_c = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_c):
+        cache_step()
+
+    def cache_dev_step():
+        graph_c.replay()
+        if world > 1:
+            torch.cat([p.grad.reshape(-1) for p in lat], out=flat)
+            dist.all_reduce(flat)
+
+    ms_cache = timed(cache_dev_step, steps)
     flops = 6.0 * 2 * MLP_D * MLP_F * MLP_T  # per GPU: fwd 2*in*out, bwd 4*in*out, two matrices
     peaks = _peaks()
     achieved = flops / (ms * 1e-3) / 1e12
@@ -489,6 +518,10 @@ def measure_mlp_pair(dev, world: int, steps: int, warmup: int) -> dict:
                 "h2d_bytes_per_step": MLP_T * MLP_D * 2,
                 "d2h_bytes_per_step": 2 * 32768 * 2 + MLP_T * MLP_D * 2,
                 "api": "BlockFHTLinear modules, eager (x in, latent and input gradients out)"},
+        "weight_cache_path": {"value": world * MLP_T / (ms_cache * 1e-3), "unit": "tokens/s", "ms_per_step": ms_cache,
+                              "tensor_frac": flops / (ms_cache * 1e-3) / 1e12 / peaks["bf16_tflops"],
+                              "path": "prepare_/flush_block_fht_weight_cache around the same fwd+bwd: one grouped "
+                                      "generation and one grouped latent projection per step, one CUDA graph"},
     }
 
 
@@ -562,7 +595,8 @@ def run_mlp(args) -> None:
     next_pow2 rule)."""
     import torch
 
-    from latent_weight_lab import BlockFHTLinear, _native
+    from latent_weight_lab import (BlockFHTLinear, _native, flush_block_fht_weight_cache,
+                                   prepare_block_fht_weight_cache)
 
     _native.load()
     dev = torch.device("cuda", 0)
@@ -572,11 +606,18 @@ def run_mlp(args) -> None:
     down = BlockFHTLinear(F4, D, latent_dim=args.latent, layers=3, seed=12).to(dev, torch.bfloat16)
     x = torch.randn(T, D, device=dev, dtype=torch.bfloat16, requires_grad=True)
     gy = torch.randn(T, D, device=dev, dtype=torch.bfloat16)
+    pair = torch.nn.ModuleList([up, down])
 
     def step():
         up.generator.latent.grad = down.generator.latent.grad = x.grad = None
+        if args.cache:
+            # the reference's training path (block_fht.py:560-569): both weights
+            # generated by one grouped launch, both latent projections by one
+            prepare_block_fht_weight_cache(pair)
         y = down(torch.nn.functional.gelu(up(x)))
         y.backward(gy)
+        if args.cache:
+            flush_block_fht_weight_cache(pair)
 
     for _ in range(args.warmup):
         step()
@@ -594,8 +635,12 @@ def run_mlp(args) -> None:
         up.generator.latent.grad = down.generator.latent.grad = x.grad = None
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
+            if args.cache:
+                prepare_block_fht_weight_cache(pair)
             y = down(torch.nn.functional.gelu(up(x)))
             y.backward(gy)
+            if args.cache:
+                flush_block_fht_weight_cache(pair)
         for _ in range(args.warmup):
             graph.replay()
         torch.cuda.synchronize()
@@ -617,7 +662,9 @@ def run_mlp(args) -> None:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (x ~N(0,1), latents ~N(0,0.02))",
         "config": {"workload": f"C3 MLP pair 768->3072->768, 8192 tokens, latent {args.latent}, layers=3",
-                   "path": "weights generated by liblwl_b200, GEMMs by cuBLAS (F.linear)",
+                   "path": ("weight cache: one grouped generation and one grouped latent projection per step"
+                            if args.cache else "weights generated per module by liblwl_b200")
+                           + ", GEMMs by cuBLAS (F.linear)",
                    "execution": "eager" if args.eager else "one CUDA graph per fwd+bwd step"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": achieved / peaks["bf16_tflops"], "traffic": None, "peak_source": peaks["source"]},
@@ -1231,6 +1278,8 @@ def main() -> None:
     ap.add_argument("--features", type=int, default=3072, help="features for --workload mix")
     ap.add_argument("--xl-layers", type=int, default=48, help="layers for --workload gpt2xl")
     ap.add_argument("--eager", action="store_true", help="--workload mlp without CUDA-graph capture")
+    ap.add_argument("--cache", action="store_true",
+                    help="--workload mlp through prepare_/flush_block_fht_weight_cache (grouped launches)")
     args = ap.parse_args()
     global COORDS_PER_GPU
     COORDS_PER_GPU = 1 << args.log_coords

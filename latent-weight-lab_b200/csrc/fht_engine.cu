@@ -288,9 +288,19 @@ int plan_fht(const FhtArgs& a, FhtPlan& plan) {
     const size_t h = (size_t(nblk) * size_t(B) * 2 + 255) & ~size_t(255);
     plan.ws_bytes = h;
     if (bwd) {
-      plan.launches[plan.nlaunch - 1].p.ws_out32 = 1;
+      TileLaunch& last = plan.launches[plan.nlaunch - 1];
       plan.f32_off = h;
-      plan.ws_bytes = h + size_t(nblk) * size_t(B) * 4;
+      if ((B >> 15) <= 128) {
+        // the last low pass sums its tiles in tensor memory: partial rows of
+        // [L] per group of tpb CTAs instead of an fp32 copy of every block
+        last.p.acc_rows = 1;
+        last.grid = mma_lo_grid(last.p);
+        plan.partial_rows = last.grid / (B >> 15);
+        plan.ws_bytes = h + size_t(plan.partial_rows) * size_t(a.latent_size) * 4;
+      } else {
+        last.p.ws_out32 = 1;
+        plan.ws_bytes = h + size_t(nblk) * size_t(B) * 4;
+      }
     }
   }
   return 0;
@@ -324,6 +334,7 @@ int run_plan_t(const FhtArgs& a, FhtPlan& plan, cudaStream_t st) {
     p.src = (p.src_kind == SRC_WS) ? a.workspace : a.in;
     if (p.dst_kind == DST_SLICE) p.dst = a.out;
     else if (p.dst_kind == DST_WS) p.dst = static_cast<char*>(a.workspace) + (p.ws_out32 ? plan.f32_off : 0);
+    if (p.acc_rows) p.partial = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + plan.f32_off);
     else p.partial = reinterpret_cast<float*>(a.workspace);
     if (p.lo == 2) {
       if (fht32_lo_launch(a.dtype, p, st) != 0) {
@@ -350,7 +361,8 @@ int run_plan_t(const FhtArgs& a, FhtPlan& plan, cudaStream_t st) {
     LWL_CUDA_TRY(cudaGetLastError());
   }
   if (a.backward) {
-    int64_t stride = plan.launches[0].p.dst_kind == DST_ACC ? a.latent_size : plan.B;
+    const bool rows_of_L = plan.launches[0].p.dst_kind == DST_ACC || plan.launches[plan.nlaunch - 1].p.acc_rows;
+    int64_t stride = rows_of_L ? a.latent_size : plan.B;
     int threads = 256;
     int64_t blocks = std::min<int64_t>((a.latent_size + threads - 1) / threads, 65535);
     reduce_rows_kernel<T><<<(int)blocks, threads, 0, st>>>(

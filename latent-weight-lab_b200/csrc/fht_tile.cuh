@@ -65,6 +65,8 @@ struct TileParams {
   // and the low pass streams its workspace tiles by bulk copy, one tile ahead.
   int ws16;
   int ws_out32;  // bf16 backward plans: this (last) launch writes its workspace output in fp32
+  int acc_rows;  // ... or, with a grid that is a multiple of the tiles per block, sums its tiles in
+                 // tensor memory and writes one [L] partial row segment per CTA into `partial`
 };
 
 __device__ __forceinline__ int pad_idx(int t) { return t + (t >> 5); }

@@ -82,9 +82,41 @@ __device__ __forceinline__ void lo32_load(float (&v)[kRegs], const TileParams& p
 // 16-byte (fp32) or 8-byte (16-bit) store per group where aligned.
 template <typename T, int SET, int DST>
 __device__ __forceinline__ void lo32_store(const float (&v)[kRegs], const TileParams& p, int64_t b, int64_t pos0,
-                                           int base) {
+                                           int base, bool first) {
   constexpr int TB = 15;
   static_assert(SET == SD || SET == SD2, "stores leave from the quad sets");
+  if (DST == DST_WS && p.acc_rows) {
+    // the backward's last launch: the grid is a multiple of the tiles per
+    // block, so every tile of this CTA has the same index j and the CTA sums
+    // them into its segment of partial row blockIdx.x / tpb (L2-resident):
+    // the first tile stores, later ones add.  One thread owns each address,
+    // so the sums keep program order (deterministic).
+    float* row = p.partial + (int64_t)(blockIdx.x / (int)(p.B >> TB)) * p.L;
+    const bool vec = (p.L & 3) == 0;
+#pragma unroll
+    for (int q = 0; q < kRegs / 4; ++q) {
+      const int64_t pos = pos0 + base + spread<TB, SET>(4 * q);  // position inside the block
+      float* d = row + pos;
+      if (vec && pos + 4 <= p.L) {
+        if (first) {
+          *reinterpret_cast<float4*>(d) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        } else {
+          asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(d), "f"(v[4 * q]),
+                       "f"(v[4 * q + 1]), "f"(v[4 * q + 2]), "f"(v[4 * q + 3])
+                       : "memory");
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (pos + e < p.L) {
+            if (first) d[e] = v[4 * q + e];
+            else atomicAdd(d + e, v[4 * q + e]);
+          }
+        }
+      }
+    }
+    return;
+  }
   if (DST == DST_WS) {
     float* d = reinterpret_cast<float*>(p.dst) + (b - p.first_block) * p.B + pos0 + base;
 #pragma unroll
@@ -173,7 +205,7 @@ __global__ void __launch_bounds__(Tile<15>::kThreads, 1) fht32_lo_kernel(const _
       exchange<TB, SB, SD>(v, buf, lane, warp);
       xform<TB, SD>(v, Tl::kChi, TB);
       if (s1 >= 0) sign_scaled<TB, SD>(v, sw + s1 * Tl::kWords, bD, p.scale);
-      lo32_store<T, SD, DST>(v, p, b, pos0, bD);
+      lo32_store<T, SD, DST>(v, p, b, pos0, bD, tile == blockIdx.x);
     } else {
       exchange<TB, SB, SC>(v, buf, lane, warp);
       xform<TB, SC>(v, Tl::kChi, TB);
@@ -184,7 +216,7 @@ __global__ void __launch_bounds__(Tile<15>::kThreads, 1) fht32_lo_kernel(const _
       exchange<TB, SA, SD2>(v, buf, lane, warp);
       xform<TB, SD2>(v, Tl::kBsub, TB);
       if (s2 >= 0) sign_scaled<TB, SD2>(v, sw + s2 * Tl::kWords, bD2, p.scale);
-      lo32_store<T, SD2, DST>(v, p, b, pos0, bD2);
+      lo32_store<T, SD2, DST>(v, p, b, pos0, bD2, tile == blockIdx.x);
     }
   }
 }
@@ -211,6 +243,14 @@ bool fht32_lo_supported(int dtype, int n, unsigned flags) {
   return n > 15 && n <= 23 && (dtype == LWL_F32 || (flags & LWL_FLAG_EXACT));
 }
 
+int fht32_lo_grid(const TileParams& p) {
+  int dev = 0, nsm = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t tpb = p.B >> 15, ntiles = p.nblocks * tpb;
+  if (ntiles <= nsm) return (int)ntiles;
+  return (int)(p.acc_rows ? (nsm / tpb) * tpb : nsm);  // acc_rows: a multiple of the tiles per block
+}
+
 int fht32_lo_launch(int dtype, const TileParams& p, cudaStream_t st) {
   using namespace f32k;
   const void* k = dtype == LWL_BF16 ? lo32_kernel<__nv_bfloat16>(p.src_kind, p.dst_kind, p.lo_nseg)
@@ -218,10 +258,7 @@ int fht32_lo_launch(int dtype, const TileParams& p, cudaStream_t st) {
                                     : lo32_kernel<float>(p.src_kind, p.dst_kind, p.lo_nseg);
   const size_t smem = Tile<15>::kSmem;
   if (!set_max_smem(k, (int)smem)) return -1;
-  int dev = 0, nsm = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t ntiles = p.nblocks * (p.B >> 15);
-  const int grid = (int)std::min<int64_t>(ntiles, nsm);
+  const int grid = fht32_lo_grid(p);
   void* args[] = {const_cast<TileParams*>(&p)};
   return cudaLaunchKernel(k, dim3(grid), dim3(Tile<15>::kThreads), args, smem, st) == cudaSuccess ? 0 : -1;
 }

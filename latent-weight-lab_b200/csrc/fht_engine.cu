@@ -302,12 +302,14 @@ int plan_fht(const FhtArgs& a, FhtPlan& plan) {
         plan.ws_bytes = h + size_t(nblk) * size_t(B) * 4;
       }
     }
-  } else if (bwd && plan.launches[plan.nlaunch - 1].p.lo == 1 && (B >> 15) <= 128) {
-    // fp16 backward (fp32 workspace): the same tensor-memory sums in the last low pass
+  } else if (bwd && plan.launches[plan.nlaunch - 1].p.lo != 0 && (B >> 15) <= 128) {
+    // fp16 backward (fp32 workspace): the same tensor-memory sums in the last
+    // low pass; fp32 and the exact mode (fht32_lo_kernel): per-CTA sums in an
+    // L2-resident partial row segment
     TileLaunch& last = plan.launches[plan.nlaunch - 1];
     const size_t h = (size_t(nblk) * size_t(B) * 4 + 255) & ~size_t(255);
     last.p.acc_rows = 1;
-    last.grid = mma_lo_grid(last.p);
+    last.grid = last.p.lo == 1 ? mma_lo_grid(last.p) : fht32_lo_grid(last.p);
     plan.f32_off = h;
     plan.partial_rows = last.grid / (B >> 15);
     plan.ws_bytes = h + size_t(plan.partial_rows) * size_t(a.latent_size) * 4;

@@ -62,6 +62,7 @@ int fhts_run(const FhtArgs& a, cudaStream_t st);
 // fp32 low pass of two-pass plans (fp32 and the exact mode, 2^16..2^23; fht32_lo.cu).
 bool fht32_lo_supported(int dtype, int n, unsigned flags);
 int fht32_lo_launch(int dtype, const TileParams& p, cudaStream_t st);
+int fht32_lo_grid(const TileParams& p);  // the launch's grid (a multiple of the tiles per block with acc_rows)
 
 // High-bit pass of two-pass plans with 15 low bits and 1..8 high bits (fht32_hi.cu).
 bool fht_hi_eligible(int dtype, const TileParams& p);

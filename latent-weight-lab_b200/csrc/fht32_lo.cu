@@ -91,7 +91,10 @@ __device__ __forceinline__ void lo32_store(const float (&v)[kRegs], const TilePa
     // them into its segment of partial row blockIdx.x / tpb (L2-resident):
     // the first tile stores, later ones add.  One thread owns each address,
     // so the sums keep program order (deterministic).
-    float* row = p.partial + (int64_t)(blockIdx.x / (int)(p.B >> TB)) * p.L;
+    // (with more tiles per block than CTAs, 2^23: grid = tpb / 2, row 0, the
+    // CTA meets j = blockIdx.x and blockIdx.x + gridDim.x)
+    const int tpb = (int)(p.B >> TB);
+    float* row = p.partial + (tpb > (int)gridDim.x ? 0 : (int64_t)(blockIdx.x / tpb)) * p.L;
     const bool vec = (p.L & 3) == 0;
 #pragma unroll
     for (int q = 0; q < kRegs / 4; ++q) {
@@ -173,6 +176,8 @@ __global__ void __launch_bounds__(Tile<15>::kThreads, 1) fht32_lo_kernel(const _
   const int cpb = (int)(p.B >> TB);  // chunks per block
   const int64_t ntiles = p.nblocks * cpb;
   const int s1 = p.lo_seg_slot[0], s2 = NSEG == 2 ? p.lo_seg_slot[1] : -1;
+  // acc_rows: the CTA's first tile of each tile index stores, later ones add
+  const int64_t first_end = (int64_t)gridDim.x * (cpb > (int)gridDim.x ? 2 : 1);
   float v[kRegs];
   for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const int64_t b = p.first_block + tile / cpb;
@@ -205,7 +210,7 @@ __global__ void __launch_bounds__(Tile<15>::kThreads, 1) fht32_lo_kernel(const _
       exchange<TB, SB, SD>(v, buf, lane, warp);
       xform<TB, SD>(v, Tl::kChi, TB);
       if (s1 >= 0) sign_scaled<TB, SD>(v, sw + s1 * Tl::kWords, bD, p.scale);
-      lo32_store<T, SD, DST>(v, p, b, pos0, bD, tile == blockIdx.x);
+      lo32_store<T, SD, DST>(v, p, b, pos0, bD, tile < first_end);
     } else {
       exchange<TB, SB, SC>(v, buf, lane, warp);
       xform<TB, SC>(v, Tl::kChi, TB);
@@ -216,7 +221,7 @@ __global__ void __launch_bounds__(Tile<15>::kThreads, 1) fht32_lo_kernel(const _
       exchange<TB, SA, SD2>(v, buf, lane, warp);
       xform<TB, SD2>(v, Tl::kBsub, TB);
       if (s2 >= 0) sign_scaled<TB, SD2>(v, sw + s2 * Tl::kWords, bD2, p.scale);
-      lo32_store<T, SD2, DST>(v, p, b, pos0, bD2, tile == blockIdx.x);
+      lo32_store<T, SD2, DST>(v, p, b, pos0, bD2, tile < first_end);
     }
   }
 }
@@ -247,6 +252,7 @@ int fht32_lo_grid(const TileParams& p) {
   int dev = 0, nsm = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   const int64_t tpb = p.B >> 15, ntiles = p.nblocks * tpb;
+  if (p.acc_rows && tpb > nsm) return (int)(tpb / 2);  // 2^23: each CTA meets two tile indices
   if (ntiles <= nsm) return (int)ntiles;
   return (int)(p.acc_rows ? (nsm / tpb) * tpb : nsm);  // acc_rows: a multiple of the tiles per block
 }

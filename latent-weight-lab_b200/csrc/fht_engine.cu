@@ -290,19 +290,19 @@ int plan_fht(const FhtArgs& a, FhtPlan& plan) {
     if (bwd) {
       TileLaunch& last = plan.launches[plan.nlaunch - 1];
       plan.f32_off = h;
-      if ((B >> 15) <= 128) {
+      if ((B >> 15) <= 256) {
         // the last low pass sums its tiles in tensor memory: partial rows of
         // [L] per group of tpb CTAs instead of an fp32 copy of every block
         last.p.acc_rows = 1;
         last.grid = mma_lo_grid(last.p);
-        plan.partial_rows = last.grid / (B >> 15);
+        plan.partial_rows = last.grid >= (B >> 15) ? last.grid / (B >> 15) : 1;
         plan.ws_bytes = h + size_t(plan.partial_rows) * size_t(a.latent_size) * 4;
       } else {
         last.p.ws_out32 = 1;
         plan.ws_bytes = h + size_t(nblk) * size_t(B) * 4;
       }
     }
-  } else if (bwd && plan.launches[plan.nlaunch - 1].p.lo != 0 && (B >> 15) <= 128) {
+  } else if (bwd && plan.launches[plan.nlaunch - 1].p.lo != 0 && (B >> 15) <= 256) {
     // fp16 backward (fp32 workspace): the same tensor-memory sums in the last
     // low pass; fp32 and the exact mode (fht32_lo_kernel): per-CTA sums in an
     // L2-resident partial row segment
@@ -311,7 +311,7 @@ int plan_fht(const FhtArgs& a, FhtPlan& plan) {
     last.p.acc_rows = 1;
     last.grid = last.p.lo == 1 ? mma_lo_grid(last.p) : fht32_lo_grid(last.p);
     plan.f32_off = h;
-    plan.partial_rows = last.grid / (B >> 15);
+    plan.partial_rows = last.grid >= (B >> 15) ? last.grid / (B >> 15) : 1;
     plan.ws_bytes = h + size_t(plan.partial_rows) * size_t(a.latent_size) * 4;
   }
   return 0;

@@ -1433,12 +1433,16 @@ __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_consta
   // (the grid is a multiple of tpb), so their final results are summed in
   // tensor memory, 128 lanes x 256 columns = the 32768 fp32 positions of tile
   // j, as in the 2^15 backward; one partial row segment per CTA at the end.
+  // With 256 tiles per block (2^23) the grid is 128 and each CTA meets two
+  // tile indices, j = blockIdx.x and blockIdx.x + 128: two 256-column slots.
   __shared__ uint32_t lo_tmem;
   uint32_t tacc = 0;
+  const int slots = (p.acc_rows && tpb > (int)gridDim.x) ? 2 : 1;
+  const uint32_t tcols = 256u * (uint32_t)slots;
   if (p.acc_rows) {
     if (w == 0) {
-      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;\n" ::"r"(
-          (uint32_t)__cvta_generic_to_shared(&lo_tmem)));
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+          (uint32_t)__cvta_generic_to_shared(&lo_tmem)), "r"(tcols));
       asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
     }
     asm volatile("tcgen05.fence::before_thread_sync;\n");
@@ -1446,8 +1450,10 @@ __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_consta
     asm volatile("tcgen05.fence::after_thread_sync;\n");
     tacc = lo_tmem + ((uint32_t)(32 * (w & 3)) << 16) + (uint32_t)(64 * (w >> 2));
     const float z8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int s = 0; s < slots; ++s) {
 #pragma unroll
-    for (int k = 0; k < 8; ++k) tmem_st8(tacc + 8 * k, z8);
+      for (int k = 0; k < 8; ++k) tmem_st8(tacc + 256u * s + 8 * k, z8);
+    }
     tmem_wait_st();
   }
   bool inflight = false;  // thread 0: a bulk copy was issued and not yet waited for
@@ -1563,7 +1569,8 @@ __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_consta
     for (int sg = 0; sg < nseg; ++sg)
       if (p.lo_seg_slot[sg] >= 0) scale *= p.scale;
     if (p.acc_rows) {
-      run_final_acc(f, xb, sw + post * kWordsPad, scale, tacc, w, lane, g, t);
+      const uint32_t slot = (slots == 2 && j >= (int)gridDim.x) ? 256u : 0u;
+      run_final_acc(f, xb, sw + post * kWordsPad, scale, tacc + slot, w, lane, g, t);
     } else if (p.dst_kind == DST_WS && p.ws16 && !p.ws_out32) {
       // bf16 workspace: the staged copy-out of the slice path, into the tile's
       // 64 KB of the workspace (tile index counted from the plan's first block)
@@ -1622,27 +1629,31 @@ __global__ void __launch_bounds__(kThreads, 1) fht_lo_kernel(const __grid_consta
   if (p.acc_rows) {
     // the CTA's sums of tile j in natural order through the exchange buffers,
     // then its segment [j 2^15, (j+1) 2^15) of partial row blockIdx.x / tpb
-    __syncthreads();
+    // (two slots: segments blockIdx.x and blockIdx.x + 128 of row 0)
     float* prow = reinterpret_cast<float*>(smem);
+    for (int s = 0; s < slots; ++s) {
+      __syncthreads();
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      float acc[8];
-      tmem_ld8(tacc + 8 * k, acc);
+      for (int k = 0; k < 8; ++k) {
+        float acc[8];
+        tmem_ld8(tacc + 256u * s + 8 * k, acc);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int R = g + 8 * ((i >> 1) & 1), C = 2 * t + (i & 1) + 8 * (i >> 2);
-        prow[prow_swz(dep_a(w, k, R, C))] = acc[i];
+        for (int i = 0; i < 8; ++i) {
+          const int R = g + 8 * ((i >> 1) & 1), C = 2 * t + (i & 1) + 8 * (i >> 2);
+          prow[prow_swz(dep_a(w, k, R, C))] = acc[i];
+        }
       }
+      __syncthreads();
+      const int jj = slots == 2 ? (int)blockIdx.x + s * (int)gridDim.x : (int)blockIdx.x % tpb;
+      const int64_t rix = slots == 2 ? 0 : blockIdx.x / tpb;
+      float* row = p.partial + rix * p.L + ((int64_t)jj << kLog);
+      const int64_t lim = p.L - ((int64_t)jj << kLog);  // positions of this segment inside [0, L)
+      for (int q = tid; q < kB && q < lim; q += kThreads) row[q] = prow[prow_swz(q)];
     }
-    __syncthreads();
-    const int jj = blockIdx.x % tpb;
-    float* row = p.partial + (int64_t)(blockIdx.x / tpb) * p.L + ((int64_t)jj << kLog);
-    const int64_t lim = p.L - ((int64_t)jj << kLog);  // positions of this segment inside [0, L)
-    for (int q = tid; q < kB && q < lim; q += kThreads) row[q] = prow[prow_swz(q)];
     asm volatile("tcgen05.fence::before_thread_sync;\n");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;\n");
-    if (w == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;\n" ::"r"(lo_tmem));
+    if (w == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(lo_tmem), "r"(tcols));
   }
   if (bulk && tid == 0 && inflight) {
     // after a wait gave up: let the outstanding copy land before the CTA exits (bounded)
@@ -1830,7 +1841,8 @@ bool mma_lo_supported(int dtype, int n, unsigned flags) {
 int mma_lo_grid(const TileParams& p) {
   const int64_t tpb = p.B >> fmma::kLog, ntiles = p.nblocks * tpb;
   const int sms = fmma::sm_count();
-  if (p.acc_rows) {  // a multiple of the tiles per block (ntiles is one)
+  if (p.acc_rows) {  // a multiple of the tiles per block (ntiles is one), or half of them at 2^23
+    if (tpb > sms) return (int)(tpb / 2);
     const int64_t g = ntiles < sms ? ntiles : (sms / tpb) * tpb;
     return (int)g;
   }
